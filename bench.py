@@ -1,0 +1,518 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 embedding-bag engine.
+
+Default workload (one GPU): multi-table weighted/mean pooling -- 8 bf16 tables
+of 500,000 x 128 rows, batch 8192, 20 ids per bag, uniform ids, per-id fp32
+weights U(0,1); tables 0-3 pool as weighted sums, 4-7 as means; fp32
+accumulation; output 8192 x 8 x 128 fp32. A step is one pooled lookup of one
+batch over all tables (one execute_batch group: a validation kernel and a
+pooling kernel).
+
+With N GPUs (torchrun, one process per GPU, NCCL) every rank holds 8 such
+tables (8N tables in all, table-wise sharded) and pools them for the whole
+batch; an NCCL all-to-all then returns each sample block to its owning rank
+(weak scaling: fixed work per GPU).
+
+Prints one JSON line (rank 0). `--impl reference` times the CPU restatement
+of the reference's embedding-bag (the reference itself cannot be built here)
+on the host cores instead.
+"""
+
+import argparse
+import ctypes
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PACKAGE_DIR = os.path.join(ROOT, "xla-serving_b200")
+
+# Workload constants.
+NUM_TABLES = 8
+VOCAB = 500_000
+DIM = 128
+BATCH = 8192
+BAG = 20
+SEED = 0
+ROTATE = 8  # distinct input/output sets cycled between steps (> L2 in all)
+ROW_BYTES = DIM * 2
+WORKLOAD = ("multi_table_bf16: 8 bf16 tables x 500,000 x 128 per GPU, batch "
+            "8192, 20 ids per bag, uniform ids, tables 0-3 per-id weighted "
+            "sum, 4-7 mean, fp32 accumulate, output 8192x8x128 fp32")
+
+
+def load_package():
+  name = "xla_serving_b200"
+  if name in sys.modules:
+    return sys.modules[name]
+  spec = importlib.util.spec_from_file_location(
+      name, os.path.join(PACKAGE_DIR, "__init__.py"),
+      submodule_search_locations=[PACKAGE_DIR])
+  module = importlib.util.module_from_spec(spec)
+  sys.modules[name] = module
+  spec.loader.exec_module(module)
+  return module
+
+
+def algorithmic_bytes_per_step():
+  """Bytes one step must move: every id occurrence's row and id, the weights
+  of weighted tables, the int64 offsets and the fp32 outputs (no cache
+  credit)."""
+  nnz = NUM_TABLES * BATCH * BAG
+  weighted_ids = (NUM_TABLES // 2) * BATCH * BAG
+  return (nnz * (ROW_BYTES + 8) + weighted_ids * 4 +
+          (BATCH + 1) * 8 * NUM_TABLES + BATCH * NUM_TABLES * DIM * 4)
+
+
+def measured_peaks():
+  path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+  try:
+    with open(path, encoding="utf-8") as f:
+      p = json.load(f)
+    return float(p["hbm_gbs"]), "measured"
+  except (OSError, KeyError, ValueError):
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+  """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+  FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,"
+            "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+            "clocks_event_reasons.hw_thermal_slowdown,"
+            "clocks_event_reasons.sw_thermal_slowdown,"
+            "clocks_event_reasons.sw_power_cap")
+
+  def __init__(self, gpu_index):
+    self.gpu_index = gpu_index
+    self.proc = None
+    self.lines = []
+    self.thread = None
+
+  def start(self):
+    try:
+      self.proc = subprocess.Popen(
+          ["nvidia-smi", f"--id={self.gpu_index}",
+           f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+          text=True)
+    except OSError:
+      self.proc = None
+      return
+    self.thread = threading.Thread(target=self._read, daemon=True)
+    self.thread.start()
+
+  def _read(self):
+    for line in self.proc.stdout:
+      self.lines.append(line.strip())
+
+  def stop(self):
+    if self.proc is None:
+      return None
+    self.proc.terminate()
+    try:
+      self.proc.wait(timeout=5)
+    except subprocess.TimeoutExpired:
+      self.proc.kill()
+    if self.thread is not None:
+      self.thread.join(timeout=2)
+    sm, mx, reasons = [], 0.0, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+             "sw_power_cap"]
+    for line in self.lines:
+      parts = [p.strip() for p in line.split(",")]
+      if len(parts) < 9:
+        continue
+      try:
+        sm.append(float(parts[1]))
+        mx = max(mx, float(parts[2]))
+      except ValueError:
+        continue
+      for name, flag in zip(names, parts[5:9]):
+        if flag.lower() == "active":
+          reasons.add(name)
+    if not sm:
+      return None
+    loaded = [s for s in sm if s >= 0.5 * mx] or sm
+    return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx,
+            "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def init_distributed():
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  rank = int(os.environ.get("RANK", "0"))
+  local = int(os.environ.get("LOCAL_RANK", "0"))
+  if world > 1:
+    from datetime import timedelta  # pylint: disable=import-outside-toplevel
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+  return world, rank, local
+
+
+def barrier(world, local):
+  if world > 1:
+    dist.barrier(device_ids=[local])
+
+
+def max_over_ranks(value, world):
+  if world == 1:
+    return value
+  t = torch.tensor([value], dtype=torch.float64, device="cuda")
+  dist.all_reduce(t, op=dist.ReduceOp.MAX)
+  return float(t.item())
+
+
+def sum_over_ranks(value, world):
+  if world == 1:
+    return value
+  t = torch.tensor([value], dtype=torch.float64, device="cuda")
+  dist.all_reduce(t, op=dist.ReduceOp.SUM)
+  return float(t.item())
+
+
+class Workload:
+  """Tables, rotating inputs and outputs of one rank, on its GPU."""
+
+  def __init__(self, xse, rank, world):
+    from xla_serving_b200 import synth  # pylint: disable=import-outside-toplevel
+    self.xse = xse
+    self.world = world
+    self.engine = xse.EmbeddingEngine(torch.cuda.current_device())
+    self.specs = synth.multi_table_specs()
+    self.tables = []
+    for k, spec in enumerate(self.specs):
+      g = rank * NUM_TABLES + k
+      rows, _, _ = synth.synth_table(xse._capi.DT_BF16, VOCAB, DIM, SEED, g)
+      self.tables.append(rows)
+      self.engine.add_table(spec.name, rows, spec.combine, adopt=True)
+      self.engine.register_feature(spec.name, spec.name)
+    self.inputs = []
+    for v in range(ROTATE):
+      batch = []
+      for k, spec in enumerate(self.specs):
+        batch.append(synth.synth_batch(spec, rank * NUM_TABLES + k, BATCH,
+                                       BAG, BAG, SEED, 0.0, variant=v))
+      self.inputs.append(batch)
+    self.pooled = [torch.empty((BATCH, NUM_TABLES, DIM), dtype=torch.float32,
+                               device="cuda") for _ in range(ROTATE)]
+    self.recv = ([torch.empty_like(p) for p in self.pooled]
+                 if world > 1 else None)
+    self.requests = [self._requests(self.inputs[v], self.pooled[v])
+                     for v in range(ROTATE)]
+    self.status = xse.Status(NUM_TABLES)
+    torch.cuda.synchronize()
+
+  def _requests(self, batch, pooled):
+    reqs = []
+    for k, spec in enumerate(self.specs):
+      fb = batch[k]
+      reqs.append(self.xse.BagRequest(spec.name, fb.ids, fb.offsets,
+                                      pooled[:, k, :], fb.weights,
+                                      output_stride=NUM_TABLES * DIM))
+    return reqs
+
+  def step(self, i):
+    v = i % ROTATE
+    self.engine.execute_batch(self.requests[v], status=self.status)
+    launches = self.xse.last_launch_count()
+    if self.world > 1:
+      dist.all_to_all_single(self.recv[v], self.pooled[v])
+    return launches
+
+  def ids_per_step(self):
+    return NUM_TABLES * BATCH * BAG
+
+
+class HostInputs:
+  """Pinned host copies of rotating inputs for the end-to-end measurement:
+  each step copies one set host->device, pools it and reads the pooled
+  output back into pinned host memory."""
+
+  def __init__(self, wl):
+    self.wl = wl
+    self.sets = []
+    for v in range(ROTATE):
+      parts = []
+      for fb in wl.inputs[v]:
+        parts.append(fb.ids.view(torch.uint8))
+        parts.append(fb.offsets.view(torch.uint8))
+        if fb.weights is not None:
+          parts.append(fb.weights.view(torch.uint8))
+      flat = torch.cat(parts).cpu().pin_memory()
+      self.sets.append(flat)
+    self.h2d_bytes = int(self.sets[0].numel())
+    self.dev = torch.empty(self.h2d_bytes, dtype=torch.uint8, device="cuda")
+    # Device views into the staging buffer, one set of requests.
+    self.requests = []
+    off = 0
+    views = []
+    for fb in wl.inputs[0]:
+      n_ids, n_off = fb.ids.numel(), fb.offsets.numel()
+      ids = self.dev[off:off + 8 * n_ids].view(torch.int64)
+      off += 8 * n_ids
+      offs = self.dev[off:off + 8 * n_off].view(torch.int64)
+      off += 8 * n_off
+      w = None
+      if fb.weights is not None:
+        w = self.dev[off:off + 4 * n_ids].view(torch.float32)
+        off += 4 * n_ids
+      views.append((ids, offs, w))
+    self.out_dev = torch.empty((BATCH, NUM_TABLES, DIM), dtype=torch.float32,
+                               device="cuda")
+    self.out_host = torch.empty_like(self.out_dev, device="cpu").pin_memory()
+    self.d2h_bytes = self.out_host.numel() * 4
+    for k, spec in enumerate(wl.specs):
+      ids, offs, w = views[k]
+      self.requests.append(wl.xse.BagRequest(
+          spec.name, ids, offs, self.out_dev[:, k, :], w,
+          output_stride=NUM_TABLES * DIM))
+
+  def step(self, i):
+    self.dev.copy_(self.sets[i % ROTATE], non_blocking=True)
+    # Synchronous engine call: validation, pooling, status read-back.
+    self.wl.engine.execute_batch(self.requests)
+    self.out_host.copy_(self.out_dev, non_blocking=True)
+    torch.cuda.current_stream().synchronize()
+
+
+def cpu_baseline(wl, seconds):
+  """Times the oracle (CPU restatement of the reference's threaded
+  ExecuteEmbeddingBagBatch) on this host's cores over full batches of the
+  same workload (same tables and ids, copied to host)."""
+  sys.path.insert(0, ROOT)
+  from oracle import oracle  # pylint: disable=import-outside-toplevel
+  cores = oracle.host_cores()
+  bags = []
+  for k, spec in enumerate(wl.specs):
+    bits = wl.tables[k].view(torch.int16).cpu().numpy().view(np.uint16)
+    fb = wl.inputs[0][k]
+    bags.append(oracle.Bag(
+        bits, fb.ids.cpu().numpy(), fb.offsets.cpu().numpy(),
+        None if fb.weights is None else fb.weights.cpu().numpy(),
+        spec.combine, oracle.BF16))
+  oracle.embedding_bag_batch(bags, num_threads=cores)  # warm-up
+  reps, t0 = 0, time.perf_counter()
+  while True:
+    oracle.embedding_bag_batch(bags, num_threads=cores)
+    reps += 1
+    el = time.perf_counter() - t0
+    if el >= seconds:
+      break
+  ids = reps * wl.ids_per_step()
+  return {"value": ids / el, "unit": "ids/s", "cores": cores, "kind": "port",
+          "sample": f"{reps} full batches (8 tables x 8192 bags x 20 ids, "
+                    f"bf16 rows widened to fp32) in {el:.1f} s"}, bags
+
+
+def run_reference(args):
+  """CPU restatement of the reference path on all host cores, same workload
+  and metric; each step pools a bounded sample of the batch."""
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  rank = int(os.environ.get("RANK", "0"))
+  if rank != 0:
+    return
+  sys.path.insert(0, ROOT)
+  from oracle import oracle  # pylint: disable=import-outside-toplevel
+  cores = oracle.host_cores()
+  rng = np.random.default_rng(SEED)
+  specs = [(k < 4, "SUM" if k < 4 else "MEAN") for k in range(NUM_TABLES)]
+  tables = []
+  for k in range(NUM_TABLES):
+    bits, _, _ = oracle.synth_rows(oracle.BF16, SEED, k, 0, VOCAB, DIM)
+    tables.append(bits)
+
+  def make_bags(bags_per_table):
+    out = []
+    for k, (weighted, combine) in enumerate(specs):
+      ids = rng.integers(0, VOCAB, bags_per_table * BAG)
+      offsets = np.arange(bags_per_table + 1, dtype=np.int64) * BAG
+      w = rng.uniform(0, 1, len(ids)).astype(np.float32) if weighted else None
+      out.append(oracle.Bag(tables[k], ids, offsets, w, combine, oracle.BF16))
+    return out
+
+  probe = make_bags(BATCH)
+  t0 = time.perf_counter()
+  oracle.embedding_bag_batch(probe, num_threads=cores)
+  full = time.perf_counter() - t0
+  budget = 120.0 / max(args.steps + args.warmup, 1)
+  frac = min(1.0, budget / max(full, 1e-6))
+  bags_per_step = max(64, int(BATCH * frac))
+  sets = [make_bags(bags_per_step) for _ in range(4)]
+  for i in range(args.warmup):
+    oracle.embedding_bag_batch(sets[i % 4], num_threads=cores)
+  t0 = time.perf_counter()
+  for i in range(args.steps):
+    oracle.embedding_bag_batch(sets[i % 4], num_threads=cores)
+  el = time.perf_counter() - t0
+  ids = args.steps * NUM_TABLES * bags_per_step * BAG
+  value = ids / el
+  sample = (f"{bags_per_step} of {BATCH} bags per table per step "
+            f"({NUM_TABLES} tables, {BAG} ids per bag)")
+  line = {
+      "impl": "reference", "metric": "embedding-bag ids/sec",
+      "value": value, "unit": "ids/s", "n_gpus": world,
+      "steps": args.steps, "warmup": args.warmup,
+      "ms_per_step": 1000.0 * el / max(args.steps, 1),
+      "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+      "dtype": "bf16", "data": "synthetic (seeded, uniform ids)",
+      "config": {"workload": WORKLOAD, "global_batch": BATCH,
+                 "parallelism": "host threads"},
+      "cpu_baseline": {"value": value, "unit": "ids/s", "cores": cores,
+                       "kind": "port", "sample": sample},
+      "e2e": {"value": value, "unit": "ids/s", "h2d_bytes_per_step": 0,
+              "d2h_bytes_per_step": 0},
+  }
+  print(json.dumps(line), flush=True)
+
+
+def main():
+  ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+  ap.add_argument("--gpus", type=int, default=1)
+  ap.add_argument("--steps", type=int, default=2000)
+  ap.add_argument("--warmup", type=int, default=50)
+  ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+  ap.add_argument("--e2e-steps", type=int, default=200)
+  ap.add_argument("--cpu-seconds", type=float, default=10.0)
+  ap.add_argument("--no-cpu-baseline", action="store_true")
+  args = ap.parse_args()
+  if args.warmup < 3:
+    args.warmup = 3
+  if args.impl == "reference":
+    run_reference(args)
+    return
+
+  world, rank, local = init_distributed()
+  torch.cuda.set_device(local)
+  xse = load_package()
+  wl = Workload(xse, rank, world)
+  host = HostInputs(wl)
+  clocks = ClockSampler(local)
+  clocks.start()
+
+  for i in range(args.warmup):
+    wl.step(i)
+  wl.status.wait()
+  torch.cuda.synchronize()
+  barrier(world, local)
+
+  stream = torch.cuda.current_stream()
+  start = torch.cuda.Event(enable_timing=True)
+  end = torch.cuda.Event(enable_timing=True)
+  wl.engine.set_profiling(True)
+  launches = 0
+  torch.cuda.synchronize()
+  barrier(world, local)
+  start.record(stream)
+  for i in range(args.steps):
+    launches += wl.step(i)
+  end.record(stream)
+  torch.cuda.synchronize()
+  barrier(world, local)
+  wl.status.wait()
+  elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
+  pool_ms, pool_n = wl.engine.profile_read()
+  wl.engine.set_profiling(False)
+
+  # End to end through the engine's public call with host buffers.
+  for i in range(3):
+    host.step(i)
+  barrier(world, local)
+  e2e_start = torch.cuda.Event(enable_timing=True)
+  e2e_end = torch.cuda.Event(enable_timing=True)
+  e2e_start.record(stream)
+  for i in range(args.e2e_steps):
+    host.step(i)
+  e2e_end.record(stream)
+  torch.cuda.synchronize()
+  barrier(world, local)
+  e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end), world)
+  clock_info = clocks.stop()
+
+  ids_total = sum_over_ranks(wl.ids_per_step() * args.steps, world)
+  value = ids_total / (elapsed_ms / 1000.0)
+  e2e_ids = sum_over_ranks(wl.ids_per_step() * args.e2e_steps, world)
+  e2e_value = e2e_ids / (e2e_ms / 1000.0)
+
+  peak, peak_kind = measured_peaks()
+  bytes_step = algorithmic_bytes_per_step()
+  pool_avg_ms = pool_ms / max(pool_n, 1)
+  achieved = bytes_step / (pool_avg_ms / 1000.0) / 1e9
+
+  base = None
+  if world == 1 and not args.no_cpu_baseline:
+    base, _ = cpu_baseline(wl, args.cpu_seconds)
+
+  if rank == 0:
+    line = {
+        "metric": "embedding-bag ids/sec",
+        "value": value,
+        "unit": "ids/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded counter RNG: uniform ids, U(0,1) weights, "
+                "U(-0.05,0.05) rows)",
+        "config": {
+            "workload": WORKLOAD,
+            "global_batch": BATCH,
+            "tables_per_gpu": NUM_TABLES,
+            "tables_total": NUM_TABLES * world,
+            "accumulate": "fp32",
+            "parallelism": ("single GPU" if world == 1 else
+                            f"table-wise x{world}, NCCL all-to-all of pooled "
+                            "outputs"),
+            "l2": "inputs larger than L2: 1.0 GB of tables per GPU and "
+                  f"{ROTATE} rotating id/offset/weight/output sets",
+            "validation": "strict (separate validation kernel each step)",
+        },
+        "hbm_gbs_algorithmic_step": bytes_step / (elapsed_ms / args.steps /
+                                                  1000.0) / 1e9,
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "PoolVecKernel<bf16, G=16, V=1>",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": None,
+            "algorithmic_bytes_per_launch": bytes_step,
+            "avg_launch_ms": pool_avg_ms,
+        },
+        "e2e": {
+            "value": e2e_value,
+            "unit": "ids/s",
+            "h2d_bytes_per_step": host.h2d_bytes,
+            "d2h_bytes_per_step": host.d2h_bytes,
+            "path": "EmbeddingEngine.execute_batch (C ABI) with pinned host "
+                    "inputs copied in and pooled outputs copied out, "
+                    "synchronous per step",
+        },
+        "gpu_launches": launches,
+        "cpu_baseline": base,
+        "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+  wl.status.close()
+  wl.engine.close()
+  if world > 1:
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+  main()

@@ -1,0 +1,224 @@
+"""ctypes loader of the CPU oracle (oracle/xse_oracle.cc).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, by the smoke check and by the
+benchmark's CPU-baseline leg, never by the product. See xse_oracle.h for what
+the oracle restates and how it is pinned.
+"""
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libxse_oracle.so")
+
+OK, INVALID_ARGUMENT, NOT_FOUND, FAILED_PRECONDITION = 0, 3, 5, 9
+F32, BF16, I8_ROWWISE = 0, 1, 2
+SUM, MEAN, SQRTN = 1, 2, 3
+COMBINE = {"SUM": SUM, "MEAN": MEAN, "SQRT_N": SQRTN, "SQRTN": SQRTN}
+
+
+class Request(ctypes.Structure):
+  _fields_ = [
+      ("dtype", ctypes.c_int32),
+      ("combine", ctypes.c_int32),
+      ("table", ctypes.c_void_p),
+      ("scale", ctypes.c_void_p),
+      ("bias", ctypes.c_void_p),
+      ("vocab", ctypes.c_int64),
+      ("dim", ctypes.c_int64),
+      ("ids", ctypes.c_void_p),
+      ("num_ids", ctypes.c_int64),
+      ("offsets", ctypes.c_void_p),
+      ("offsets_i64", ctypes.c_int32),
+      ("num_offsets", ctypes.c_int64),
+      ("weights", ctypes.c_void_p),
+      ("num_weights", ctypes.c_int64),
+      ("out", ctypes.c_void_p),
+  ]
+
+
+def build():
+  subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _load():
+  if not os.path.exists(LIB_PATH):
+    build()
+  lib = ctypes.CDLL(LIB_PATH)
+  P, I32, I64, U64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64
+  lib.oracle_embedding_bag_batch.argtypes = [ctypes.POINTER(Request), I32, I32,
+                                             I64, ctypes.c_char_p, I32]
+  lib.oracle_assemble_bf16_accumulate.argtypes = [P, I64, I64, I32, P, I64, P,
+                                                  I64, P, P, ctypes.c_char_p,
+                                                  I32]
+  lib.oracle_dense_to_csr.argtypes = [P, I32, I64, I64, I64, P, P, P,
+                                      ctypes.c_char_p, I32]
+  lib.oracle_dense_lookup_row_pointers.argtypes = [I64, I64, P,
+                                                   ctypes.c_char_p, I32]
+  lib.oracle_dot_interaction.argtypes = [P, P, I64, I32, I32, P]
+  lib.oracle_dot_interaction.restype = None
+  lib.oracle_uniform.argtypes = [U64, U64, U64]
+  lib.oracle_uniform.restype = ctypes.c_double
+  lib.oracle_synth_rows_f32.argtypes = [U64, U64, I64, I64, I64, P]
+  lib.oracle_synth_rows_f32.restype = None
+  lib.oracle_synth_rows_bf16.argtypes = [U64, U64, I64, I64, I64, P]
+  lib.oracle_synth_rows_bf16.restype = None
+  lib.oracle_synth_rows_i8.argtypes = [U64, U64, I64, I64, I64, P, P, P]
+  lib.oracle_synth_rows_i8.restype = None
+  lib.oracle_zipf_rank.argtypes = [U64, U64, U64, I64, ctypes.c_double]
+  lib.oracle_zipf_rank.restype = I64
+  lib.oracle_host_cores.argtypes = []
+  lib.oracle_host_cores.restype = I32
+  return lib
+
+
+lib = _load()
+
+
+class OracleError(RuntimeError):
+
+  def __init__(self, code, message):
+    super().__init__(f"{code}: {message}")
+    self.code = code
+    self.message = message
+
+
+def _p(a):
+  return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def host_cores():
+  return lib.oracle_host_cores()
+
+
+class Bag:
+  """One request for the oracle, on numpy arrays."""
+
+  def __init__(self, table, ids, offsets, weights=None, combine="SUM",
+               dtype=F32, scale=None, bias=None, out=None):
+    self.table = np.ascontiguousarray(table)
+    self.ids = np.ascontiguousarray(ids, dtype=np.int64)
+    self.offsets = np.ascontiguousarray(offsets)
+    assert self.offsets.dtype in (np.int32, np.int64)
+    self.weights = None if weights is None else np.ascontiguousarray(
+        weights, dtype=np.float32)
+    self.combine = COMBINE[combine] if isinstance(combine, str) else combine
+    self.dtype = dtype
+    self.scale = None if scale is None else np.ascontiguousarray(
+        scale, dtype=np.float32)
+    self.bias = None if bias is None else np.ascontiguousarray(
+        bias, dtype=np.float32)
+    dim = self.table.shape[1]
+    self.out = out if out is not None else np.zeros(
+        (max(len(self.offsets) - 1, 0), dim), dtype=np.float32)
+
+  def c_request(self):
+    return Request(
+        dtype=self.dtype, combine=self.combine, table=_p(self.table),
+        scale=_p(self.scale), bias=_p(self.bias), vocab=self.table.shape[0],
+        dim=self.table.shape[1], ids=_p(self.ids), num_ids=len(self.ids),
+        offsets=_p(self.offsets),
+        offsets_i64=1 if self.offsets.dtype == np.int64 else 0,
+        num_offsets=len(self.offsets), weights=_p(self.weights),
+        num_weights=0 if self.weights is None else len(self.weights),
+        out=_p(self.out))
+
+
+def embedding_bag_batch(bags, num_threads=1, inline_threshold=65536):
+  """ExecuteEmbeddingBagBatch restatement; raises OracleError on failure."""
+  arr = (Request * len(bags))(*[b.c_request() for b in bags])
+  err = ctypes.create_string_buffer(1024)
+  rc = lib.oracle_embedding_bag_batch(arr, len(bags), num_threads,
+                                      inline_threshold, err, len(err))
+  if rc != OK:
+    raise OracleError(rc, err.value.decode())
+  return [b.out for b in bags]
+
+
+def embedding_bag(table, ids, offsets, weights=None, combine="SUM", dtype=F32,
+                  scale=None, bias=None, num_threads=1):
+  bag = Bag(table, ids, offsets, weights, combine, dtype, scale, bias)
+  return embedding_bag_batch([bag], num_threads)[0]
+
+
+def assemble_bf16_accumulate(table_bits, ids, row_pointers, weights=None,
+                             combine="SUM"):
+  """Reference bf16 path (bf16 accumulator); returns bf16 bits as uint16."""
+  table_bits = np.ascontiguousarray(table_bits, dtype=np.uint16)
+  ids = np.ascontiguousarray(ids, dtype=np.int64)
+  rp = np.ascontiguousarray(row_pointers, dtype=np.int32)
+  w = None if weights is None else np.ascontiguousarray(weights, np.float32)
+  out = np.zeros((len(rp) - 1, table_bits.shape[1]), dtype=np.uint16)
+  err = ctypes.create_string_buffer(1024)
+  rc = lib.oracle_assemble_bf16_accumulate(
+      _p(table_bits), table_bits.shape[0], table_bits.shape[1],
+      COMBINE[combine], _p(ids), len(ids), _p(rp), len(rp), _p(w), _p(out),
+      err, len(err))
+  if rc != OK:
+    raise OracleError(rc, err.value.decode())
+  return out
+
+
+def dense_to_csr(dense, pad_value=0):
+  dense = np.ascontiguousarray(dense)
+  assert dense.dtype in (np.int32, np.int64)
+  batch = dense.shape[0]
+  seq = dense.size // batch if batch > 0 else 0
+  ids = np.zeros(batch * seq + batch, dtype=np.int64)
+  rp = np.zeros(batch + 1, dtype=np.int32)
+  n = ctypes.c_int64()
+  err = ctypes.create_string_buffer(1024)
+  rc = lib.oracle_dense_to_csr(_p(dense), 1 if dense.dtype == np.int64 else 0,
+                               batch, seq, pad_value, _p(ids), _p(rp),
+                               ctypes.byref(n), err, len(err))
+  if rc != OK:
+    raise OracleError(rc, err.value.decode())
+  return ids[:n.value], rp
+
+
+def dense_lookup_row_pointers(batch, valency, materialize=True):
+  rp = np.zeros(batch + 1, dtype=np.int32) if materialize else None
+  err = ctypes.create_string_buffer(1024)
+  rc = lib.oracle_dense_lookup_row_pointers(batch, valency, _p(rp), err,
+                                            len(err))
+  if rc != OK:
+    raise OracleError(rc, err.value.decode())
+  return rp
+
+
+def dot_interaction(dense, pooled):
+  dense = np.ascontiguousarray(dense, dtype=np.float32)
+  pooled = np.ascontiguousarray(pooled, dtype=np.float32)
+  b, t, d = pooled.shape
+  rows = t + 1
+  out = np.zeros((b, d + rows * (rows - 1) // 2), dtype=np.float32)
+  lib.oracle_dot_interaction(_p(dense), _p(pooled), b, t, d, _p(out))
+  return out
+
+
+def synth_rows(dtype, seed, table, row0, nrows, dim):
+  if dtype == F32:
+    out = np.zeros((nrows, dim), dtype=np.float32)
+    lib.oracle_synth_rows_f32(seed, table, row0, nrows, dim, _p(out))
+    return out, None, None
+  if dtype == BF16:
+    out = np.zeros((nrows, dim), dtype=np.uint16)
+    lib.oracle_synth_rows_bf16(seed, table, row0, nrows, dim, _p(out))
+    return out, None, None
+  q = np.zeros((nrows, dim), dtype=np.int8)
+  s = np.zeros(nrows, dtype=np.float32)
+  b = np.zeros(nrows, dtype=np.float32)
+  lib.oracle_synth_rows_i8(seed, table, row0, nrows, dim, _p(q), _p(s), _p(b))
+  return q, s, b
+
+
+def zipf_rank(seed, stream, index, n, alpha):
+  return lib.oracle_zipf_rank(seed, stream, index, n, alpha)
+
+
+def bf16_bits_to_f32(bits):
+  return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(
+      np.float32)

@@ -1,0 +1,276 @@
+"""GPU parity tests of the pooled lookup: the CUDA path (called through the C
+ABI) against the CPU oracle on the same inputs. fp32-accumulated results are
+compared bit for bit (the kernels keep the reference's CSR addition order and
+rounding); error statuses and messages must match exactly."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from parity_helpers import (TORCH_DT, assert_bitwise, oracle_pool,
+                            random_csr, random_table, to_dev)
+
+pytestmark = pytest.mark.gpu
+
+
+def make_engine(xse, golden_tables):
+  eng = xse.EmbeddingEngine(0)
+  for name, t in golden_tables.items():
+    data = np.asarray(t["data"], np.float32).reshape(-1, t["dim"])
+    eng.add_table(name, data, t["combine"])
+    eng.register_feature(name, name)
+  return eng
+
+
+def golden_requests(xse, case, outputs):
+  reqs = []
+  for r, out in zip(case["requests"], outputs):
+    w = r.get("weights")
+    reqs.append(xse.BagRequest(
+        r["table"], to_dev(np.asarray(r["ids"], np.int64)),
+        to_dev(np.asarray(r["offsets"], np.int32)), out,
+        None if w is None else to_dev(np.asarray(w, np.float32))))
+  return reqs
+
+
+def test_golden_known_answers(xse, golden):
+  for case in golden["cases"]:
+    eng = make_engine(xse, case["tables"])
+    if "requests" in case:
+      outs = []
+      for r in case["requests"]:
+        dim = case["tables"][r["table"]]["dim"]
+        outs.append(torch.full((len(r["offsets"]) - 1, dim), -99.0,
+                               device="cuda"))
+      eng.execute_batch(golden_requests(xse, case, outs))
+      want = []
+      for r in case["requests"]:
+        t = case["tables"][r["table"]]
+        want.append(oracle.embedding_bag(
+            np.asarray(t["data"], np.float32).reshape(-1, t["dim"]), r["ids"],
+            np.asarray(r["offsets"], np.int32), r.get("weights"),
+            t["combine"]))
+    else:
+      outs, want = [], []
+      for entry in case["dense"]:
+        t = case["tables"][entry["table"]]
+        ids, rp = oracle.dense_to_csr(np.asarray(entry["ids"], np.int32),
+                                      entry["pad_value"])
+        outs.append(eng.pool(entry["table"], to_dev(ids), to_dev(rp)))
+        want.append(oracle.embedding_bag(
+            np.asarray(t["data"], np.float32).reshape(-1, t["dim"]), ids, rp,
+            combine=t["combine"]))
+    for got, w, expect in zip(outs, want, case["expect"]):
+      assert_bitwise(got.cpu().numpy(), w, case["name"])
+      np.testing.assert_allclose(got.cpu().numpy().ravel(), expect,
+                                 atol=case["tol"], rtol=0,
+                                 err_msg=case["name"])
+    eng.close()
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_golden_errors(xse, golden, fused):
+  for case in golden["errors"]:
+    eng = make_engine(xse, case["tables"])
+    outs = []
+    shared = None
+    weights_dev = {}
+    reqs = []
+    for k, r in enumerate(case["requests"]):
+      dim = case["tables"][r["table"]]["dim"]
+      nb = len(r["offsets"]) - 1
+      w = r.get("weights")
+      wd = None if w is None else to_dev(np.asarray(w, np.float32))
+      weights_dev[k] = wd
+      if r.get("output") == "shared":
+        if shared is None:
+          shared = torch.full((nb, dim), 23.0, device="cuda")
+        out = shared
+      elif r.get("output") == "weights":
+        out = wd
+      else:
+        out = torch.full((nb, dim), 17.0 + k, device="cuda")
+      outs.append(out)
+      reqs.append(xse.BagRequest(
+          r["table"], to_dev(np.asarray(r["ids"], np.int64)),
+          to_dev(np.asarray(r["offsets"], np.int64)), out, wd))
+    before = [o.clone() for o in outs]
+    with pytest.raises(xse.XseError) as e:
+      eng.execute_batch(reqs, fused=fused)
+    assert e.value.code == case["code"], case["name"]
+    assert e.value.message == case["message"], case["name"]
+    if not fused:  # strict mode writes nothing on error
+      for o, b in zip(outs, before):
+        assert torch.equal(o, b), case["name"]
+    eng.close()
+
+
+DTYPES = [oracle.F32, oracle.BF16, oracle.I8_ROWWISE]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("dim", [3, 16, 40, 64, 128, 256, 512])
+@pytest.mark.parametrize("combine", ["SUM", "MEAN", "SQRT_N"])
+def test_random_parity(xse, dtype, dim, combine):
+  if dtype == oracle.I8_ROWWISE and dim == 3:
+    dim = 5  # odd int8 rows still take the element-wise kernel
+  rng = np.random.default_rng(dtype * 100003 + dim * 31 + len(combine))
+  vocab = 300
+  host, dev, scale, bias = random_table(rng, dtype, vocab, dim)
+  eng = xse.EmbeddingEngine(0)
+  eng.add_table("t", dev, combine, scale=scale, bias=bias)
+  eng.register_feature("f", "t")
+  for weighted in (False, True):
+    for first in (0, 5):
+      ids, offsets = random_csr(rng, vocab, 97, 70, first=first)
+      w = rng.uniform(0, 1, len(ids)).astype(np.float32) if weighted else None
+      for off_dt in (np.int32, np.int64):
+        for id_dt in (torch.int32, torch.int64):
+          got = eng.pool("f", to_dev(ids, id_dt), to_dev(offsets.astype(off_dt)),
+                         None if w is None else to_dev(w))
+          want = oracle_pool(host, dtype, ids, offsets.astype(off_dt), w,
+                             combine, scale, bias)
+          assert_bitwise(got.cpu().numpy(), want,
+                         f"dtype={dtype} dim={dim} {combine} w={weighted} "
+                         f"first={first}")
+      got_fused = eng.pool("f", to_dev(ids), to_dev(offsets),
+                           None if w is None else to_dev(w), fused=True)
+      assert_bitwise(got_fused.cpu().numpy(), want, "fused")
+  eng.close()
+
+
+def test_strided_output_and_mixed_group(xse):
+  """One group mixing dtypes and dims, written into a [B, T, D] buffer like
+  the DLRM pooled layout, and a second group into plain outputs."""
+  rng = np.random.default_rng(11)
+  eng = xse.EmbeddingEngine(0)
+  specs = [(oracle.F32, 128, "SUM"), (oracle.BF16, 128, "MEAN"),
+           (oracle.I8_ROWWISE, 128, "SQRT_N"), (oracle.F32, 128, "MEAN")]
+  batch, hosts = 257, []
+  for k, (dt, dim, comb) in enumerate(specs):
+    host, dev, s, b = random_table(rng, dt, 1000 + k, dim)
+    hosts.append((host, s, b))
+    eng.add_table(f"t{k}", dev, comb, scale=s, bias=b)
+    eng.register_feature(f"f{k}", f"t{k}")
+  pooled = torch.full((batch, len(specs), 128), -1.0, device="cuda")
+  reqs, want = [], []
+  for k, (dt, dim, comb) in enumerate(specs):
+    ids, offsets = random_csr(rng, 1000 + k, batch, 40)
+    w = rng.uniform(0, 1, len(ids)).astype(np.float32) if k % 2 else None
+    reqs.append(xse.BagRequest(f"f{k}", to_dev(ids), to_dev(offsets),
+                               pooled[:, k, :], None if w is None else to_dev(w),
+                               output_stride=len(specs) * 128))
+    host, s, b = hosts[k]
+    want.append(oracle_pool(host, dt, ids, offsets, w, comb, s, b))
+  eng.execute_batch(reqs)
+  got = pooled.cpu().numpy()
+  for k in range(len(specs)):
+    assert_bitwise(got[:, k, :], want[k], f"table {k}")
+  eng.close()
+
+
+def test_shard_windows_sum_to_whole(xse):
+  """Row-wise shards: each engine holds a window of rows; ids outside it are
+  skipped. The per-shard partials add up to the whole-table pool."""
+  rng = np.random.default_rng(12)
+  vocab, dim = 1000, 64
+  host, dev, _, _ = random_table(rng, oracle.F32, vocab, dim)
+  ids, offsets = random_csr(rng, vocab, 200, 30)
+  whole = oracle_pool(host, oracle.F32, ids, offsets, None, "SUM")
+  bounds = [0, 250, 600, 1000]
+  total = np.zeros_like(whole, dtype=np.float64)
+  for s in range(3):
+    eng = xse.EmbeddingEngine(0)
+    lo, hi = bounds[s], bounds[s + 1]
+    eng.add_table("t", dev[lo:hi], "SUM", vocab=vocab, row_begin=lo,
+                  row_end=hi)
+    eng.register_feature("f", "t")
+    part = eng.pool("f", to_dev(ids), to_dev(offsets)).cpu().numpy()
+    keep = (ids >= lo) & (ids < hi)
+    want = oracle_pool(host, oracle.F32, np.where(keep, ids, 0), offsets,
+                       keep.astype(np.float32), "SUM")
+    np.testing.assert_allclose(part, want, rtol=1e-6, atol=1e-6)
+    total += part
+    eng.close()
+  np.testing.assert_allclose(total, whole, rtol=1e-5, atol=1e-5)
+
+
+def test_async_status_and_errors(xse):
+  rng = np.random.default_rng(13)
+  host, dev, _, _ = random_table(rng, oracle.F32, 100, 32)
+  eng = xse.EmbeddingEngine(0)
+  eng.add_table("t", dev, "SUM")
+  eng.register_feature("f", "t")
+  eng.register_feature("seq", "t", max_sequence_length=4)
+  ids, offsets = random_csr(rng, 100, 50, 10)
+  out = torch.empty((50, 32), device="cuda")
+  st = xse.Status(8)
+  eng.execute_batch([xse.BagRequest("f", to_dev(ids), to_dev(offsets), out)],
+                    status=st)
+  st.wait()
+  assert_bitwise(out.cpu().numpy(), oracle_pool(host, oracle.F32, ids, offsets,
+                                                None, "SUM"))
+  bad = ids.copy()
+  bad[len(bad) // 2] = 100
+  eng.execute_batch([xse.BagRequest("f", to_dev(bad), to_dev(offsets), out)],
+                    status=st, fused=True)
+  with pytest.raises(xse.XseError) as e:
+    st.wait()
+  assert e.value.message == (
+      f"FP32 embedding-bag request 0: Embedding ID (100) at index "
+      f"{len(bad) // 2} is out of bounds [0, 100).")
+  with pytest.raises(xse.XseError) as e:
+    eng.execute_batch([])
+  assert e.value.message == "Embedding batch requires at least one request."
+  with pytest.raises(xse.XseError) as e:
+    eng.execute_batch([xse.BagRequest("nope", to_dev(ids), to_dev(offsets),
+                                      out)])
+  assert e.value.code == xse._capi.NOT_FOUND
+  with pytest.raises(xse.XseError) as e:
+    eng.execute_batch([xse.BagRequest("seq", to_dev(ids), to_dev(offsets),
+                                      out)])
+  assert e.value.code == xse._capi.UNIMPLEMENTED
+  with pytest.raises(xse.XseError) as e:
+    eng.add_table("t", dev, "SUM")
+  assert e.value.code == xse._capi.ALREADY_EXISTS
+  with pytest.raises(xse.XseError) as e:
+    eng.register_feature("f", "t")
+  assert e.value.code == xse._capi.ALREADY_EXISTS
+  eng.clear()
+  with pytest.raises(xse.XseError) as e:
+    eng.pool("f", to_dev(ids), to_dev(offsets))
+  assert e.value.code == xse._capi.NOT_FOUND
+  st.close()
+  eng.close()
+
+
+def test_addition_order_fixture(xse):
+  import os  # pylint: disable=import-outside-toplevel
+  g = np.load(os.path.join(os.path.dirname(__file__), "golden",
+                           "numpy_lookup.npz"))
+  eng = xse.EmbeddingEngine(0)
+  eng.add_table("t", g["order_table"], "SUM")
+  eng.register_feature("f", "t")
+  got = eng.pool("f", to_dev(g["order_ids"]), to_dev(g["order_offsets"]))
+  assert_bitwise(got.cpu().numpy(), g["order_out"], "order")
+  for i in range(int(g["num_tables"])):
+    eng.add_table(f"n{i}", g[f"table_{i}"], "SUM")
+    eng.register_feature(f"n{i}", f"n{i}")
+    dense = g[f"ids_{i}"]
+    b, v = dense.shape
+    offs = np.arange(b + 1, dtype=np.int32) * v
+    got = eng.pool(f"n{i}", to_dev(dense.ravel()), to_dev(offs)).cpu().numpy()
+    want = oracle.embedding_bag(g[f"table_{i}"], dense.ravel(), offs)
+    assert_bitwise(got, want, f"numpy fixture {i}")
+    np.testing.assert_allclose(got, g[f"out_{i}"], rtol=1e-5, atol=1e-6)
+  eng.close()
+
+
+def test_dtype_table_views(xse):
+  assert TORCH_DT[oracle.BF16] == torch.bfloat16
+  eng = xse.EmbeddingEngine(0)
+  eng.add_table("t", np.zeros((4, 8), np.float32), "MEAN")
+  info = eng.table_info("t")
+  assert (info.vocab, info.dim, info.combine) == (4, 8, 2)
+  eng.close()

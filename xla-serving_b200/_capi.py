@@ -1,0 +1,173 @@
+"""ctypes bindings of the engine's C ABI (include/xse_emb.h).
+
+The shared library libxse_emb.so is built in-tree (see Makefile). Loading it is
+mandatory: there is no CPU fallback, so a missing or unloadable library raises
+ImportError at import time.
+"""
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libxse_emb.so")
+
+# absl::StatusCode numbering.
+OK = 0
+CANCELLED = 1
+UNKNOWN = 2
+INVALID_ARGUMENT = 3
+DEADLINE_EXCEEDED = 4
+NOT_FOUND = 5
+ALREADY_EXISTS = 6
+RESOURCE_EXHAUSTED = 8
+FAILED_PRECONDITION = 9
+UNIMPLEMENTED = 12
+INTERNAL = 13
+
+STATUS_NAMES = {
+    OK: "OK",
+    CANCELLED: "CANCELLED",
+    UNKNOWN: "UNKNOWN",
+    INVALID_ARGUMENT: "INVALID_ARGUMENT",
+    DEADLINE_EXCEEDED: "DEADLINE_EXCEEDED",
+    NOT_FOUND: "NOT_FOUND",
+    ALREADY_EXISTS: "ALREADY_EXISTS",
+    RESOURCE_EXHAUSTED: "RESOURCE_EXHAUSTED",
+    FAILED_PRECONDITION: "FAILED_PRECONDITION",
+    UNIMPLEMENTED: "UNIMPLEMENTED",
+    INTERNAL: "INTERNAL",
+}
+
+DT_F32, DT_BF16, DT_I8_ROWWISE = 0, 1, 2
+COMBINE_SUM, COMBINE_MEAN, COMBINE_SQRTN = 1, 2, 3
+INDEX_I32, INDEX_I64 = 0, 1
+PLACE_COPY_FROM_HOST, PLACE_COPY_FROM_DEVICE, PLACE_ADOPT_DEVICE = 0, 1, 2
+EXEC_STRICT, EXEC_FUSED, EXEC_ASYNC = 0, 1, 2
+
+COMBINE_MODES = {"SUM": COMBINE_SUM, "MEAN": COMBINE_MEAN,
+                 "SQRT_N": COMBINE_SQRTN, "SQRTN": COMBINE_SQRTN}
+
+
+class XseError(RuntimeError):
+  """A non-OK status returned through the C ABI."""
+
+  def __init__(self, code, message):
+    super().__init__(f"{STATUS_NAMES.get(code, code)}: {message}")
+    self.code = code
+    self.message = message
+
+
+class EngineOptions(ctypes.Structure):
+  _fields_ = [("device", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class TableDesc(ctypes.Structure):
+  _fields_ = [
+      ("name", ctypes.c_char_p),
+      ("dtype", ctypes.c_int32),
+      ("combine", ctypes.c_int32),
+      ("vocab", ctypes.c_int64),
+      ("dim", ctypes.c_int32),
+      ("placement", ctypes.c_int32),
+      ("rows", ctypes.c_void_p),
+      ("scale", ctypes.c_void_p),
+      ("bias", ctypes.c_void_p),
+      ("row_begin", ctypes.c_int64),
+      ("row_end", ctypes.c_int64),
+  ]
+
+
+class TableInfo(ctypes.Structure):
+  _fields_ = [
+      ("dtype", ctypes.c_int32),
+      ("combine", ctypes.c_int32),
+      ("dim", ctypes.c_int32),
+      ("reserved", ctypes.c_int32),
+      ("vocab", ctypes.c_int64),
+      ("row_begin", ctypes.c_int64),
+      ("row_end", ctypes.c_int64),
+      ("rows", ctypes.c_void_p),
+  ]
+
+
+class BagRequest(ctypes.Structure):
+  _fields_ = [
+      ("feature_name", ctypes.c_char_p),
+      ("ids", ctypes.c_void_p),
+      ("ids_type", ctypes.c_int32),
+      ("offsets_type", ctypes.c_int32),
+      ("num_ids", ctypes.c_int64),
+      ("offsets", ctypes.c_void_p),
+      ("num_offsets", ctypes.c_int64),
+      ("weights", ctypes.c_void_p),
+      ("num_weights", ctypes.c_int64),
+      ("output", ctypes.c_void_p),
+      ("output_stride", ctypes.c_int64),
+  ]
+
+
+_I = ctypes.c_int
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+_U64 = ctypes.c_uint64
+
+# name -> (restype, argtypes); every entry point declared in include/xse_emb.h.
+SIGNATURES = {
+    "xse_last_error": (ctypes.c_char_p, []),
+    "xse_abi_version": (_I32, []),
+    "xse_last_launch_count": (_I32, []),
+    "xse_engine_create": (_I, [ctypes.POINTER(EngineOptions), _P]),
+    "xse_engine_destroy": (None, [_P]),
+    "xse_engine_add_table": (_I, [_P, ctypes.POINTER(TableDesc)]),
+    "xse_engine_register_feature": (_I, [_P, ctypes.c_char_p, ctypes.c_char_p,
+                                         _I32]),
+    "xse_engine_clear": (_I, [_P]),
+    "xse_engine_table_info": (_I, [_P, ctypes.c_char_p,
+                                   ctypes.POINTER(TableInfo)]),
+    "xse_engine_feature_table": (_I, [_P, ctypes.c_char_p, ctypes.c_char_p,
+                                      _I32, ctypes.POINTER(_I32)]),
+    "xse_status_create": (_I, [_I32, _P]),
+    "xse_status_destroy": (None, [_P]),
+    "xse_engine_execute_batch": (_I, [_P, ctypes.POINTER(BagRequest), _I32, _P,
+                                      _I32, _P]),
+    "xse_status_wait": (_I, [_P, _P]),
+    "xse_engine_set_profiling": (_I, [_P, _I32]),
+    "xse_engine_profile_read": (_I, [_P, ctypes.POINTER(ctypes.c_double),
+                                     ctypes.POINTER(_I64)]),
+    "xse_dot_interaction": (_I, [_P, _P, _I64, _I32, _I32, _P, _P]),
+    "xse_synth_table": (_I, [_P, _P, _P, _I32, _U64, _U64, _I64, _I64, _I32,
+                             _P]),
+    "xse_synth_lengths": (_I, [_P, _I64, _I32, _I32, _U64, _U64, _P]),
+    "xse_synth_ids": (_I, [_P, _I64, _I64, ctypes.c_double, _U64, _U64, _U64,
+                           _U64, _I64, _P]),
+    "xse_synth_weights": (_I, [_P, _I64, _U64, _U64, _I64, _P]),
+}
+
+
+def _load():
+  if not os.path.exists(LIB_PATH):
+    raise ImportError(
+        f"{LIB_PATH} is missing: build it with `make -C {_HERE}` "
+        "(the engine has no CPU fallback)")
+  lib = ctypes.CDLL(LIB_PATH)
+  for name, (restype, argtypes) in SIGNATURES.items():
+    fn = getattr(lib, name)
+    fn.restype = restype
+    fn.argtypes = argtypes
+  return lib
+
+
+lib = _load()
+
+
+def last_error():
+  msg = lib.xse_last_error()
+  return msg.decode() if msg else ""
+
+
+def check(rc):
+  """Raises XseError for a non-OK status code."""
+  if rc != OK:
+    raise XseError(rc, last_error())
+  return rc

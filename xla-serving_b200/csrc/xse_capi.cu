@@ -1,0 +1,883 @@
+// C ABI of the engine (declared in include/xse_emb.h).
+//
+// The engine mirrors CpuEmbeddingEngine (data/cpu_embedding/cc/
+// cpu_embedding_engine.{h,cc}): a registry of tables and feature specs under
+// two mutexes taken in the order specs -> tables. Tables live in HBM. A group
+// execution follows internal::ExecuteEmbeddingBagBatch (embedding_bag.cc:
+// 477-535): validate the whole group, check output isolation, then pool; the
+// validation of offsets and ids runs on the device and its result gates the
+// pooling kernel, so a failing group writes nothing.
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <cinttypes>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/xse_emb.h"
+#include "xse_internal.h"
+
+extern "C" int xse_synth_table_impl(void*, float*, float*, int32_t, uint64_t,
+                                    uint64_t, int64_t, int64_t, int32_t,
+                                    cudaStream_t);
+extern "C" int xse_synth_lengths_impl(int64_t*, int64_t, int32_t, int32_t,
+                                      uint64_t, uint64_t, cudaStream_t);
+extern "C" int xse_synth_ids_impl(int64_t*, int64_t, int64_t, double,
+                                  uint64_t, uint64_t, uint64_t, uint64_t,
+                                  int64_t, cudaStream_t);
+extern "C" int xse_synth_weights_impl(float*, int64_t, uint64_t, uint64_t,
+                                      int64_t, cudaStream_t);
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local int32_t g_last_launches = 0;
+
+int SetError(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list args;
+  va_start(args, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, args);
+  va_end(args);
+  g_last_error = buf;
+  return code;
+}
+
+int Ok() {
+  g_last_error.clear();
+  return XSE_OK;
+}
+
+int CudaError(cudaError_t e, const char* what) {
+  return SetError(XSE_INTERNAL, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct Table {
+  std::string name;
+  int32_t dtype = 0, combine = 1, dim = 0;
+  int64_t vocab = 0, row_begin = 0, row_end = 0;
+  void* rows = nullptr;          // device
+  float2* scale_bias = nullptr;  // device, int8 rows
+  bool owns_rows = false;
+  int device = 0;
+  ~Table() {
+    if (rows == nullptr && scale_bias == nullptr) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    if (owns_rows && rows != nullptr) cudaFree(rows);
+    if (scale_bias != nullptr) cudaFree(scale_bias);
+    cudaSetDevice(prev);
+  }
+};
+
+struct Feature {
+  std::string table;
+  int32_t max_sequence_length = 0;
+};
+
+size_t ElemBytes(int32_t dtype) {
+  return dtype == XSE_DT_F32 ? 4 : dtype == XSE_DT_BF16 ? 2 : 1;
+}
+
+// Host-detectable error of one request, ordered as the checks of
+// ValidateEmbeddingBagInput (embedding_bag.cc:89-144).
+enum HostStage {
+  kStageNone = 0,
+  kStageEarly = 1,      // before the offset checks
+  kStageIdsNull = 2,    // after the offset/size checks, before id bounds
+  kStageWeightsNull = 3,
+};
+
+struct RequestMeta {
+  int stage = kStageNone;
+  int code = XSE_OK;
+  std::string message;
+  const void* ids = nullptr;
+  int32_t ids64 = 1;
+  int64_t vocab = 0;
+};
+
+}  // namespace
+
+struct xse_status {
+  int device = 0;
+  int32_t capacity = 0;
+  xse::DevStatus* dev = nullptr;
+  xse::DevStatus* host = nullptr;  // pinned mirror
+  std::vector<RequestMeta> meta;
+  int32_t n = 0;
+  bool pending = false;
+  int early_code = XSE_OK;  // host-side failure decided at launch time
+  std::string early_message;
+};
+
+struct xse_engine {
+  int device = 0;
+  std::mutex specs_mu;
+  std::mutex tables_mu;
+  std::unordered_map<std::string, Feature> features;
+  std::unordered_map<std::string, std::shared_ptr<Table>> tables;
+  std::mutex default_status_mu;
+  xse_status* default_status = nullptr;
+  // Kernel timing: event pairs recorded around pooling kernels.
+  std::mutex profile_mu;
+  bool profiling = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> profile_events;
+  size_t profile_used = 0;
+};
+
+namespace {
+
+// Resolves the group's errors in request order, mirroring the order of the
+// reference's per-request checks. Returns the status code.
+int ResolveStatus(xse_status* st) {
+  for (int32_t i = 0; i < st->n; ++i) {
+    const RequestMeta& m = st->meta[i];
+    if (m.stage == kStageEarly) return SetError(m.code, "%s", m.message.c_str());
+    const unsigned int flags = st->host->req[i].flags;
+    const char* msg = nullptr;
+    if (flags & xse::kErrBadOffsets) {
+      msg = "Row pointers must be non-negative and monotonic.";
+    } else if (flags & xse::kErrLastExceedsIds) {
+      msg = "Final row pointer exceeds embedding IDs size.";
+    } else if (flags & xse::kErrLastExceedsWeights) {
+      msg = "Final row pointer exceeds weights size.";
+    }
+    if (msg != nullptr) {
+      return SetError(XSE_INVALID_ARGUMENT,
+                      "FP32 embedding-bag request %d: %s", i, msg);
+    }
+    if (m.stage == kStageIdsNull || m.stage == kStageWeightsNull) {
+      return SetError(m.code, "%s", m.message.c_str());
+    }
+    if (flags & xse::kErrBadId) {
+      const int64_t index =
+          static_cast<int64_t>(~st->host->req[i].inv_min_bad_index);
+      int64_t id = 0;
+      if (m.ids64) {
+        cudaMemcpy(&id, static_cast<const int64_t*>(m.ids) + index,
+                   sizeof(id), cudaMemcpyDeviceToHost);
+      } else {
+        int32_t id32 = 0;
+        cudaMemcpy(&id32, static_cast<const int32_t*>(m.ids) + index,
+                   sizeof(id32), cudaMemcpyDeviceToHost);
+        id = id32;
+      }
+      return SetError(XSE_INVALID_ARGUMENT,
+                      "FP32 embedding-bag request %d: Embedding ID (%" PRId64
+                      ") at index %" PRId64 " is out of bounds [0, %" PRId64
+                      ").",
+                      i, id, index, m.vocab);
+    }
+  }
+  if (st->early_code != XSE_OK) {
+    return SetError(st->early_code, "%s", st->early_message.c_str());
+  }
+  return Ok();
+}
+
+struct Range {
+  uintptr_t begin, end;
+  int32_t request;
+  const char* kind;
+};
+
+void AddRange(const void* p, int64_t bytes, int32_t request, const char* kind,
+              std::vector<Range>* out) {
+  if (p == nullptr || bytes <= 0) return;
+  const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+  out->push_back({b, b + static_cast<uintptr_t>(bytes), request, kind});
+}
+
+// ValidateOutputIsolation (embedding_bag.cc:304-351) over device ranges.
+int CheckIsolation(const xse_bag_request* reqs,
+                   const std::vector<std::shared_ptr<Table>>& tables,
+                   int32_t n, std::string* message) {
+  std::vector<Range> outputs, inputs;
+  for (int32_t i = 0; i < n; ++i) {
+    const xse_bag_request& r = reqs[i];
+    const Table& t = *tables[i];
+    const int64_t bags = r.num_offsets - 1;
+    const int64_t stride = r.output_stride > 0 ? r.output_stride : t.dim;
+    if (bags > 0) {
+      AddRange(r.output, ((bags - 1) * stride + t.dim) * 4, i, "output",
+               &outputs);
+    }
+    AddRange(r.ids, r.num_ids * (r.ids_type == XSE_INDEX_I64 ? 8 : 4), i,
+             "embedding-ID", &inputs);
+    AddRange(r.offsets,
+             r.num_offsets * (r.offsets_type == XSE_INDEX_I64 ? 8 : 4), i,
+             "row-pointer", &inputs);
+    AddRange(r.weights, r.num_weights * 4, i, "weight", &inputs);
+    AddRange(t.rows,
+             (t.row_end - t.row_begin) * t.dim *
+                 static_cast<int64_t>(ElemBytes(t.dtype)),
+             i, "embedding-table", &inputs);
+  }
+  std::sort(outputs.begin(), outputs.end(),
+            [](const Range& a, const Range& b) { return a.begin < b.begin; });
+  char buf[256];
+  for (size_t k = 1; k < outputs.size(); ++k) {
+    if (outputs[k - 1].begin < outputs[k].end &&
+        outputs[k].begin < outputs[k - 1].end) {
+      snprintf(buf, sizeof(buf),
+               "FP32 embedding-bag request outputs %d and %d overlap.",
+               outputs[k - 1].request, outputs[k].request);
+      *message = buf;
+      return XSE_INVALID_ARGUMENT;
+    }
+  }
+  for (const Range& o : outputs) {
+    for (const Range& in : inputs) {
+      if (o.begin < in.end && in.begin < o.end) {
+        snprintf(buf, sizeof(buf),
+                 "FP32 embedding-bag request %d output overlaps request %d %s "
+                 "storage.",
+                 o.request, in.request, in.kind);
+        *message = buf;
+        return XSE_INVALID_ARGUMENT;
+      }
+    }
+  }
+  return XSE_OK;
+}
+
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    cudaGetDevice(&prev_);
+    if (prev_ != device) cudaSetDevice(device);
+    device_ = device;
+  }
+  ~DeviceGuard() {
+    if (prev_ != device_) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = 0, device_ = 0;
+};
+
+int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
+                 cudaStream_t stream, int32_t flags, xse_status* st) {
+  g_last_launches = 0;
+  if (n <= 0 || reqs == nullptr) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Embedding batch requires at least one request.");
+  }
+  if (n > st->capacity) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Embedding batch has %d requests; the status block holds "
+                    "%d.",
+                    n, st->capacity);
+  }
+  // Resolve specs and tables under the same lock order as Clear
+  // (cpu_embedding_engine.cc:161-186).
+  std::vector<std::shared_ptr<Table>> tables(static_cast<size_t>(n));
+  {
+    std::lock_guard<std::mutex> spec_lock(engine->specs_mu);
+    std::lock_guard<std::mutex> table_lock(engine->tables_mu);
+    for (int32_t i = 0; i < n; ++i) {
+      const char* fname = reqs[i].feature_name ? reqs[i].feature_name : "";
+      auto spec = engine->features.find(fname);
+      if (spec == engine->features.end()) {
+        return SetError(XSE_NOT_FOUND, "Feature spec not found for: %s", fname);
+      }
+      if (spec->second.max_sequence_length != 0) {
+        return SetError(XSE_UNIMPLEMENTED,
+                        "Batch request %d requires a non-sequence feature "
+                        "specification.",
+                        i);
+      }
+      auto table = engine->tables.find(spec->second.table);
+      if (table == engine->tables.end()) {
+        return SetError(XSE_NOT_FOUND, "Table not found for: %s",
+                        spec->second.table.c_str());
+      }
+      tables[i] = table->second;
+    }
+  }
+
+  DeviceGuard guard(engine->device);
+  st->n = n;
+  st->pending = false;
+  st->early_code = XSE_OK;
+  st->early_message.clear();
+  st->meta.assign(static_cast<size_t>(n), RequestMeta());
+
+  // Host-side checks (PrepareRequest, embedding_bag.cc:235-251).
+  std::vector<xse::BagDesc> descs;
+  descs.reserve(static_cast<size_t>(n));
+  bool any_early = false;
+  char buf[512];
+  for (int32_t i = 0; i < n; ++i) {
+    const xse_bag_request& r = reqs[i];
+    const Table& t = *tables[i];
+    RequestMeta& m = st->meta[i];
+    m.ids = r.ids;
+    m.ids64 = r.ids_type == XSE_INDEX_I64;
+    m.vocab = t.vocab;
+    auto early = [&](int stage, int code, const char* text, bool prefix) {
+      if (prefix) {
+        snprintf(buf, sizeof(buf), "FP32 embedding-bag request %d: %s", i,
+                 text);
+      } else {
+        snprintf(buf, sizeof(buf), text, i);
+      }
+      m.stage = stage;
+      m.code = code;
+      m.message = buf;
+    };
+    if (r.output == nullptr) {
+      early(kStageEarly, XSE_INVALID_ARGUMENT,
+            "FP32 embedding-bag request %d requires an output allocator.",
+            false);
+    } else if ((r.ids_type != XSE_INDEX_I32 && r.ids_type != XSE_INDEX_I64) ||
+               (r.offsets_type != XSE_INDEX_I32 &&
+                r.offsets_type != XSE_INDEX_I64)) {
+      early(kStageEarly, XSE_INVALID_ARGUMENT,
+            "Embedding IDs and row pointers must be int32 or int64.", true);
+    } else if (r.num_offsets < 2 || r.offsets == nullptr) {
+      early(kStageEarly, XSE_INVALID_ARGUMENT,
+            "Row pointers must contain at least two elements.", true);
+    } else if (r.num_ids < 0 || r.num_weights < 0 ||
+               (r.output_stride != 0 && r.output_stride < t.dim)) {
+      early(kStageEarly, XSE_INVALID_ARGUMENT,
+            "Request sizes must be non-negative and the output stride at "
+            "least the embedding dimension.",
+            true);
+    } else if (r.ids == nullptr && r.num_ids > 0) {
+      early(kStageIdsNull, XSE_INVALID_ARGUMENT,
+            "Embedding-ID storage must be non-null.", true);
+    } else if (r.weights == nullptr && r.num_weights > 0) {
+      early(kStageWeightsNull, XSE_INVALID_ARGUMENT,
+            "Weight storage must be non-null.", true);
+    }
+    if (m.stage == kStageEarly) {
+      any_early = true;
+      continue;
+    }
+    xse::BagDesc d{};
+    d.rows = t.rows;
+    d.scale_bias = t.scale_bias;
+    d.ids = m.stage == kStageIdsNull ? nullptr : r.ids;
+    d.offsets = r.offsets;
+    d.weights = (r.num_weights > 0 && m.stage != kStageWeightsNull)
+                    ? r.weights
+                    : nullptr;
+    d.out = r.output;
+    d.out_stride = r.output_stride > 0 ? r.output_stride : t.dim;
+    d.vocab = t.vocab;
+    d.row_begin = t.row_begin;
+    d.row_end = t.row_end;
+    d.num_ids = r.num_ids;
+    d.num_weights = r.num_weights;
+    d.num_bags = r.num_offsets - 1;
+    d.dim = t.dim;
+    d.slot = i;
+    d.combine = static_cast<int8_t>(t.combine);
+    d.ids64 = static_cast<int8_t>(r.ids_type == XSE_INDEX_I64);
+    d.offs64 = static_cast<int8_t>(r.offsets_type == XSE_INDEX_I64);
+    d.vec_out = static_cast<int8_t>(
+        (reinterpret_cast<uintptr_t>(r.output) & 15u) == 0 &&
+        d.out_stride % 4 == 0);
+    descs.push_back(d);
+  }
+  // The first request's early error wins outright when no earlier request
+  // can fail on the device.
+  if (any_early && st->meta[0].stage == kStageEarly) {
+    return SetError(st->meta[0].code, "%s", st->meta[0].message.c_str());
+  }
+  std::string iso_message;
+  int iso_code = XSE_OK;
+  if (!any_early) {
+    iso_code = CheckIsolation(reqs, tables, n, &iso_message);
+  }
+
+  cudaError_t e = cudaMemsetAsync(st->dev, 0, xse::DevStatusBytes(n), stream);
+  if (e != cudaSuccess) return CudaError(e, "status reset");
+  const bool fused = (flags & XSE_EXEC_FUSED) != 0;
+  const bool validate_only = any_early || iso_code != XSE_OK;
+  const bool any_soft = std::any_of(
+      st->meta.begin(), st->meta.end(),
+      [](const RequestMeta& m) { return m.stage != kStageNone; });
+
+  // Validation pass over every descriptor (strict mode, or whenever the
+  // group is known to fail and only its error order is needed).
+  int launches = 0;
+  if (!fused || validate_only || any_soft) {
+    for (size_t base = 0; base < descs.size();
+         base += xse::kMaxDescsPerLaunch) {
+      xse::PoolParams p{};
+      p.status = st->dev;
+      int64_t work = 0;
+      const size_t cnt =
+          std::min<size_t>(xse::kMaxDescsPerLaunch, descs.size() - base);
+      for (size_t k = 0; k < cnt; ++k) {
+        p.d[k] = descs[base + k];
+        p.d[k].work_begin = work;
+        work += p.d[k].num_bags + 1 + p.d[k].num_ids;
+      }
+      p.n = static_cast<int32_t>(cnt);
+      e = xse::LaunchValidate(p, work, stream);
+      if (e != cudaSuccess) return CudaError(e, "validation launch");
+      ++launches;
+    }
+  }
+  std::pair<cudaEvent_t, cudaEvent_t> timing{nullptr, nullptr};
+  if (!validate_only && !any_soft) {
+    {
+      std::lock_guard<std::mutex> lock(engine->profile_mu);
+      if (engine->profiling) {
+        if (engine->profile_used == engine->profile_events.size()) {
+          cudaEvent_t a, b;
+          cudaEventCreate(&a);
+          cudaEventCreate(&b);
+          engine->profile_events.emplace_back(a, b);
+        }
+        timing = engine->profile_events[engine->profile_used++];
+      }
+    }
+    if (timing.first != nullptr) cudaEventRecord(timing.first, stream);
+    // Group descriptors by kernel layout, keeping request order within each.
+    std::map<std::tuple<int, int, int>, std::vector<xse::BagDesc>> groups;
+    for (const xse::BagDesc& d : descs) {
+      const xse::Layout l =
+          xse::ChooseLayout(tables[d.slot]->dtype, d.dim, d.rows);
+      const int v = tables[d.slot]->dtype == XSE_DT_I8_ROWWISE &&
+                            d.scale_bias == nullptr
+                        ? 0
+                        : l.v;
+      groups[{l.dtype, l.g, v}].push_back(d);
+    }
+    for (auto& [key, list] : groups) {
+      const xse::Layout l{std::get<0>(key), std::get<1>(key), std::get<2>(key)};
+      for (size_t base = 0; base < list.size();
+           base += xse::kMaxDescsPerLaunch) {
+        xse::PoolParams p{};
+        p.status = st->dev;
+        p.fused_checks = fused ? 1 : 0;
+        const size_t cnt =
+            std::min<size_t>(xse::kMaxDescsPerLaunch, list.size() - base);
+        int64_t tasks = 0;
+        for (size_t k = 0; k < cnt; ++k) {
+          p.d[k] = list[base + k];
+          p.d[k].task_begin = tasks;
+          tasks += p.d[k].num_bags;
+        }
+        p.n = static_cast<int32_t>(cnt);
+        p.total_tasks = tasks;
+        e = xse::LaunchPool(l, p, stream, &launches);
+        if (e != cudaSuccess) return CudaError(e, "pooling launch");
+      }
+    }
+    if (timing.second != nullptr) cudaEventRecord(timing.second, stream);
+  }
+  g_last_launches = launches;
+  e = cudaMemcpyAsync(st->host, st->dev, xse::DevStatusBytes(n),
+                      cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return CudaError(e, "status copy");
+  if (iso_code != XSE_OK) {
+    st->early_code = iso_code;
+    st->early_message = iso_message;
+  } else if (any_early || any_soft) {
+    // Ordering decided after the device validation; nothing was pooled.
+  }
+  st->pending = true;
+  if ((flags & XSE_EXEC_ASYNC) != 0 && !validate_only && !any_soft) {
+    return Ok();
+  }
+  e = cudaStreamSynchronize(stream);
+  st->pending = false;
+  if (e != cudaSuccess) return CudaError(e, "stream synchronize");
+  const int code = ResolveStatus(st);
+  if (code == XSE_OK && (any_early || any_soft)) {
+    // Unreachable: an early or soft error always resolves to a failure.
+    return SetError(XSE_INTERNAL, "unresolved request error");
+  }
+  return code;
+}
+
+int CreateStatus(int device, int32_t capacity, xse_status** out) {
+  auto st = std::make_unique<xse_status>();
+  st->device = device;
+  st->capacity = capacity;
+  const size_t bytes = xse::DevStatusBytes(capacity);
+  cudaError_t e = cudaMalloc(&st->dev, bytes);
+  if (e != cudaSuccess) return CudaError(e, "status allocation");
+  e = cudaMallocHost(&st->host, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(st->dev);
+    return CudaError(e, "status allocation");
+  }
+  std::memset(st->host, 0, bytes);
+  *out = st.release();
+  return XSE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* xse_last_error(void) { return g_last_error.c_str(); }
+int32_t xse_abi_version(void) { return XSE_ABI_VERSION; }
+int32_t xse_last_launch_count(void) { return g_last_launches; }
+
+int xse_engine_create(const xse_engine_options* options, xse_engine** out) {
+  if (out == nullptr) return SetError(XSE_INVALID_ARGUMENT, "out is null");
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count <= 0) {
+    return SetError(XSE_FAILED_PRECONDITION,
+                    "No CUDA device is available for the embedding engine.");
+  }
+  auto engine = std::make_unique<xse_engine>();
+  engine->device = options ? options->device : 0;
+  if (engine->device < 0 || engine->device >= count) {
+    return SetError(XSE_INVALID_ARGUMENT, "Device %d does not exist.",
+                    engine->device);
+  }
+  DeviceGuard guard(engine->device);
+  const int code = CreateStatus(engine->device, 256, &engine->default_status);
+  if (code != XSE_OK) return code;
+  *out = engine.release();
+  return Ok();
+}
+
+void xse_status_destroy(xse_status* status) {
+  if (status == nullptr) return;
+  DeviceGuard guard(status->device);
+  cudaFree(status->dev);
+  cudaFreeHost(status->host);
+  delete status;
+}
+
+void xse_engine_destroy(xse_engine* engine) {
+  if (engine == nullptr) return;
+  {
+    DeviceGuard guard(engine->device);
+    cudaDeviceSynchronize();
+  }
+  xse_status_destroy(engine->default_status);
+  for (auto& ev : engine->profile_events) {
+    cudaEventDestroy(ev.first);
+    cudaEventDestroy(ev.second);
+  }
+  delete engine;
+}
+
+int xse_engine_set_profiling(xse_engine* engine, int32_t enable) {
+  if (engine == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null engine");
+  std::lock_guard<std::mutex> lock(engine->profile_mu);
+  engine->profiling = enable != 0;
+  engine->profile_used = 0;
+  return Ok();
+}
+
+int xse_engine_profile_read(xse_engine* engine, double* pool_ms,
+                            int64_t* executions) {
+  if (engine == nullptr || pool_ms == nullptr || executions == nullptr) {
+    return SetError(XSE_INVALID_ARGUMENT, "arguments must be non-null");
+  }
+  DeviceGuard guard(engine->device);
+  std::lock_guard<std::mutex> lock(engine->profile_mu);
+  double total = 0.0;
+  for (size_t k = 0; k < engine->profile_used; ++k) {
+    const auto& ev = engine->profile_events[k];
+    cudaError_t e = cudaEventSynchronize(ev.second);
+    if (e != cudaSuccess) return CudaError(e, "profile event");
+    float ms = 0.0f;
+    e = cudaEventElapsedTime(&ms, ev.first, ev.second);
+    if (e != cudaSuccess) return CudaError(e, "profile elapsed time");
+    total += ms;
+  }
+  *pool_ms = total;
+  *executions = static_cast<int64_t>(engine->profile_used);
+  engine->profile_used = 0;
+  return Ok();
+}
+
+int xse_engine_add_table(xse_engine* engine, const xse_table_desc* desc) {
+  if (engine == nullptr || desc == nullptr) {
+    return SetError(XSE_INVALID_ARGUMENT, "engine and table must be non-null");
+  }
+  if (desc->name == nullptr || desc->name[0] == '\0') {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Embedding table name cannot be empty.");
+  }
+  if (desc->dtype < XSE_DT_F32 || desc->dtype > XSE_DT_I8_ROWWISE) {
+    return SetError(XSE_INVALID_ARGUMENT, "Unsupported data type: %d",
+                    desc->dtype);
+  }
+  if (desc->combine < XSE_COMBINE_SUM || desc->combine > XSE_COMBINE_SQRTN) {
+    return SetError(XSE_INVALID_ARGUMENT, "Unknown combine mode for table: %s",
+                    desc->name);
+  }
+  if (desc->vocab <= 0 || desc->dim <= 0) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Table dimensions must be strictly positive. Got "
+                    "vocab_size: %" PRId64 ", embedding_dim: %d",
+                    desc->vocab, desc->dim);
+  }
+  int64_t row_begin = desc->row_begin, row_end = desc->row_end;
+  if (row_begin == 0 && row_end == 0) row_end = desc->vocab;
+  if (row_begin < 0 || row_end > desc->vocab || row_end < row_begin) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Shard window [%" PRId64 ", %" PRId64
+                    ") is outside the table's %" PRId64 " rows.",
+                    row_begin, row_end, desc->vocab);
+  }
+  const int64_t rows = row_end - row_begin;
+  if (rows > 0 && desc->rows == nullptr) {
+    return SetError(XSE_INVALID_ARGUMENT, "Table rows must be non-null.");
+  }
+  if (desc->dtype == XSE_DT_I8_ROWWISE && rows > 0 &&
+      (desc->scale == nullptr || desc->bias == nullptr)) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Int8 row-wise tables need per-row scale and bias.");
+  }
+  {
+    std::lock_guard<std::mutex> lock(engine->tables_mu);
+    if (engine->tables.count(desc->name)) {
+      return SetError(XSE_ALREADY_EXISTS, "Table already exists: %s",
+                      desc->name);
+    }
+  }
+  DeviceGuard guard(engine->device);
+  auto t = std::make_shared<Table>();
+  t->name = desc->name;
+  t->dtype = desc->dtype;
+  t->combine = desc->combine;
+  t->dim = desc->dim;
+  t->vocab = desc->vocab;
+  t->row_begin = row_begin;
+  t->row_end = row_end;
+  t->device = engine->device;
+  const size_t bytes =
+      static_cast<size_t>(rows) * desc->dim * ElemBytes(desc->dtype);
+  cudaError_t e = cudaSuccess;
+  if (desc->placement == XSE_PLACE_ADOPT_DEVICE) {
+    t->rows = const_cast<void*>(desc->rows);
+  } else if (bytes > 0) {
+    e = cudaMalloc(&t->rows, bytes);
+    if (e != cudaSuccess) return CudaError(e, "table allocation");
+    t->owns_rows = true;
+    e = cudaMemcpy(t->rows, desc->rows, bytes,
+                   desc->placement == XSE_PLACE_COPY_FROM_HOST
+                       ? cudaMemcpyHostToDevice
+                       : cudaMemcpyDeviceToDevice);
+    if (e != cudaSuccess) return CudaError(e, "table upload");
+  }
+  if (desc->dtype == XSE_DT_I8_ROWWISE && rows > 0) {
+    e = cudaMalloc(&t->scale_bias, sizeof(float2) * rows);
+    if (e != cudaSuccess) return CudaError(e, "scale/bias allocation");
+    if (desc->placement == XSE_PLACE_COPY_FROM_HOST) {
+      std::vector<float2> sb(static_cast<size_t>(rows));
+      for (int64_t r = 0; r < rows; ++r) {
+        sb[r] = make_float2(desc->scale[r], desc->bias[r]);
+      }
+      e = cudaMemcpy(t->scale_bias, sb.data(), sizeof(float2) * rows,
+                     cudaMemcpyHostToDevice);
+    } else {
+      e = xse::LaunchInterleaveScaleBias(desc->scale, desc->bias,
+                                         t->scale_bias, rows, nullptr);
+      if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    }
+    if (e != cudaSuccess) return CudaError(e, "scale/bias upload");
+  }
+  std::lock_guard<std::mutex> lock(engine->tables_mu);
+  auto [it, inserted] = engine->tables.emplace(t->name, t);
+  if (!inserted) {
+    return SetError(XSE_ALREADY_EXISTS, "Table already exists: %s",
+                    desc->name);
+  }
+  return Ok();
+}
+
+int xse_engine_register_feature(xse_engine* engine, const char* feature,
+                                const char* table,
+                                int32_t max_sequence_length) {
+  if (engine == nullptr || feature == nullptr || table == nullptr) {
+    return SetError(XSE_INVALID_ARGUMENT, "arguments must be non-null");
+  }
+  std::lock_guard<std::mutex> lock(engine->specs_mu);
+  auto [it, inserted] = engine->features.emplace(
+      feature, Feature{table, max_sequence_length});
+  if (!inserted) {
+    return SetError(XSE_ALREADY_EXISTS, "Feature spec already registered: %s",
+                    feature);
+  }
+  return Ok();
+}
+
+int xse_engine_clear(xse_engine* engine) {
+  if (engine == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null engine");
+  std::lock_guard<std::mutex> spec_lock(engine->specs_mu);
+  std::lock_guard<std::mutex> table_lock(engine->tables_mu);
+  engine->features.clear();
+  engine->tables.clear();
+  return Ok();
+}
+
+int xse_engine_table_info(xse_engine* engine, const char* table,
+                          xse_table_info* out) {
+  if (engine == nullptr || table == nullptr || out == nullptr) {
+    return SetError(XSE_INVALID_ARGUMENT, "arguments must be non-null");
+  }
+  std::lock_guard<std::mutex> lock(engine->tables_mu);
+  auto it = engine->tables.find(table);
+  if (it == engine->tables.end()) {
+    return SetError(XSE_NOT_FOUND, "Table not found for table: %s", table);
+  }
+  const Table& t = *it->second;
+  out->dtype = t.dtype;
+  out->combine = t.combine;
+  out->dim = t.dim;
+  out->reserved = 0;
+  out->vocab = t.vocab;
+  out->row_begin = t.row_begin;
+  out->row_end = t.row_end;
+  out->rows = t.rows;
+  return Ok();
+}
+
+int xse_engine_feature_table(xse_engine* engine, const char* feature,
+                             char* buf, int32_t buflen,
+                             int32_t* max_sequence_length) {
+  if (engine == nullptr || feature == nullptr) {
+    return SetError(XSE_INVALID_ARGUMENT, "arguments must be non-null");
+  }
+  std::lock_guard<std::mutex> lock(engine->specs_mu);
+  auto it = engine->features.find(feature);
+  if (it == engine->features.end()) {
+    return SetError(XSE_NOT_FOUND, "Feature spec not found for feature: %s",
+                    feature);
+  }
+  if (buf != nullptr && buflen > 0) {
+    snprintf(buf, static_cast<size_t>(buflen), "%s", it->second.table.c_str());
+  }
+  if (max_sequence_length != nullptr) {
+    *max_sequence_length = it->second.max_sequence_length;
+  }
+  return Ok();
+}
+
+int xse_status_create(int32_t max_requests, xse_status** out) {
+  if (out == nullptr || max_requests <= 0) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "max_requests must be positive and out non-null");
+  }
+  int device = 0;
+  cudaGetDevice(&device);
+  const int code = CreateStatus(device, max_requests, out);
+  return code == XSE_OK ? Ok() : code;
+}
+
+int xse_engine_execute_batch(xse_engine* engine, const xse_bag_request* reqs,
+                             int32_t n, void* stream, int32_t flags,
+                             xse_status* status) {
+  if (engine == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null engine");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (status != nullptr) {
+    return ExecuteBatch(engine, reqs, n, s, flags, status);
+  }
+  if ((flags & XSE_EXEC_ASYNC) != 0) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Asynchronous execution needs a caller-owned status.");
+  }
+  std::lock_guard<std::mutex> lock(engine->default_status_mu);
+  return ExecuteBatch(engine, reqs, n, s, flags, engine->default_status);
+}
+
+int xse_status_wait(xse_status* status, void* stream) {
+  if (status == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null status");
+  DeviceGuard guard(status->device);
+  if (status->pending) {
+    const cudaError_t e =
+        cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    status->pending = false;
+    if (e != cudaSuccess) return CudaError(e, "stream synchronize");
+  }
+  return ResolveStatus(status);
+}
+
+int xse_dot_interaction(const float* dense, const float* pooled,
+                        int64_t batch, int32_t num_tables, int32_t dim,
+                        float* out, void* stream) {
+  g_last_launches = 0;
+  if (batch < 0 || num_tables < 1 || dim < 1) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Interaction needs batch >= 0, at least one table and a "
+                    "positive dimension.");
+  }
+  if (batch > 0 && (dense == nullptr || pooled == nullptr || out == nullptr)) {
+    return SetError(XSE_INVALID_ARGUMENT, "Interaction buffers must be non-null.");
+  }
+  const cudaError_t e = xse::LaunchDotInteraction(
+      dense, pooled, batch, num_tables, dim, out,
+      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return CudaError(e, "interaction launch");
+  g_last_launches = batch > 0 ? 1 : 0;
+  return Ok();
+}
+
+int xse_synth_table(void* rows, float* scale, float* bias, int32_t dtype,
+                    uint64_t seed, uint64_t table, int64_t row0,
+                    int64_t nrows, int32_t dim, void* stream) {
+  if (dtype < XSE_DT_F32 || dtype > XSE_DT_I8_ROWWISE || nrows < 0 ||
+      dim <= 0 || row0 < 0 || (nrows > 0 && rows == nullptr) ||
+      (dtype == XSE_DT_I8_ROWWISE && nrows > 0 &&
+       (scale == nullptr || bias == nullptr))) {
+    return SetError(XSE_INVALID_ARGUMENT, "invalid synthetic table request");
+  }
+  const int rc = xse_synth_table_impl(rows, scale, bias, dtype, seed, table,
+                                      row0, nrows, dim,
+                                      static_cast<cudaStream_t>(stream));
+  return rc == 0 ? Ok() : SetError(rc, "synthetic table launch failed");
+}
+
+int xse_synth_lengths(int64_t* lengths, int64_t n, int32_t lo, int32_t hi,
+                      uint64_t seed, uint64_t table, void* stream) {
+  if (n < 0 || lo < 0 || hi < lo || (n > 0 && lengths == nullptr)) {
+    return SetError(XSE_INVALID_ARGUMENT, "invalid synthetic lengths request");
+  }
+  const int rc = xse_synth_lengths_impl(lengths, n, lo, hi, seed, table,
+                                        static_cast<cudaStream_t>(stream));
+  return rc == 0 ? Ok() : SetError(rc, "synthetic lengths launch failed");
+}
+
+int xse_synth_ids(int64_t* ids, int64_t n, int64_t vocab, double zipf_alpha,
+                  uint64_t perm_mul, uint64_t perm_add, uint64_t seed,
+                  uint64_t table, int64_t index0, void* stream) {
+  if (n < 0 || vocab <= 0 || vocab >= (1ll << 31) ||
+      perm_mul >= (1ull << 32) || perm_add >= (1ull << 32) ||
+      (n > 0 && ids == nullptr) || index0 < 0) {
+    return SetError(XSE_INVALID_ARGUMENT, "invalid synthetic ids request");
+  }
+  const int rc = xse_synth_ids_impl(ids, n, vocab, zipf_alpha, perm_mul,
+                                    perm_add, seed, table, index0,
+                                    static_cast<cudaStream_t>(stream));
+  return rc == 0 ? Ok() : SetError(rc, "synthetic ids launch failed");
+}
+
+int xse_synth_weights(float* weights, int64_t n, uint64_t seed,
+                      uint64_t table, int64_t index0, void* stream) {
+  if (n < 0 || (n > 0 && weights == nullptr) || index0 < 0) {
+    return SetError(XSE_INVALID_ARGUMENT, "invalid synthetic weights request");
+  }
+  const int rc = xse_synth_weights_impl(weights, n, seed, table, index0,
+                                        static_cast<cudaStream_t>(stream));
+  return rc == 0 ? Ok() : SetError(rc, "synthetic weights launch failed");
+}
+
+}  // extern "C"

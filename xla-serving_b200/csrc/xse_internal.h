@@ -1,0 +1,96 @@
+// Internal declarations shared by the CUDA sources of the engine.
+#ifndef XSE_INTERNAL_H_
+#define XSE_INTERNAL_H_
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace xse {
+
+// Descriptors passed by value in one launch (kernel parameter space holds up
+// to 32 KB on sm_70+ with CUDA 12.1+).
+constexpr int kMaxDescsPerLaunch = 64;
+
+// One pooling request as the kernels see it.
+struct BagDesc {
+  const void* rows;           // table rows of the shard window, row-major
+  const float2* scale_bias;   // int8 rows: (scale, bias) per window row
+  const void* ids;            // int32 or int64
+  const void* offsets;        // int32 or int64, num_bags + 1 entries
+  const float* weights;       // nullptr when unweighted
+  float* out;                 // bag b at out + b * out_stride
+  int64_t out_stride;
+  int64_t vocab;              // global rows; valid ids are [0, vocab)
+  int64_t row_begin;          // shard window [row_begin, row_end)
+  int64_t row_end;
+  int64_t num_ids;
+  int64_t num_weights;
+  int64_t num_bags;
+  int64_t task_begin;         // first global task (bag) of this descriptor
+  int64_t work_begin;         // first validation work item of this descriptor
+  int32_t dim;
+  int32_t slot;               // request index into the status block
+  int8_t combine;             // 1 sum, 2 mean, 3 sqrtn
+  int8_t ids64;
+  int8_t offs64;
+  int8_t vec_out;             // output rows 16-byte aligned
+};
+
+// Per-request error record written by the device.
+enum : unsigned int {
+  kErrBadOffsets = 1u,         // first offset negative or offsets decreasing
+  kErrLastExceedsIds = 2u,     // final offset > number of ids
+  kErrLastExceedsWeights = 4u, // final offset > number of weights
+  kErrBadId = 8u,              // some id outside [0, vocab)
+};
+
+struct DevRequestStatus {
+  unsigned int flags;
+  unsigned int reserved;
+  // Bitwise complement of the smallest failing id position (0 = none), so
+  // that a zeroed block starts empty and atomicMax keeps the minimum.
+  unsigned long long inv_min_bad_index;
+};
+
+struct DevStatus {
+  unsigned int group_error;  // nonzero once any request failed validation
+  unsigned int reserved[3];
+  DevRequestStatus req[1];   // capacity set at allocation
+};
+
+inline size_t DevStatusBytes(int capacity) {
+  return sizeof(DevStatus) + sizeof(DevRequestStatus) * (capacity - 1);
+}
+
+struct PoolParams {
+  int32_t n;
+  int32_t fused_checks;   // 1: record errors here; 0: a validation pass ran
+  int64_t total_tasks;
+  DevStatus* status;
+  BagDesc d[kMaxDescsPerLaunch];
+};
+
+// Row layout class of a launch: G lanes per row, V 16-byte vectors per lane.
+// V == 0 selects the element-wise kernel (dims that are not whole vectors).
+struct Layout {
+  int dtype;
+  int g;
+  int v;
+};
+
+Layout ChooseLayout(int dtype, int dim, const void* rows);
+
+cudaError_t LaunchValidate(const PoolParams& p, int64_t total_work,
+                           cudaStream_t stream);
+cudaError_t LaunchPool(const Layout& layout, const PoolParams& p,
+                       cudaStream_t stream, int* launches);
+cudaError_t LaunchInterleaveScaleBias(const float* scale, const float* bias,
+                                      float2* out, int64_t n,
+                                      cudaStream_t stream);
+cudaError_t LaunchDotInteraction(const float* dense, const float* pooled,
+                                 int64_t batch, int num_tables, int dim,
+                                 float* out, cudaStream_t stream);
+
+}  // namespace xse
+
+#endif  // XSE_INTERNAL_H_
