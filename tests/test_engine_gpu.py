@@ -167,6 +167,15 @@ def test_strided_output_and_mixed_group(xse):
   got = pooled.cpu().numpy()
   for k in range(len(specs)):
     assert_bitwise(got[:, k, :], want[k], f"table {k}")
+  # Interleaved column blocks are disjoint; overlapping ones are rejected
+  # before anything is written.
+  before = pooled.clone()
+  reqs[3].output = pooled[:, 2, 64:].contiguous()  # separate buffer: fine
+  reqs[3].output = pooled.view(batch, -1)[:, 2 * 128 + 64:]
+  with pytest.raises(xse.XseError) as e:
+    eng.execute_batch(reqs)
+  assert e.value.message == "FP32 embedding-bag request outputs 2 and 3 overlap."
+  assert torch.equal(pooled, before)
   eng.close()
 
 

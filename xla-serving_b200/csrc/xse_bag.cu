@@ -8,12 +8,24 @@
 // bags at once). Each lane owns V 16-byte column vectors of a row, so a row
 // gather is G*V independent 16-byte loads. The ids (and weights) of a bag are
 // loaded G at a time, one per lane, and broadcast through the group with
-// shuffles; U rows are loaded before any of them is added, which keeps
-// U*V loads in flight per lane while the adds still run in CSR order. Every
-// element is accumulated in fp32 in exactly the reference's order
+// shuffles; U rows are loaded before any of them is added, which keeps U*V
+// loads in flight per lane while the adds still run in CSR order.
+//
+// Random 256-byte row gathers reach the HBM copy bandwidth only with about 32
+// resident warps per SM and several rows in flight per lane, and the pooling
+// work around each gathered vector must stay small enough that instruction
+// issue does not become the limit. So the per-row state held across a batch
+// is only the loaded data, the kernels are bounded to four 256-thread blocks
+// per SM, layouts whose rows are exactly G*V vectors drop per-lane bounds
+// checks at compile time, and the fp32 arithmetic runs on packed pairs
+// (sm_100 add/mul.rn.f32x2: two independently rounded IEEE operations in one
+// instruction).
+//
+// Every element is accumulated in fp32 in exactly the reference's order
 // (out = 0; out += row or out += w*row, one separately rounded multiply and
-// add), so fp32 results are bit-identical to the reference semantics; mean and
-// sqrt-n scales are applied as one multiply by a correctly rounded reciprocal.
+// add), so fp32 results are bit-identical to the reference semantics; mean
+// and sqrt-n scales are applied as one multiply by a correctly rounded
+// reciprocal.
 //
 // HBM traffic per id: one row (dim * elem bytes) + the id (4/8 B) + the weight
 // if any; per bag: one offset and the fp32 output row.
@@ -27,6 +39,7 @@ namespace xse {
 namespace {
 
 constexpr int kThreads = 256;
+using u64 = unsigned long long;
 
 template <int DT>
 struct ElemsPerVec;
@@ -42,6 +55,58 @@ template <>
 struct ElemsPerVec<2> {
   static constexpr int value = 16;  // int8
 };
+
+// Tuning: rows in flight per lane for fp32/bf16 rows (int8 rows, whose
+// dequantized vectors need four times the registers, use half), and the
+// resident 256-thread blocks per SM the register budget is sized for.
+#ifndef XSE_POOL_ROWS
+#define XSE_POOL_ROWS 4
+#endif
+#ifndef XSE_POOL_MIN_BLOCKS
+#define XSE_POOL_MIN_BLOCKS 4
+#endif
+
+// Rows gathered per batch (in flight per lane, times V vectors each).
+template <int DT, int V>
+struct RowsInFlight {
+  static constexpr int base = DT == 2 ? XSE_POOL_ROWS / 2 : XSE_POOL_ROWS;
+  static constexpr int value = V >= base ? 1 : base / V;
+};
+
+// Resident blocks per SM each variant's register budget is sized for.
+template <int DT, int V>
+struct MinBlocks {
+  static constexpr int value =
+      ElemsPerVec<DT>::value * V <= 16 && RowsInFlight<DT, V>::value * V <= 8
+          ? XSE_POOL_MIN_BLOCKS
+          : 2;
+};
+
+// ---- packed fp32 pairs (low word = first element) ------------------------
+__device__ __forceinline__ u64 PackBits(uint32_t lo, uint32_t hi) {
+  u64 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ u64 PackF(float lo, float hi) {
+  return PackBits(__float_as_uint(lo), __float_as_uint(hi));
+}
+__device__ __forceinline__ float LoF(u64 v) {
+  return __uint_as_float(static_cast<uint32_t>(v));
+}
+__device__ __forceinline__ float HiF(u64 v) {
+  return __uint_as_float(static_cast<uint32_t>(v >> 32));
+}
+__device__ __forceinline__ u64 Add2(u64 a, u64 b) {
+  u64 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ u64 Mul2(u64 a, u64 b) {
+  u64 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 
 __device__ __forceinline__ int64_t LoadIndex(const void* base, int is64,
                                              int64_t i) {
@@ -59,39 +124,55 @@ __device__ __forceinline__ uint4 LoadRowVec(const uint4* p) {
   return r;
 }
 
-__device__ __forceinline__ float Bf16Lo(uint32_t w) {
-  return __uint_as_float(w << 16);
-}
-__device__ __forceinline__ float Bf16Hi(uint32_t w) {
-  return __uint_as_float(w & 0xffff0000u);
-}
 __device__ __forceinline__ float I8At(uint32_t w, int k) {
   // Sign-extend byte k of w.
   return __int2float_rn(static_cast<int>(w << (24 - 8 * k)) >> 24);
 }
 
-// Unpacks one 16-byte vector into EPV fp32 values (int8 rows dequantized as
-// float(q)*scale + bias, each step rounded separately).
+// Products are scalar mul.rn.f32, which PTX never contracts into an FMA; a
+// packed mul.rn.f32x2 feeding a packed add can be fused by the assembler,
+// which would round once instead of twice and break bit parity.
+__device__ __forceinline__ u64 MulPair(float a, float lo, float hi) {
+  return PackF(__fmul_rn(a, lo), __fmul_rn(a, hi));
+}
+
+// One 16-byte row vector as fp32 pairs: int8 rows dequantized as
+// float(q)*scale + bias, each step rounded separately.
 template <int DT>
-__device__ __forceinline__ void Unpack(const uint4& r, float2 sb,
-                                       float (&x)[ElemsPerVec<DT>::value]) {
+__device__ __forceinline__ void UnpackPairs(
+    const uint4& r, float scale, u64 b2,
+    u64 (&x)[ElemsPerVec<DT>::value / 2]) {
   const uint32_t w[4] = {r.x, r.y, r.z, r.w};
   if constexpr (DT == 0) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) x[k] = __uint_as_float(w[k]);
+    x[0] = PackBits(w[0], w[1]);
+    x[1] = PackBits(w[2], w[3]);
   } else if constexpr (DT == 1) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      x[2 * k] = Bf16Lo(w[k]);
-      x[2 * k + 1] = Bf16Hi(w[k]);
-    }
+    for (int k = 0; k < 4; ++k) x[k] = PackBits(w[k] << 16, w[k] & 0xffff0000u);
   } else {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
+      x[2 * k] = Add2(MulPair(scale, I8At(w[k], 0), I8At(w[k], 1)), b2);
+      x[2 * k + 1] = Add2(MulPair(scale, I8At(w[k], 2), I8At(w[k], 3)), b2);
+    }
+  }
+}
+
+// acc += row (or acc += w*row), element by element in fp32.
+template <int DT, int V>
+__device__ __forceinline__ void AddRow(
+    u64 (&acc)[V][ElemsPerVec<DT>::value / 2], const uint4 (&raw)[V],
+    float scale, u64 b2, bool weighted, float w) {
+  constexpr int PPV = ElemsPerVec<DT>::value / 2;
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        x[4 * k + b] = __fadd_rn(__fmul_rn(I8At(w[k], b), sb.x), sb.y);
-      }
+  for (int v = 0; v < V; ++v) {
+    u64 x[PPV];
+    UnpackPairs<DT>(raw[v], scale, b2, x);
+#pragma unroll
+    for (int k = 0; k < PPV; ++k) {
+      acc[v][k] = weighted
+                      ? Add2(acc[v][k], MulPair(w, LoF(x[k]), HiF(x[k])))
+                      : Add2(acc[v][k], x[k]);
     }
   }
 }
@@ -145,11 +226,227 @@ __device__ __forceinline__ bool BagRange(const PoolParams& p,
   return !bad;
 }
 
-template <int DT, int G, int V>
-__global__ void __launch_bounds__(kThreads)
+// Stages one chunk of ids: lane gl takes position pos (if below end) and
+// returns its row within the shard window, or -1 when the id contributes
+// nothing (invalid -- an error -- or another shard's row).
+__device__ __forceinline__ int StageRow(const PoolParams& p, const BagDesc& d,
+                                        int64_t id, int64_t pos, bool live) {
+  if (!live) return -1;
+  if (id < 0 || id >= d.vocab) {
+    if (p.fused_checks) RecordBadId(p.status, d.slot, pos);
+    return -1;
+  }
+  if (id < d.row_begin || id >= d.row_end) return -1;
+  return static_cast<int>(id - d.row_begin);
+}
+
+// How a bag's weights enter the pool; fixed per bag so the row loops carry no
+// weighting branches. Only weighted means and sqrt-n need the weight sum.
+// Each kernel is compiled for one mode: a kernel that branches between modes
+// per bag keeps the union of their registers live and spills.
+enum WeightMode : int {
+  kUnweighted = 0,
+  kWeightedSum = 1,   // weighted sum: no weight total needed
+  kWeightedNorm = 2,  // weighted mean (sum of w) or sqrt-n (sum of w*w)
+};
+
+template <int WM>
+__device__ __forceinline__ void AddWeight(float* wsum, float w, int combine) {
+  if constexpr (WM == kWeightedNorm) {
+    *wsum = __fadd_rn(*wsum, combine == 3 ? __fmul_rn(w, w) : w);
+  }
+}
+
+// Adds raw row u to acc (dequantizing int8 rows with their scale/bias).
+template <int DT, int V, int WM>
+__device__ __forceinline__ void AddGathered(
+    u64 (&acc)[V][ElemsPerVec<DT>::value / 2], const uint4 (&raw)[V],
+    float2 sb, float w) {
+  float scale = 0.0f;
+  u64 b2 = 0;
+  if constexpr (DT == 2) {
+    scale = sb.x;
+    b2 = PackF(sb.y, sb.y);
+  }
+  AddRow<DT, V>(acc, raw, scale, b2, WM != kUnweighted, w);
+}
+
+// Full batch of U rows of a chunk whose ids all contribute: no per-row
+// checks. Lanes past the end of a non-exact row add zeros to accumulator
+// lanes that are never stored.
+template <int DT, int G, int V, bool EXACT, int WM, typename Hook>
+__device__ __forceinline__ void FullBatch(
+    const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
+    int my_row, float my_w, int j0,
+    u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, Hook&& hook) {
+  constexpr int U = RowsInFlight<DT, V>::value;
+  const int stride = EXACT ? G * V : row_vecs;
+  uint4 raw[U][V];
+  float2 sb[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int r = __shfl_sync(gmask, my_row, j0 + u, G);
+    if constexpr (DT == 2) sb[u] = __ldg(d.scale_bias + r);
+    const uint4* src = rows + static_cast<int64_t>(r) * stride;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      if (EXACT || gl + v * G < row_vecs) {
+        raw[u][v] = LoadRowVec(src + v * G);
+      } else {
+        raw[u][v] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+  hook();  // runs while this batch's rows are in flight
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    float w = 1.0f;
+    if constexpr (WM != kUnweighted) {
+      w = __shfl_sync(gmask, my_w, j0 + u, G);
+      AddWeight<WM>(wsum, w, d.combine);
+    }
+    AddGathered<DT, V, WM>(acc, raw[u], DT == 2 ? sb[u] : make_float2(0, 0),
+                           w);
+  }
+}
+
+// General batch: up to U rows (positions j0..j0+n-1 of the chunk), skipping
+// ids that contribute nothing.
+template <int DT, int G, int V, bool EXACT, int WM, typename Hook>
+__device__ __forceinline__ void GatherBatch(
+    const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
+    int my_row, float my_w, int j0, int n,
+    u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, Hook&& hook) {
+  constexpr int U = RowsInFlight<DT, V>::value;
+  const int stride = EXACT ? G * V : row_vecs;
+  uint4 raw[U][V];
+  float2 sb[U];
+  unsigned int present = 0;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int j = u < n ? j0 + u : j0;
+    const int r = __shfl_sync(gmask, my_row, j, G);
+    const bool use = u < n && r >= 0;
+    present |= use ? (1u << u) : 0u;
+    if constexpr (DT == 2) {
+      sb[u] = use ? __ldg(d.scale_bias + r) : make_float2(0.0f, 0.0f);
+    }
+    const uint4* src = rows + static_cast<int64_t>(r) * stride;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      if (use) {
+        if (EXACT || gl + v * G < row_vecs) {
+          raw[u][v] = LoadRowVec(src + v * G);
+        } else {
+          raw[u][v] = make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
+  }
+  hook();  // runs while this batch's rows are in flight
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (u < n) {
+      float w = 1.0f;
+      if constexpr (WM != kUnweighted) {
+        w = __shfl_sync(gmask, my_w, j0 + u, G);
+        AddWeight<WM>(wsum, w, d.combine);
+      }
+      if (present & (1u << u)) {
+        AddGathered<DT, V, WM>(acc, raw[u],
+                               DT == 2 ? sb[u] : make_float2(0, 0), w);
+      }
+    }
+  }
+}
+
+// Scales (mean / sqrt-n) and stores one finished bag, then clears the
+// accumulator for the next one.
+template <int DT, int G, int V, bool EXACT>
+__device__ __forceinline__ void FinishBag(
+    const BagDesc& d, int64_t bag, int64_t n, bool weighted,
+    u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, int gl,
+    int row_vecs) {
+  constexpr int PPV = ElemsPerVec<DT>::value / 2;
+  if (n > 0 && d.combine != 1) {
+    const float s = BagScale(d.combine, weighted, n, *wsum);
+    const u64 s2 = PackF(s, s);
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+#pragma unroll
+      for (int k = 0; k < PPV; ++k) acc[v][k] = Mul2(acc[v][k], s2);
+  }
+  float* out = d.out + bag * d.out_stride;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int k = gl + v * G;
+    if (EXACT || k < row_vecs) {
+      float* o = out + k * (2 * PPV);
+      if (d.vec_out) {
+#pragma unroll
+        for (int e = 0; e < PPV; e += 2) {
+          *reinterpret_cast<ulonglong2*>(o + 2 * e) =
+              make_ulonglong2(acc[v][e], acc[v][e + 1]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < PPV; ++e) {
+          o[2 * e] = LoF(acc[v][e]);
+          o[2 * e + 1] = HiF(acc[v][e]);
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < PPV; ++e) acc[v][e] = 0;
+  }
+  *wsum = 0.0f;
+}
+
+// Checks a bag's offsets; returns false (recording the error in fused mode)
+// when the bag must be skipped.
+__device__ __forceinline__ bool CheckBag(const PoolParams& p, const BagDesc& d,
+                                         int64_t begin, int64_t end) {
+  const bool weights_short = d.weights != nullptr && end > d.num_weights;
+  const bool bad = begin < 0 || end < begin || end > d.num_ids || weights_short;
+  if (bad && p.fused_checks) {
+    unsigned int f = 0;
+    if (begin < 0 || end < begin) f |= kErrBadOffsets;
+    if (end > d.num_ids) f |= kErrLastExceedsIds;
+    if (weights_short) f |= kErrLastExceedsWeights;
+    RecordError(p.status, d.slot, f);
+  }
+  return !bad;
+}
+
+__device__ __forceinline__ bool SafeBag(const BagDesc& d, int64_t begin,
+                                        int64_t end) {
+  return begin >= 0 && end >= begin && end <= d.num_ids &&
+         (d.weights == nullptr || end <= d.num_weights);
+}
+
+// Loads the id (and weight) at position pos + gl of a bag ending at end.
+template <int WM>
+__device__ __forceinline__ void LoadChunk(const BagDesc& d, int64_t pos,
+                                          int64_t end, int gl, int64_t* id,
+                                          float* w) {
+  if (pos + gl < end) {
+    *id = LoadIndex(d.ids, d.ids64, pos + gl);
+    if constexpr (WM != kUnweighted) *w = __ldg(d.weights + pos + gl);
+  }
+}
+
+// One bag per lane-group task. Every descriptor of a launch has weighting
+// mode WM (the launcher groups requests by mode). A group pools its bags in
+// grid-stride order with one bag of lookahead: the next bag's offsets are
+// loaded when the current bag starts, and the next id chunk -- of this bag,
+// or the first of the next bag -- is loaded while the current chunk's first
+// rows are in flight, so a bag's dependent loads (offsets, then ids, then
+// rows) overlap the previous bag's row gathers.
+template <int DT, int G, int V, bool EXACT, int WM>
+__global__ void __launch_bounds__(kThreads, MinBlocks<DT, V>::value)
     PoolVecKernel(const __grid_constant__ PoolParams p) {
-  constexpr int EPV = ElemsPerVec<DT>::value;
-  constexpr int U = V >= 8 ? 1 : 8 / V;
+  constexpr int PPV = ElemsPerVec<DT>::value / 2;
+  constexpr int U = RowsInFlight<DT, V>::value;
   constexpr int kGroupsPerBlock = kThreads / G;
   if (!p.fused_checks && p.status->group_error != 0) return;
 
@@ -158,118 +455,90 @@ __global__ void __launch_bounds__(kThreads)
   const unsigned gmask =
       G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane - gl));
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kGroupsPerBlock;
-  int t = 0;
-  for (int64_t task = static_cast<int64_t>(blockIdx.x) * kGroupsPerBlock +
-                      threadIdx.x / G;
-       task < p.total_tasks; task += stride) {
-    t = AdvanceDesc(p, t, task);
+  int64_t task = static_cast<int64_t>(blockIdx.x) * kGroupsPerBlock +
+                 threadIdx.x / G;
+  if (task >= p.total_tasks) return;
+  int t = AdvanceDesc(p, 0, task);
+  int64_t begin, end;
+  {
+    const BagDesc& d = p.d[t];
+    begin = LoadIndex(d.offsets, d.offs64, task - d.task_begin);
+    end = LoadIndex(d.offsets, d.offs64, task - d.task_begin + 1);
+  }
+  bool have_chunk = false;  // cid/cw hold the current bag's first chunk
+  int64_t cid = 0;
+  float cw = 1.0f;
+  for (;;) {
     const BagDesc& d = p.d[t];
     const int64_t bag = task - d.task_begin;
-    int64_t begin, end;
-    if (!BagRange(p, d, bag, &begin, &end)) continue;
-
-    const int row_vecs = d.dim / EPV;  // 16-byte vectors per row
-    const bool weighted = d.weights != nullptr;
-    const uint4* rows = static_cast<const uint4*>(d.rows);
-    float acc[V][EPV];
-#pragma unroll
-    for (int v = 0; v < V; ++v)
-#pragma unroll
-      for (int e = 0; e < EPV; ++e) acc[v][e] = 0.0f;
-    float wsum = 0.0f;
-
-    for (int64_t base = begin; base < end; base += G) {
-      const int cnt = static_cast<int>(end - base < G ? end - base : G);
-      // Stage G ids (and weights) of the bag, one per lane. -1 marks an id
-      // that contributes nothing (invalid, or outside this shard's window).
-      int64_t my_row = -1;
-      float my_w = 1.0f;
-      if (gl < cnt) {
-        const int64_t id = LoadIndex(d.ids, d.ids64, base + gl);
-        if (weighted) my_w = __ldg(d.weights + base + gl);
-        if (id < 0 || id >= d.vocab) {
-          if (p.fused_checks) RecordBadId(p.status, d.slot, base + gl);
-        } else if (id >= d.row_begin && id < d.row_end) {
-          my_row = id - d.row_begin;
-        }
-      }
-      for (int j0 = 0; j0 < cnt; j0 += U) {
-        uint4 raw[U][V];
-        float2 sb[U];
-        int64_t row[U];
-        float w[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int j = j0 + u < cnt ? j0 + u : cnt - 1;
-          row[u] = __shfl_sync(gmask, my_row, j, G);
-          w[u] = __shfl_sync(gmask, my_w, j, G);
-          if (j0 + u >= cnt) row[u] = -1;
-          sb[u] = make_float2(0.0f, 0.0f);
-          if constexpr (DT == 2) {
-            if (row[u] >= 0) sb[u] = __ldg(d.scale_bias + row[u]);
-          }
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            const int k = gl + v * G;
-            if (row[u] >= 0 && k < row_vecs) {
-              raw[u][v] = LoadRowVec(rows + row[u] * row_vecs + k);
-            } else {
-              raw[u][v] = make_uint4(0, 0, 0, 0);
-            }
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          if (j0 + u < cnt) {
-            if (weighted) {
-              wsum = __fadd_rn(wsum, d.combine == 3 ? __fmul_rn(w[u], w[u])
-                                                    : w[u]);
-            }
-            if (row[u] >= 0) {
-#pragma unroll
-              for (int v = 0; v < V; ++v) {
-                float x[EPV];
-                Unpack<DT>(raw[u][v], sb[u], x);
-#pragma unroll
-                for (int e = 0; e < EPV; ++e) {
-                  acc[v][e] = weighted
-                                  ? __fadd_rn(acc[v][e], __fmul_rn(w[u], x[e]))
-                                  : __fadd_rn(acc[v][e], x[e]);
-                }
-              }
-            }
-          }
-        }
-      }
+    // Lookahead: the next task's offsets, consumed one bag later.
+    const int64_t ntask = task + stride;
+    const bool has_next = ntask < p.total_tasks;
+    int nt = t;
+    int64_t nbegin = 0, nend = 0;
+    if (has_next) {
+      nt = AdvanceDesc(p, t, ntask);
+      const BagDesc& nd = p.d[nt];
+      nbegin = LoadIndex(nd.offsets, nd.offs64, ntask - nd.task_begin);
+      nend = LoadIndex(nd.offsets, nd.offs64, ntask - nd.task_begin + 1);
     }
-
-    const int64_t n = end - begin;
-    if (n > 0 && d.combine != 1) {
-      const float s = BagScale(d.combine, weighted, n, wsum);
+    bool next_chunk = false;
+    if (CheckBag(p, d, begin, end)) {
+      const int row_vecs = EXACT ? G * V : d.dim / ElemsPerVec<DT>::value;
+      const uint4* rows = static_cast<const uint4*>(d.rows) + gl;
+      u64 acc[V][PPV];
 #pragma unroll
       for (int v = 0; v < V; ++v)
 #pragma unroll
-        for (int e = 0; e < EPV; ++e) acc[v][e] = __fmul_rn(acc[v][e], s);
-    }
-    float* out = d.out + bag * d.out_stride;
-#pragma unroll
-    for (int v = 0; v < V; ++v) {
-      const int k = gl + v * G;
-      if (k < row_vecs) {
-        float* o = out + k * EPV;
-        if (d.vec_out) {
-#pragma unroll
-          for (int e = 0; e < EPV; e += 4) {
-            *reinterpret_cast<float4*>(o + e) =
-                make_float4(acc[v][e], acc[v][e + 1], acc[v][e + 2],
-                            acc[v][e + 3]);
+        for (int k = 0; k < PPV; ++k) acc[v][k] = 0;
+      float wsum = 0.0f;
+      if (!have_chunk) LoadChunk<WM>(d, begin, end, gl, &cid, &cw);
+      for (int64_t base = begin; base < end; base += G) {
+        const int cnt = static_cast<int>(end - base < G ? end - base : G);
+        const int64_t id = cid;
+        const float my_w = cw;
+        const bool last = base + G >= end;
+        // Issued after the chunk's first batch of rows: the next chunk of
+        // this bag, or the next bag's first chunk.
+        bool pending = true;
+        auto prefetch = [&]() {
+          if (!pending) return;
+          pending = false;
+          if (!last) {
+            LoadChunk<WM>(d, base + G, end, gl, &cid, &cw);
+          } else if (has_next) {
+            const BagDesc& nd = p.d[nt];
+            if (SafeBag(nd, nbegin, nend)) {
+              LoadChunk<WM>(nd, nbegin, nend, gl, &cid, &cw);
+              next_chunk = true;
+            }
           }
-        } else {
-#pragma unroll
-          for (int e = 0; e < EPV; ++e) o[e] = acc[v][e];
+        };
+        const int my_row = StageRow(p, d, id, base + gl, gl < cnt);
+        int j0 = 0;
+        if (__all_sync(gmask, gl >= cnt || my_row >= 0)) {
+          for (; j0 + U <= cnt; j0 += U) {
+            FullBatch<DT, G, V, EXACT, WM>(d, rows, row_vecs, gl, gmask,
+                                           my_row, my_w, j0, acc, &wsum,
+                                           prefetch);
+          }
+        }
+        for (; j0 < cnt; j0 += U) {
+          const int n = cnt - j0 < U ? cnt - j0 : U;
+          GatherBatch<DT, G, V, EXACT, WM>(d, rows, row_vecs, gl, gmask,
+                                           my_row, my_w, j0, n, acc, &wsum,
+                                           prefetch);
         }
       }
+      FinishBag<DT, G, V, EXACT>(d, bag, end - begin, WM != kUnweighted, acc,
+                                 &wsum, gl, row_vecs);
     }
+    if (!has_next) break;
+    task = ntask;
+    t = nt;
+    begin = nbegin;
+    end = nend;
+    have_chunk = next_chunk;
   }
 }
 
@@ -350,10 +619,13 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-// Group validation (ValidateEmbeddingBagInput, embedding_bag.cc:99-133):
-// one work item per offset and per id position. Offsets must start >= 0 and
-// never decrease; the final offset must not exceed the ids (or weights);
-// every id in [first, last) must be in [0, vocab).
+// Group validation (ValidateEmbeddingBagInput, embedding_bag.cc:99-133).
+// Offsets must start >= 0 and never decrease; the final offset must not
+// exceed the ids (or weights); every id in [first, last) must be in
+// [0, vocab). Work items are runs of kValidateRun consecutive offsets or
+// id positions of one request.
+constexpr int kValidateRun = 8;
+
 __global__ void __launch_bounds__(kThreads)
     ValidateKernel(const __grid_constant__ PoolParams p, int64_t total_work) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -362,28 +634,42 @@ __global__ void __launch_bounds__(kThreads)
        w < total_work; w += stride) {
     while (t + 1 < p.n && w >= p.d[t + 1].work_begin) ++t;
     const BagDesc& d = p.d[t];
-    const int64_t i = w - d.work_begin;
+    const int64_t item = w - d.work_begin;
     const int64_t num_offsets = d.num_bags + 1;
-    if (i < num_offsets) {
-      const int64_t cur = LoadIndex(d.offsets, d.offs64, i);
-      if (i == 0) {
-        if (cur < 0) RecordError(p.status, d.slot, kErrBadOffsets);
-      } else if (LoadIndex(d.offsets, d.offs64, i - 1) > cur) {
-        RecordError(p.status, d.slot, kErrBadOffsets);
+    const int64_t offset_runs = (num_offsets + kValidateRun - 1) / kValidateRun;
+    if (item < offset_runs) {
+      const int64_t i0 = item * kValidateRun;
+      const int64_t i1 = i0 + kValidateRun < num_offsets ? i0 + kValidateRun
+                                                         : num_offsets;
+      int64_t prev = i0 == 0 ? 0 : LoadIndex(d.offsets, d.offs64, i0 - 1);
+      bool bad = false;
+      int64_t cur = 0;
+      for (int64_t i = i0; i < i1; ++i) {
+        cur = LoadIndex(d.offsets, d.offs64, i);
+        bad |= i == 0 ? cur < 0 : cur < prev;
+        prev = cur;
       }
-      if (i == num_offsets - 1) {
+      if (bad) RecordError(p.status, d.slot, kErrBadOffsets);
+      if (i1 == num_offsets) {
         if (cur > d.num_ids) RecordError(p.status, d.slot, kErrLastExceedsIds);
         if (d.weights != nullptr && cur > d.num_weights) {
           RecordError(p.status, d.slot, kErrLastExceedsWeights);
         }
       }
     } else if (d.ids != nullptr) {
-      const int64_t pos = i - num_offsets;
       const int64_t first = LoadIndex(d.offsets, d.offs64, 0);
       const int64_t last = LoadIndex(d.offsets, d.offs64, d.num_bags);
-      if (pos >= first && pos < last) {
+      const int64_t p0 = (item - offset_runs) * kValidateRun;
+      int64_t lo = p0 > first ? p0 : first;
+      int64_t hi = p0 + kValidateRun;
+      if (hi > last) hi = last;
+      if (hi > d.num_ids) hi = d.num_ids;
+      for (int64_t pos = lo; pos < hi; ++pos) {
         const int64_t id = LoadIndex(d.ids, d.ids64, pos);
-        if (id < 0 || id >= d.vocab) RecordBadId(p.status, d.slot, pos);
+        if (id < 0 || id >= d.vocab) {
+          RecordBadId(p.status, d.slot, pos);
+          break;  // later positions of this run cannot be the minimum
+        }
       }
     }
   }
@@ -409,46 +695,83 @@ int SmCount() {
 }
 
 template <typename Kernel>
-int GridFor(Kernel kernel, int64_t groups_needed, int groups_per_block) {
+int BlocksPerSm(Kernel kernel) {
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0);
-  if (per_sm <= 0) per_sm = 1;
-  const int64_t max_grid = static_cast<int64_t>(SmCount()) * per_sm;
+  return per_sm > 0 ? per_sm : 1;
+}
+
+template <typename Kernel>
+int GridFor(Kernel kernel, int64_t groups_needed, int groups_per_block) {
+  const int64_t max_grid =
+      static_cast<int64_t>(SmCount()) * BlocksPerSm(kernel);
   const int64_t want = (groups_needed + groups_per_block - 1) / groups_per_block;
   return static_cast<int>(want < 1 ? 1 : (want < max_grid ? want : max_grid));
 }
 
-template <int DT, int G, int V>
-cudaError_t LaunchVec(const PoolParams& p, cudaStream_t stream) {
-  auto kernel = PoolVecKernel<DT, G, V>;
+// Numbers the tasks of every descriptor for runs of `runs` bags.
+void AssignTasks(PoolParams* p, int runs) {
+  int64_t tasks = 0;
+  for (int k = 0; k < p->n; ++k) {
+    p->d[k].task_begin = tasks;
+    tasks += (p->d[k].num_bags + runs - 1) / runs;
+  }
+  p->bags_per_task = runs;
+  p->total_tasks = tasks;
+}
+
+template <int DT, int G, int V, bool EXACT, int WM>
+cudaError_t LaunchVec(const PoolParams& in, cudaStream_t stream) {
+  PoolParams p = in;
+  AssignTasks(&p, 1);
+  auto kernel = PoolVecKernel<DT, G, V, EXACT, WM>;
   const int grid = GridFor(kernel, p.total_tasks, kThreads / G);
   kernel<<<grid, kThreads, 0, stream>>>(p);
   return cudaGetLastError();
+}
+
+template <int DT, int G, int V, bool EXACT>
+cudaError_t LaunchVecMode(const Layout& l, const PoolParams& p,
+                          cudaStream_t stream) {
+  switch (l.wmode) {
+    case kUnweighted: return LaunchVec<DT, G, V, EXACT, kUnweighted>(p, stream);
+    case kWeightedSum: return LaunchVec<DT, G, V, EXACT, kWeightedSum>(p, stream);
+    default: return LaunchVec<DT, G, V, EXACT, kWeightedNorm>(p, stream);
+  }
+}
+
+template <int DT, int G, int V>
+cudaError_t LaunchVecExact(const Layout& l, const PoolParams& p,
+                           cudaStream_t stream) {
+  return l.exact ? LaunchVecMode<DT, G, V, true>(l, p, stream)
+                 : LaunchVecMode<DT, G, V, false>(l, p, stream);
 }
 
 template <int DT>
 cudaError_t LaunchForDtype(const Layout& l, const PoolParams& p,
                            cudaStream_t stream) {
   if (l.v == 0) {
+    PoolParams q = p;
+    AssignTasks(&q, 1);
     auto kernel = PoolScalarKernel<DT>;
-    const int grid = GridFor(kernel, p.total_tasks, kThreads / 32);
-    kernel<<<grid, kThreads, 0, stream>>>(p);
+    const int grid = GridFor(kernel, q.total_tasks, kThreads / 32);
+    kernel<<<grid, kThreads, 0, stream>>>(q);
     return cudaGetLastError();
   }
   if (l.v == 1) {
     switch (l.g) {
-      case 4: return LaunchVec<DT, 4, 1>(p, stream);
-      case 8: return LaunchVec<DT, 8, 1>(p, stream);
-      case 16: return LaunchVec<DT, 16, 1>(p, stream);
-      default: return LaunchVec<DT, 32, 1>(p, stream);
+      case 4: return LaunchVecExact<DT, 4, 1>(l, p, stream);
+      case 8: return LaunchVecExact<DT, 8, 1>(l, p, stream);
+      case 16: return LaunchVecExact<DT, 16, 1>(l, p, stream);
+      default: return LaunchVecExact<DT, 32, 1>(l, p, stream);
     }
   }
-  if (l.v == 2) return LaunchVec<DT, 32, 2>(p, stream);
+  if (l.v == 2) return LaunchVecExact<DT, 32, 2>(l, p, stream);
   if constexpr (DT == 2) {
-    return LaunchVec<DT, 32, 4>(p, stream);
+    return LaunchVecExact<DT, 32, 4>(l, p, stream);
   } else {
-    if (l.v == 4) return LaunchVec<DT, 32, 4>(p, stream);
-    return LaunchVec<DT, 32, 8>(p, stream);
+    if (l.v == 4) return LaunchVecExact<DT, 32, 4>(l, p, stream);
+    return LaunchVecExact<DT, 32, 8>(l, p, stream);
   }
 }
 
@@ -458,18 +781,35 @@ Layout ChooseLayout(int dtype, int dim, const void* rows) {
   const int elem = dtype == 0 ? 4 : dtype == 1 ? 2 : 1;
   const int64_t row_bytes = static_cast<int64_t>(dim) * elem;
   const bool aligned = (reinterpret_cast<uintptr_t>(rows) & 15u) == 0;
-  if (!aligned || row_bytes % 16 != 0) return {dtype, 32, 0};
+  if (!aligned || row_bytes % 16 != 0) return {dtype, 32, 0, false};
   const int64_t vecs = row_bytes / 16;
   if (vecs <= 32) {
     int g = 4;
     while (g < vecs) g *= 2;
-    return {dtype, g, 1};
+    return {dtype, g, 1, g == vecs};
   }
   const int64_t per_lane = (vecs + 31) / 32;
-  if (per_lane <= 2) return {dtype, 32, 2};
-  if (per_lane <= 4) return {dtype, 32, 4};
-  if (per_lane <= 8 && dtype != 2) return {dtype, 32, 8};
-  return {dtype, 32, 0};
+  int v = 0;
+  if (per_lane <= 2) {
+    v = 2;
+  } else if (per_lane <= 4) {
+    v = 4;
+  } else if (per_lane <= 8 && dtype != 2) {
+    v = 8;
+  } else {
+    return {dtype, 32, 0, false};
+  }
+  return {dtype, 32, v, 32 * v == vecs};
+}
+
+int64_t TasksFor(const Layout& layout, int64_t num_bags) {
+  (void)layout;  // the launcher renumbers tasks for its kernel
+  return num_bags;
+}
+
+int64_t ValidationWork(int64_t num_bags, int64_t num_ids) {
+  return (num_bags + 1 + kValidateRun - 1) / kValidateRun +
+         (num_ids + kValidateRun - 1) / kValidateRun;
 }
 
 cudaError_t LaunchPool(const Layout& layout, const PoolParams& p,

@@ -187,17 +187,54 @@ int ResolveStatus(xse_status* st) {
   return Ok();
 }
 
+// A set of `count` byte intervals [base + k*stride, base + k*stride + width).
+// Contiguous buffers have count 1. Outputs may be strided (one table's
+// column block of an interleaved [batch, tables, dim] buffer), which the
+// reference's contiguous outputs never are.
 struct Range {
-  uintptr_t begin, end;
+  int64_t base, stride, width, count;
   int32_t request;
   const char* kind;
+  int64_t end() const { return base + (count - 1) * stride + width; }
 };
+
+int64_t FloorDiv(int64_t a, int64_t b) {
+  const int64_t q = a / b;
+  return (a % b != 0 && ((a < 0) != (b < 0))) ? q - 1 : q;
+}
+
+// Exact overlap test when both ranges share one stride (or either is a
+// single interval); a conservative hull test otherwise.
+bool Overlaps(const Range& a, const Range& b) {
+  if (a.count == 1 && b.count == 1) {
+    return a.base < b.base + b.width && b.base < a.base + a.width;
+  }
+  if (a.end() <= b.base || b.end() <= a.base) return false;
+  const Range& s = a.count >= b.count ? a : b;  // strided
+  const Range& o = a.count >= b.count ? b : a;
+  if (o.count == 1) {
+    // Rows k of s meet [o.base, o.base + o.width) iff
+    // o.base - width < s.base + k*stride < o.base + o.width.
+    const int64_t k_lo = FloorDiv(o.base - s.width - s.base, s.stride) + 1;
+    const int64_t k_hi =
+        -FloorDiv(-(o.base + o.width - s.base), s.stride) - 1;
+    return std::max<int64_t>(k_lo, 0) <= std::min<int64_t>(k_hi, s.count - 1);
+  }
+  if (a.stride != b.stride) return true;
+  // Rows k of a and j of b meet iff m = k - j satisfies
+  // d - a.width < m*stride < d + b.width with d = b.base - a.base.
+  const int64_t d = b.base - a.base;
+  const int64_t m_lo = FloorDiv(d - a.width, a.stride) + 1;
+  const int64_t m_hi = -FloorDiv(-(d + b.width), a.stride) - 1;
+  return std::max<int64_t>(m_lo, -(b.count - 1)) <=
+         std::min<int64_t>(m_hi, a.count - 1);
+}
 
 void AddRange(const void* p, int64_t bytes, int32_t request, const char* kind,
               std::vector<Range>* out) {
   if (p == nullptr || bytes <= 0) return;
-  const uintptr_t b = reinterpret_cast<uintptr_t>(p);
-  out->push_back({b, b + static_cast<uintptr_t>(bytes), request, kind});
+  out->push_back({static_cast<int64_t>(reinterpret_cast<uintptr_t>(p)), bytes,
+                  bytes, 1, request, kind});
 }
 
 // ValidateOutputIsolation (embedding_bag.cc:304-351) over device ranges.
@@ -210,9 +247,10 @@ int CheckIsolation(const xse_bag_request* reqs,
     const Table& t = *tables[i];
     const int64_t bags = r.num_offsets - 1;
     const int64_t stride = r.output_stride > 0 ? r.output_stride : t.dim;
-    if (bags > 0) {
-      AddRange(r.output, ((bags - 1) * stride + t.dim) * 4, i, "output",
-               &outputs);
+    if (bags > 0 && r.output != nullptr) {
+      outputs.push_back(
+          {static_cast<int64_t>(reinterpret_cast<uintptr_t>(r.output)),
+           stride * 4, static_cast<int64_t>(t.dim) * 4, bags, i, "output"});
     }
     AddRange(r.ids, r.num_ids * (r.ids_type == XSE_INDEX_I64 ? 8 : 4), i,
              "embedding-ID", &inputs);
@@ -225,22 +263,28 @@ int CheckIsolation(const xse_bag_request* reqs,
                  static_cast<int64_t>(ElemBytes(t.dtype)),
              i, "embedding-table", &inputs);
   }
+  // Sorted by start, outputs are compared pairwise while their hulls can
+  // still meet (strided outputs interleave, so neighbours are not enough).
   std::sort(outputs.begin(), outputs.end(),
-            [](const Range& a, const Range& b) { return a.begin < b.begin; });
+            [](const Range& a, const Range& b) { return a.base < b.base; });
   char buf[256];
-  for (size_t k = 1; k < outputs.size(); ++k) {
-    if (outputs[k - 1].begin < outputs[k].end &&
-        outputs[k].begin < outputs[k - 1].end) {
-      snprintf(buf, sizeof(buf),
-               "FP32 embedding-bag request outputs %d and %d overlap.",
-               outputs[k - 1].request, outputs[k].request);
-      *message = buf;
-      return XSE_INVALID_ARGUMENT;
+  for (size_t k = 0; k < outputs.size(); ++k) {
+    for (size_t j = k + 1;
+         j < outputs.size() && outputs[j].base < outputs[k].end(); ++j) {
+      if (Overlaps(outputs[k], outputs[j])) {
+        const int32_t lo = std::min(outputs[k].request, outputs[j].request);
+        const int32_t hi = std::max(outputs[k].request, outputs[j].request);
+        snprintf(buf, sizeof(buf),
+                 "FP32 embedding-bag request outputs %d and %d overlap.", lo,
+                 hi);
+        *message = buf;
+        return XSE_INVALID_ARGUMENT;
+      }
     }
   }
   for (const Range& o : outputs) {
     for (const Range& in : inputs) {
-      if (o.begin < in.end && in.begin < o.end) {
+      if (Overlaps(o, in)) {
         snprintf(buf, sizeof(buf),
                  "FP32 embedding-bag request %d output overlaps request %d %s "
                  "storage.",
@@ -426,7 +470,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
       for (size_t k = 0; k < cnt; ++k) {
         p.d[k] = descs[base + k];
         p.d[k].work_begin = work;
-        work += p.d[k].num_bags + 1 + p.d[k].num_ids;
+        work += xse::ValidationWork(p.d[k].num_bags, p.d[k].num_ids);
       }
       p.n = static_cast<int32_t>(cnt);
       e = xse::LaunchValidate(p, work, stream);
@@ -450,18 +494,21 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
     }
     if (timing.first != nullptr) cudaEventRecord(timing.first, stream);
     // Group descriptors by kernel layout, keeping request order within each.
-    std::map<std::tuple<int, int, int>, std::vector<xse::BagDesc>> groups;
+    std::map<std::tuple<int, int, int, bool, int>, std::vector<xse::BagDesc>>
+        groups;
     for (const xse::BagDesc& d : descs) {
-      const xse::Layout l =
-          xse::ChooseLayout(tables[d.slot]->dtype, d.dim, d.rows);
-      const int v = tables[d.slot]->dtype == XSE_DT_I8_ROWWISE &&
-                            d.scale_bias == nullptr
-                        ? 0
-                        : l.v;
-      groups[{l.dtype, l.g, v}].push_back(d);
+      xse::Layout l = xse::ChooseLayout(tables[d.slot]->dtype, d.dim, d.rows);
+      if (tables[d.slot]->dtype == XSE_DT_I8_ROWWISE &&
+          d.scale_bias == nullptr) {
+        l.v = 0;  // an empty int8 window: the element-wise kernel
+        l.exact = false;
+      }
+      l.wmode = l.v == 0 ? 0 : xse::WeightModeOf(d);
+      groups[{l.dtype, l.g, l.v, l.exact, l.wmode}].push_back(d);
     }
     for (auto& [key, list] : groups) {
-      const xse::Layout l{std::get<0>(key), std::get<1>(key), std::get<2>(key)};
+      const xse::Layout l{std::get<0>(key), std::get<1>(key), std::get<2>(key),
+                          std::get<3>(key), std::get<4>(key)};
       for (size_t base = 0; base < list.size();
            base += xse::kMaxDescsPerLaunch) {
         xse::PoolParams p{};
@@ -473,7 +520,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
         for (size_t k = 0; k < cnt; ++k) {
           p.d[k] = list[base + k];
           p.d[k].task_begin = tasks;
-          tasks += p.d[k].num_bags;
+          tasks += xse::TasksFor(l, p.d[k].num_bags);
         }
         p.n = static_cast<int32_t>(cnt);
         p.total_tasks = tasks;

@@ -26,7 +26,7 @@ struct BagDesc {
   int64_t num_ids;
   int64_t num_weights;
   int64_t num_bags;
-  int64_t task_begin;         // first global task (bag) of this descriptor
+  int64_t task_begin;         // first pooling task of this descriptor
   int64_t work_begin;         // first validation work item of this descriptor
   int32_t dim;
   int32_t slot;               // request index into the status block
@@ -66,6 +66,8 @@ struct PoolParams {
   int32_t n;
   int32_t fused_checks;   // 1: record errors here; 0: a validation pass ran
   int64_t total_tasks;
+  int32_t bags_per_task;  // consecutive bags one lane group pools per task
+  int32_t reserved;
   DevStatus* status;
   BagDesc d[kMaxDescsPerLaunch];
 };
@@ -76,9 +78,21 @@ struct Layout {
   int dtype;
   int g;
   int v;
+  bool exact;  // rows are exactly g*v vectors: no per-lane bounds checks
+  int wmode;   // 0 unweighted, 1 weighted sum, 2 weighted mean / sqrt-n
 };
 
+// Weighting mode of a request (kernels are compiled per mode).
+inline int WeightModeOf(const BagDesc& d) {
+  if (d.weights == nullptr) return 0;
+  return d.combine == 1 ? 1 : 2;
+}
+
 Layout ChooseLayout(int dtype, int dim, const void* rows);
+// Pooling tasks (work units of one lane group) for num_bags bags.
+int64_t TasksFor(const Layout& layout, int64_t num_bags);
+// Validation work items of one request.
+int64_t ValidationWork(int64_t num_bags, int64_t num_ids);
 
 cudaError_t LaunchValidate(const PoolParams& p, int64_t total_work,
                            cudaStream_t stream);
