@@ -254,6 +254,55 @@ def test_async_status_and_errors(xse):
   eng.close()
 
 
+def test_async_ring_reports_first_failure(xse):
+  """Asynchronous executions share a status ring: the wait reports the first
+  failing execution, including after the ring wrapped; the status is
+  reusable after a wait, and a synchronous call settles pending ones."""
+  rng = np.random.default_rng(21)
+  host, dev, _, _ = random_table(rng, oracle.F32, 50, 16)
+  eng = xse.EmbeddingEngine(0)
+  eng.add_table("t", dev, "SUM")
+  eng.register_feature("f", "t")
+  ids, offsets = random_csr(rng, 50, 40, 6)
+  good = to_dev(ids)
+  bad_host = ids.copy()
+  bad_host[3] = 50
+  bad = to_dev(bad_host)
+  offs = to_dev(offsets)
+  out = torch.empty((40, 16), device="cuda")
+  st = xse.Status(4)
+  want = oracle_pool(host, oracle.F32, ids, offsets, None, "SUM")
+  msg = ("FP32 embedding-bag request 0: Embedding ID (50) at index 3 is out "
+         "of bounds [0, 50).")
+  for failing in (10, 70):  # 70: the ring (64 slots) wraps first
+    for k in range(100):
+      eng.execute_batch([xse.BagRequest("f", bad if k == failing else good,
+                                        offs, out)], status=st)
+    with pytest.raises(xse.XseError) as e:
+      st.wait()
+    assert e.value.message == msg
+    st.wait()  # settled: nothing pending
+  for _ in range(3):
+    eng.execute_batch([xse.BagRequest("f", good, offs, out)], status=st)
+  st.wait()
+  assert_bitwise(out.cpu().numpy(), want, "after ring")
+  # A synchronous call through the same status block settles pending
+  # asynchronous executions first and reports their error.
+  eng.execute_batch([xse.BagRequest("f", bad, offs, out)], status=st)
+  arr, _ = eng._c_requests([xse.BagRequest("f", good, offs, out)])
+  rc = xse._capi.lib.xse_engine_execute_batch(
+      eng.handle, arr, 1, xse.stream_handle(), xse._capi.EXEC_STRICT,
+      st.handle)
+  assert rc == xse._capi.INVALID_ARGUMENT
+  assert xse._capi.last_error() == msg
+  rc = xse._capi.lib.xse_engine_execute_batch(
+      eng.handle, arr, 1, xse.stream_handle(), xse._capi.EXEC_STRICT,
+      st.handle)
+  assert rc == xse._capi.OK
+  st.close()
+  eng.close()
+
+
 def test_addition_order_fixture(xse):
   import os  # pylint: disable=import-outside-toplevel
   g = np.load(os.path.join(os.path.dirname(__file__), "golden",

@@ -207,6 +207,13 @@ __device__ __forceinline__ int AdvanceDesc(const PoolParams& p, int t,
   return t;
 }
 
+// Same for validation work items, ordered by work_begin.
+__device__ __forceinline__ int AdvanceWork(const PoolParams& p, int t,
+                                           int64_t w) {
+  while (t + 1 < p.n && w >= p.d[t + 1].work_begin) ++t;
+  return t;
+}
+
 // Offsets of bag `bag`, checked. Returns false when the bag must be skipped.
 __device__ __forceinline__ bool BagRange(const PoolParams& p,
                                          const BagDesc& d, int64_t bag,
@@ -622,54 +629,42 @@ __global__ void __launch_bounds__(kThreads)
 // Group validation (ValidateEmbeddingBagInput, embedding_bag.cc:99-133).
 // Offsets must start >= 0 and never decrease; the final offset must not
 // exceed the ids (or weights); every id in [first, last) must be in
-// [0, vocab). Work items are runs of kValidateRun consecutive offsets or
-// id positions of one request.
-constexpr int kValidateRun = 8;
-
+// [0, vocab). One work item per offset and per id position, consecutive
+// items on consecutive threads (coalesced); each thread keeps the first and
+// last offsets of the request it is in.
 __global__ void __launch_bounds__(kThreads)
     ValidateKernel(const __grid_constant__ PoolParams p, int64_t total_work) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int t = 0;
+  int t = -1;
+  int64_t first = 0, last = 0;
   for (int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        w < total_work; w += stride) {
-    while (t + 1 < p.n && w >= p.d[t + 1].work_begin) ++t;
-    const BagDesc& d = p.d[t];
-    const int64_t item = w - d.work_begin;
+    const int t0 = t < 0 ? 0 : t;
+    const int tn = AdvanceWork(p, t0, w);
+    const BagDesc& d = p.d[tn];
+    if (tn != t) {
+      t = tn;
+      first = LoadIndex(d.offsets, d.offs64, 0);
+      last = LoadIndex(d.offsets, d.offs64, d.num_bags);
+    }
+    const int64_t i = w - d.work_begin;
     const int64_t num_offsets = d.num_bags + 1;
-    const int64_t offset_runs = (num_offsets + kValidateRun - 1) / kValidateRun;
-    if (item < offset_runs) {
-      const int64_t i0 = item * kValidateRun;
-      const int64_t i1 = i0 + kValidateRun < num_offsets ? i0 + kValidateRun
-                                                         : num_offsets;
-      int64_t prev = i0 == 0 ? 0 : LoadIndex(d.offsets, d.offs64, i0 - 1);
-      bool bad = false;
-      int64_t cur = 0;
-      for (int64_t i = i0; i < i1; ++i) {
-        cur = LoadIndex(d.offsets, d.offs64, i);
-        bad |= i == 0 ? cur < 0 : cur < prev;
-        prev = cur;
-      }
+    if (i < num_offsets) {
+      const int64_t cur = LoadIndex(d.offsets, d.offs64, i);
+      const bool bad =
+          i == 0 ? cur < 0 : LoadIndex(d.offsets, d.offs64, i - 1) > cur;
       if (bad) RecordError(p.status, d.slot, kErrBadOffsets);
-      if (i1 == num_offsets) {
+      if (i == num_offsets - 1) {
         if (cur > d.num_ids) RecordError(p.status, d.slot, kErrLastExceedsIds);
         if (d.weights != nullptr && cur > d.num_weights) {
           RecordError(p.status, d.slot, kErrLastExceedsWeights);
         }
       }
     } else if (d.ids != nullptr) {
-      const int64_t first = LoadIndex(d.offsets, d.offs64, 0);
-      const int64_t last = LoadIndex(d.offsets, d.offs64, d.num_bags);
-      const int64_t p0 = (item - offset_runs) * kValidateRun;
-      int64_t lo = p0 > first ? p0 : first;
-      int64_t hi = p0 + kValidateRun;
-      if (hi > last) hi = last;
-      if (hi > d.num_ids) hi = d.num_ids;
-      for (int64_t pos = lo; pos < hi; ++pos) {
+      const int64_t pos = i - num_offsets;
+      if (pos >= first && pos < last) {
         const int64_t id = LoadIndex(d.ids, d.ids64, pos);
-        if (id < 0 || id >= d.vocab) {
-          RecordBadId(p.status, d.slot, pos);
-          break;  // later positions of this run cannot be the minimum
-        }
+        if (id < 0 || id >= d.vocab) RecordBadId(p.status, d.slot, pos);
       }
     }
   }
@@ -808,8 +803,7 @@ int64_t TasksFor(const Layout& layout, int64_t num_bags) {
 }
 
 int64_t ValidationWork(int64_t num_bags, int64_t num_ids) {
-  return (num_bags + 1 + kValidateRun - 1) / kValidateRun +
-         (num_ids + kValidateRun - 1) / kValidateRun;
+  return num_bags + 1 + num_ids;
 }
 
 cudaError_t LaunchPool(const Layout& layout, const PoolParams& p,

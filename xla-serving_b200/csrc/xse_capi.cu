@@ -110,16 +110,42 @@ struct RequestMeta {
 
 }  // namespace
 
-struct xse_status {
-  int device = 0;
-  int32_t capacity = 0;
-  xse::DevStatus* dev = nullptr;
-  xse::DevStatus* host = nullptr;  // pinned mirror
+namespace {
+
+// What the host knows about one execution recorded in a status slot.
+struct StatusSlot {
   std::vector<RequestMeta> meta;
   int32_t n = 0;
-  bool pending = false;
   int early_code = XSE_OK;  // host-side failure decided at launch time
   std::string early_message;
+};
+
+}  // namespace
+
+// A ring of device status slots, one per execution. Synchronous executions
+// use slot 0 and read it back at once. Asynchronous executions fill slots in
+// turn with no per-execution memset or read-back: the ring is cleared with
+// one memset when it starts over and read back in one copy at
+// xse_status_wait, which reports the first failing execution.
+struct xse_status {
+  int device = 0;
+  int32_t capacity = 0;  // requests per execution
+  int32_t ring = 1;      // slots
+  size_t slot_bytes = 0;
+  char* dev = nullptr;
+  char* host = nullptr;  // pinned mirror
+  std::vector<StatusSlot> slots;
+  int32_t used = 0;        // slots filled since the last read-back
+  bool need_reset = true;  // slots 1.. may hold old results
+  int deferred_code = XSE_OK;  // first error of a read-back forced by a full ring
+  std::string deferred_message;
+
+  xse::DevStatus* dev_slot(int k) {
+    return reinterpret_cast<xse::DevStatus*>(dev + slot_bytes * k);
+  }
+  xse::DevStatus* host_slot(int k) {
+    return reinterpret_cast<xse::DevStatus*>(host + slot_bytes * k);
+  }
 };
 
 struct xse_engine {
@@ -139,13 +165,15 @@ struct xse_engine {
 
 namespace {
 
-// Resolves the group's errors in request order, mirroring the order of the
-// reference's per-request checks. Returns the status code.
-int ResolveStatus(xse_status* st) {
-  for (int32_t i = 0; i < st->n; ++i) {
-    const RequestMeta& m = st->meta[i];
+// Resolves the errors of the execution in slot k in request order, mirroring
+// the order of the reference's per-request checks. Returns the status code.
+int ResolveSlot(xse_status* st, int k) {
+  const StatusSlot& slot = st->slots[k];
+  const xse::DevStatus* host = st->host_slot(k);
+  for (int32_t i = 0; i < slot.n; ++i) {
+    const RequestMeta& m = slot.meta[i];
     if (m.stage == kStageEarly) return SetError(m.code, "%s", m.message.c_str());
-    const unsigned int flags = st->host->req[i].flags;
+    const unsigned int flags = host->req[i].flags;
     const char* msg = nullptr;
     if (flags & xse::kErrBadOffsets) {
       msg = "Row pointers must be non-negative and monotonic.";
@@ -163,7 +191,7 @@ int ResolveStatus(xse_status* st) {
     }
     if (flags & xse::kErrBadId) {
       const int64_t index =
-          static_cast<int64_t>(~st->host->req[i].inv_min_bad_index);
+          static_cast<int64_t>(~host->req[i].inv_min_bad_index);
       int64_t id = 0;
       if (m.ids64) {
         cudaMemcpy(&id, static_cast<const int64_t*>(m.ids) + index,
@@ -181,10 +209,41 @@ int ResolveStatus(xse_status* st) {
                       i, id, index, m.vocab);
     }
   }
-  if (st->early_code != XSE_OK) {
-    return SetError(st->early_code, "%s", st->early_message.c_str());
+  if (slot.early_code != XSE_OK) {
+    return SetError(slot.early_code, "%s", slot.early_message.c_str());
   }
   return Ok();
+}
+
+// Waits for the stream, reads back every filled slot and returns the first
+// error among them (or one deferred by an earlier forced read-back).
+int SettleStatus(xse_status* st, cudaStream_t stream) {
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return SetError(XSE_INTERNAL, "stream synchronize: %s",
+                                        cudaGetErrorString(e));
+  int code = XSE_OK;
+  std::string message;
+  if (st->used > 0) {
+    e = cudaMemcpy(st->host, st->dev, st->slot_bytes * st->used,
+                   cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) {
+      return SetError(XSE_INTERNAL, "status read-back: %s",
+                      cudaGetErrorString(e));
+    }
+    for (int32_t k = 0; k < st->used && code == XSE_OK; ++k) {
+      code = ResolveSlot(st, k);
+      if (code != XSE_OK) message = g_last_error;
+    }
+  }
+  st->used = 0;
+  st->need_reset = true;
+  if (st->deferred_code != XSE_OK) {
+    code = st->deferred_code;
+    message = st->deferred_message;
+    st->deferred_code = XSE_OK;
+    st->deferred_message.clear();
+  }
+  return code == XSE_OK ? Ok() : SetError(code, "%s", message.c_str());
 }
 
 // A set of `count` byte intervals [base + k*stride, base + k*stride + width).
@@ -353,11 +412,25 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
   }
 
   DeviceGuard guard(engine->device);
-  st->n = n;
-  st->pending = false;
-  st->early_code = XSE_OK;
-  st->early_message.clear();
-  st->meta.assign(static_cast<size_t>(n), RequestMeta());
+  const bool async = (flags & XSE_EXEC_ASYNC) != 0;
+  // A synchronous execution first settles earlier asynchronous ones; an
+  // asynchronous one settles the ring only when it is full (an error found
+  // then is reported by the next wait).
+  if (st->used > 0 && (!async || st->used == st->ring)) {
+    const int code = SettleStatus(st, stream);
+    if (code != XSE_OK) {
+      if (!async) return code;
+      st->deferred_code = code;
+      st->deferred_message = g_last_error;
+    }
+  }
+  const int slot_index = st->used;
+  StatusSlot& slot = st->slots[slot_index];
+  slot.n = n;
+  slot.early_code = XSE_OK;
+  slot.early_message.clear();
+  slot.meta.assign(static_cast<size_t>(n), RequestMeta());
+  xse::DevStatus* const dev_status = st->dev_slot(slot_index);
 
   // Host-side checks (PrepareRequest, embedding_bag.cc:235-251).
   std::vector<xse::BagDesc> descs;
@@ -367,7 +440,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
   for (int32_t i = 0; i < n; ++i) {
     const xse_bag_request& r = reqs[i];
     const Table& t = *tables[i];
-    RequestMeta& m = st->meta[i];
+    RequestMeta& m = slot.meta[i];
     m.ids = r.ids;
     m.ids64 = r.ids_type == XSE_INDEX_I64;
     m.vocab = t.vocab;
@@ -439,8 +512,8 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
   }
   // The first request's early error wins outright when no earlier request
   // can fail on the device.
-  if (any_early && st->meta[0].stage == kStageEarly) {
-    return SetError(st->meta[0].code, "%s", st->meta[0].message.c_str());
+  if (any_early && slot.meta[0].stage == kStageEarly) {
+    return SetError(slot.meta[0].code, "%s", slot.meta[0].message.c_str());
   }
   std::string iso_message;
   int iso_code = XSE_OK;
@@ -448,12 +521,20 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
     iso_code = CheckIsolation(reqs, tables, n, &iso_message);
   }
 
-  cudaError_t e = cudaMemsetAsync(st->dev, 0, xse::DevStatusBytes(n), stream);
+  // Clear this execution's slot: the whole ring when an asynchronous run of
+  // executions starts, only slot 0 for a synchronous one.
+  cudaError_t e = cudaSuccess;
+  if (async && slot_index == 0) {
+    e = cudaMemsetAsync(st->dev, 0, st->slot_bytes * st->ring, stream);
+    st->need_reset = false;
+  } else if (!async || st->need_reset) {
+    e = cudaMemsetAsync(dev_status, 0, xse::DevStatusBytes(n), stream);
+  }
   if (e != cudaSuccess) return CudaError(e, "status reset");
   const bool fused = (flags & XSE_EXEC_FUSED) != 0;
   const bool validate_only = any_early || iso_code != XSE_OK;
   const bool any_soft = std::any_of(
-      st->meta.begin(), st->meta.end(),
+      slot.meta.begin(), slot.meta.end(),
       [](const RequestMeta& m) { return m.stage != kStageNone; });
 
   // Validation pass over every descriptor (strict mode, or whenever the
@@ -463,7 +544,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
     for (size_t base = 0; base < descs.size();
          base += xse::kMaxDescsPerLaunch) {
       xse::PoolParams p{};
-      p.status = st->dev;
+      p.status = dev_status;
       int64_t work = 0;
       const size_t cnt =
           std::min<size_t>(xse::kMaxDescsPerLaunch, descs.size() - base);
@@ -512,7 +593,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
       for (size_t base = 0; base < list.size();
            base += xse::kMaxDescsPerLaunch) {
         xse::PoolParams p{};
-        p.status = st->dev;
+        p.status = dev_status;
         p.fused_checks = fused ? 1 : 0;
         const size_t cnt =
             std::min<size_t>(xse::kMaxDescsPerLaunch, list.size() - base);
@@ -531,23 +612,14 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
     if (timing.second != nullptr) cudaEventRecord(timing.second, stream);
   }
   g_last_launches = launches;
-  e = cudaMemcpyAsync(st->host, st->dev, xse::DevStatusBytes(n),
-                      cudaMemcpyDeviceToHost, stream);
-  if (e != cudaSuccess) return CudaError(e, "status copy");
   if (iso_code != XSE_OK) {
-    st->early_code = iso_code;
-    st->early_message = iso_message;
-  } else if (any_early || any_soft) {
-    // Ordering decided after the device validation; nothing was pooled.
+    slot.early_code = iso_code;
+    slot.early_message = iso_message;
   }
-  st->pending = true;
-  if ((flags & XSE_EXEC_ASYNC) != 0 && !validate_only && !any_soft) {
-    return Ok();
-  }
-  e = cudaStreamSynchronize(stream);
-  st->pending = false;
-  if (e != cudaSuccess) return CudaError(e, "stream synchronize");
-  const int code = ResolveStatus(st);
+  st->used = slot_index + 1;
+  if (async && !validate_only && !any_soft) return Ok();
+  // Synchronous, or the group is known to fail: read the result now.
+  const int code = SettleStatus(st, stream);
   if (code == XSE_OK && (any_early || any_soft)) {
     // Unreachable: an early or soft error always resolves to a failure.
     return SetError(XSE_INTERNAL, "unresolved request error");
@@ -555,11 +627,19 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
   return code;
 }
 
-int CreateStatus(int device, int32_t capacity, xse_status** out) {
+// Asynchronous executions recorded before a read-back is forced.
+constexpr int32_t kStatusRing = 64;
+
+// Status blocks of `ring` slots of `capacity` requests each.
+int CreateStatus(int device, int32_t capacity, int32_t ring,
+                 xse_status** out) {
   auto st = std::make_unique<xse_status>();
   st->device = device;
   st->capacity = capacity;
-  const size_t bytes = xse::DevStatusBytes(capacity);
+  st->ring = ring;
+  st->slot_bytes = (xse::DevStatusBytes(capacity) + 255) / 256 * 256;
+  st->slots.resize(static_cast<size_t>(ring));
+  const size_t bytes = st->slot_bytes * ring;
   cudaError_t e = cudaMalloc(&st->dev, bytes);
   if (e != cudaSuccess) return CudaError(e, "status allocation");
   e = cudaMallocHost(&st->host, bytes);
@@ -595,7 +675,8 @@ int xse_engine_create(const xse_engine_options* options, xse_engine** out) {
                     engine->device);
   }
   DeviceGuard guard(engine->device);
-  const int code = CreateStatus(engine->device, 256, &engine->default_status);
+  const int code =
+      CreateStatus(engine->device, 256, 1, &engine->default_status);
   if (code != XSE_OK) return code;
   *out = engine.release();
   return Ok();
@@ -826,7 +907,7 @@ int xse_status_create(int32_t max_requests, xse_status** out) {
   }
   int device = 0;
   cudaGetDevice(&device);
-  const int code = CreateStatus(device, max_requests, out);
+  const int code = CreateStatus(device, max_requests, kStatusRing, out);
   return code == XSE_OK ? Ok() : code;
 }
 
@@ -849,13 +930,7 @@ int xse_engine_execute_batch(xse_engine* engine, const xse_bag_request* reqs,
 int xse_status_wait(xse_status* status, void* stream) {
   if (status == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null status");
   DeviceGuard guard(status->device);
-  if (status->pending) {
-    const cudaError_t e =
-        cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
-    status->pending = false;
-    if (e != cudaSuccess) return CudaError(e, "stream synchronize");
-  }
-  return ResolveStatus(status);
+  return SettleStatus(status, static_cast<cudaStream_t>(stream));
 }
 
 int xse_dot_interaction(const float* dense, const float* pooled,
