@@ -180,6 +180,32 @@ int xse_engine_execute_batch(xse_engine* engine, const xse_bag_request* reqs,
  * with this block (and its message through xse_last_error). */
 int xse_status_wait(xse_status* status, void* stream);
 
+/* Allocation-free variant of xse_engine_execute_batch (strict mode,
+ * synchronous). No counterpart in the reference, which pools on the host.
+ *
+ * For callers that must not allocate GPU memory while serving a request:
+ * code running inside a host framework that owns every device buffer (an
+ * XLA custom call or a serving runtime with its own pre-sized arena), or a
+ * latency-critical thread where a cudaMalloc would synchronize the device.
+ * The caller passes inputs and outputs as for xse_engine_execute_batch; the
+ * per-call validation status that the regular call keeps in a status block
+ * lives instead in one fixed array in device memory, sized for at most
+ * XSE_NOALLOC_MAX_REQUESTS requests (larger groups are rejected with
+ * XSE_INVALID_ARGUMENT). Every device that loads this library holds that
+ * array (about 1 KB) until the process exits. The call allocates no device
+ * or pinned memory and calls no allocating library routine.
+ *
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call outside any CUDA stream
+ * capture. All calls share the one array and clear it at their start, so
+ * calls that overlap on the GPU (from several host threads or streams at
+ * once) race on it: serialize them. Host-side argument errors are reported
+ * before any device-side validation error. */
+#define XSE_NOALLOC_MAX_REQUESTS 64
+int xse_engine_execute_batch_noalloc(xse_engine* engine,
+                                     const xse_bag_request* reqs, int32_t n,
+                                     void* stream);
+
 /* Number of CUDA kernels the last xse_engine_execute_batch on this thread
  * launched. */
 int32_t xse_last_launch_count(void);

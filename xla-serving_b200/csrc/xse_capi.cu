@@ -1003,3 +1003,315 @@ int xse_synth_weights(float* weights, int64_t n, uint64_t seed,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free execution (xse_engine_execute_batch_noalloc).
+//
+// The status that xse_engine_execute_batch keeps in an allocated block lives
+// here in one fixed device array. Everything else the call needs on the host
+// (resolved tables, descriptors, the kernel parameter block, the status
+// read-back) sits on the stack, so the call allocates nothing.
+
+namespace {
+
+constexpr int32_t kNoAllocMaxRequests = XSE_NOALLOC_MAX_REQUESTS;
+static_assert(kNoAllocMaxRequests <= xse::kMaxDescsPerLaunch,
+              "one validation launch covers the whole group");
+constexpr size_t kNoAllocStatusBytes =
+    sizeof(xse::DevStatus) +
+    sizeof(xse::DevRequestStatus) * (kNoAllocMaxRequests - 1);
+
+}  // namespace
+
+// Device scratch of the allocation-free call: every GPU that loads this
+// library holds one copy until the process exits. Host code only sees a
+// stand-in for it; its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char
+    g_noalloc_status[kNoAllocStatusBytes];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_address[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on `device` (which must be current),
+// looked up on the first call per device.
+int NoAllocScratch(int device, xse::DevStatus** out) {
+  if (device < 0 || device >= kNoAllocMaxDevices) {
+    return SetError(XSE_FAILED_PRECONDITION,
+                    "Device %d is beyond the %d devices the allocation-free "
+                    "call supports.",
+                    device, kNoAllocMaxDevices);
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_address[device] == nullptr) {
+    void* address = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&address, g_noalloc_status);
+    if (e != cudaSuccess) return CudaError(e, "scratch symbol address");
+    g_noalloc_address[device] = address;
+  }
+  *out = static_cast<xse::DevStatus*>(g_noalloc_address[device]);
+  return XSE_OK;
+}
+
+}  // namespace
+
+extern "C" int xse_engine_execute_batch_noalloc(xse_engine* engine,
+                                                const xse_bag_request* reqs,
+                                                int32_t n, void* stream) {
+  g_last_launches = 0;
+  if (engine == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null engine");
+  if (n <= 0 || reqs == nullptr) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Embedding batch requires at least one request.");
+  }
+  if (n > kNoAllocMaxRequests) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "The allocation-free call takes at most %d requests; got "
+                    "%d. Split the group or use xse_engine_execute_batch.",
+                    kNoAllocMaxRequests, n);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::shared_ptr<Table> tables[kNoAllocMaxRequests];
+  {
+    std::lock_guard<std::mutex> spec_lock(engine->specs_mu);
+    std::lock_guard<std::mutex> table_lock(engine->tables_mu);
+    for (int32_t i = 0; i < n; ++i) {
+      const char* fname = reqs[i].feature_name ? reqs[i].feature_name : "";
+      // A scan instead of find(): find would build a std::string key.
+      auto spec = engine->features.begin();
+      while (spec != engine->features.end() &&
+             std::strcmp(spec->first.c_str(), fname) != 0) {
+        ++spec;
+      }
+      if (spec == engine->features.end()) {
+        return SetError(XSE_NOT_FOUND, "Feature spec not found for: %s", fname);
+      }
+      if (spec->second.max_sequence_length != 0) {
+        return SetError(XSE_UNIMPLEMENTED,
+                        "Batch request %d requires a non-sequence feature "
+                        "specification.",
+                        i);
+      }
+      auto table = engine->tables.find(spec->second.table);
+      if (table == engine->tables.end()) {
+        return SetError(XSE_NOT_FOUND, "Table not found for: %s",
+                        spec->second.table.c_str());
+      }
+      tables[i] = table->second;
+    }
+  }
+
+  DeviceGuard guard(engine->device);
+  xse::DevStatus* scratch = nullptr;
+  int code = NoAllocScratch(engine->device, &scratch);
+  if (code != XSE_OK) return code;
+
+  // Host checks (PrepareRequest, embedding_bag.cc:235-251) and descriptors.
+  xse::PoolParams params{};  // kernel parameter block (~9 KB, on the stack)
+  xse::BagDesc* descs = params.d;
+  for (int32_t i = 0; i < n; ++i) {
+    const xse_bag_request& r = reqs[i];
+    const Table& t = *tables[i];
+    if (r.output == nullptr) {
+      return SetError(XSE_INVALID_ARGUMENT,
+                      "FP32 embedding-bag request %d requires an output "
+                      "allocator.",
+                      i);
+    }
+    const char* problem = nullptr;
+    if ((r.ids_type != XSE_INDEX_I32 && r.ids_type != XSE_INDEX_I64) ||
+        (r.offsets_type != XSE_INDEX_I32 && r.offsets_type != XSE_INDEX_I64)) {
+      problem = "Embedding IDs and row pointers must be int32 or int64.";
+    } else if (r.num_offsets < 2 || r.offsets == nullptr) {
+      problem = "Row pointers must contain at least two elements.";
+    } else if (r.num_ids < 0 || r.num_weights < 0 ||
+               (r.output_stride != 0 && r.output_stride < t.dim)) {
+      problem =
+          "Request sizes must be non-negative and the output stride at least "
+          "the embedding dimension.";
+    } else if (r.ids == nullptr && r.num_ids > 0) {
+      problem = "Embedding-ID storage must be non-null.";
+    } else if (r.weights == nullptr && r.num_weights > 0) {
+      problem = "Weight storage must be non-null.";
+    }
+    if (problem != nullptr) {
+      return SetError(XSE_INVALID_ARGUMENT, "FP32 embedding-bag request %d: %s",
+                      i, problem);
+    }
+    xse::BagDesc d{};
+    d.rows = t.rows;
+    d.scale_bias = t.scale_bias;
+    d.ids = r.ids;
+    d.offsets = r.offsets;
+    d.weights = r.num_weights > 0 ? r.weights : nullptr;
+    d.out = r.output;
+    d.out_stride = r.output_stride > 0 ? r.output_stride : t.dim;
+    d.vocab = t.vocab;
+    d.row_begin = t.row_begin;
+    d.row_end = t.row_end;
+    d.num_ids = r.num_ids;
+    d.num_weights = r.num_weights;
+    d.num_bags = r.num_offsets - 1;
+    d.dim = t.dim;
+    d.slot = i;
+    d.combine = static_cast<int8_t>(t.combine);
+    d.ids64 = static_cast<int8_t>(r.ids_type == XSE_INDEX_I64);
+    d.offs64 = static_cast<int8_t>(r.offsets_type == XSE_INDEX_I64);
+    d.vec_out = static_cast<int8_t>(
+        (reinterpret_cast<uintptr_t>(r.output) & 15u) == 0 &&
+        d.out_stride % 4 == 0);
+    descs[i] = d;
+  }
+
+  // Output isolation (embedding_bag.cc:304-351) on fixed arrays.
+  Range outputs[kNoAllocMaxRequests];
+  Range inputs[kNoAllocMaxRequests * 4];
+  int32_t n_out = 0, n_in = 0;
+  for (int32_t i = 0; i < n; ++i) {
+    const xse::BagDesc& d = descs[i];
+    const Table& t = *tables[i];
+    if (d.num_bags > 0) {
+      outputs[n_out++] = {static_cast<int64_t>(reinterpret_cast<uintptr_t>(d.out)),
+                          d.out_stride * 4, static_cast<int64_t>(t.dim) * 4,
+                          d.num_bags, i, "output"};
+    }
+    auto add = [&](const void* p, int64_t bytes, const char* kind) {
+      if (p != nullptr && bytes > 0) {
+        inputs[n_in++] = {static_cast<int64_t>(reinterpret_cast<uintptr_t>(p)),
+                          bytes, bytes, 1, i, kind};
+      }
+    };
+    add(d.ids, d.num_ids * (d.ids64 ? 8 : 4), "embedding-ID");
+    add(d.offsets, (d.num_bags + 1) * (d.offs64 ? 8 : 4), "row-pointer");
+    add(d.weights, d.num_weights * 4, "weight");
+    add(t.rows,
+        (t.row_end - t.row_begin) * t.dim *
+            static_cast<int64_t>(ElemBytes(t.dtype)),
+        "embedding-table");
+  }
+  for (int32_t a = 0; a < n_out; ++a) {
+    for (int32_t b = a + 1; b < n_out; ++b) {
+      if (Overlaps(outputs[a], outputs[b])) {
+        return SetError(XSE_INVALID_ARGUMENT,
+                        "FP32 embedding-bag request outputs %d and %d "
+                        "overlap.",
+                        outputs[a].request, outputs[b].request);
+      }
+    }
+    for (int32_t b = 0; b < n_in; ++b) {
+      if (Overlaps(outputs[a], inputs[b])) {
+        return SetError(XSE_INVALID_ARGUMENT,
+                        "FP32 embedding-bag request %d output overlaps "
+                        "request %d %s storage.",
+                        outputs[a].request, inputs[b].request, inputs[b].kind);
+      }
+    }
+  }
+
+  // The array keeps the previous call's status: clear this call's part.
+  cudaError_t e = cudaMemsetAsync(scratch, 0, xse::DevStatusBytes(n), s);
+  if (e != cudaSuccess) return CudaError(e, "scratch reset");
+  int launches = 0;
+  {
+    int64_t work = 0;
+    for (int32_t i = 0; i < n; ++i) {
+      descs[i].work_begin = work;
+      work += xse::ValidationWork(descs[i].num_bags, descs[i].num_ids);
+    }
+    params.n = n;
+    params.fused_checks = 0;
+    params.status = scratch;
+    e = xse::LaunchValidate(params, work, s);
+    if (e != cudaSuccess) return CudaError(e, "validation launch");
+    ++launches;
+  }
+  // One pooling launch per kernel layout, requests kept in order.
+  xse::PoolParams group{};
+  bool launched[kNoAllocMaxRequests] = {};
+  for (int32_t i = 0; i < n; ++i) {
+    if (launched[i]) continue;
+    xse::Layout li = xse::ChooseLayout(tables[i]->dtype, descs[i].dim,
+                                       descs[i].rows);
+    if (tables[i]->dtype == XSE_DT_I8_ROWWISE &&
+        descs[i].scale_bias == nullptr) {
+      li.v = 0;
+      li.exact = false;
+    }
+    li.wmode = li.v == 0 ? 0 : xse::WeightModeOf(descs[i]);
+    group.n = 0;
+    group.fused_checks = 0;
+    group.status = scratch;
+    int64_t tasks = 0;
+    for (int32_t j = i; j < n; ++j) {
+      if (launched[j]) continue;
+      xse::Layout lj = xse::ChooseLayout(tables[j]->dtype, descs[j].dim,
+                                         descs[j].rows);
+      if (tables[j]->dtype == XSE_DT_I8_ROWWISE &&
+          descs[j].scale_bias == nullptr) {
+        lj.v = 0;
+        lj.exact = false;
+      }
+      lj.wmode = lj.v == 0 ? 0 : xse::WeightModeOf(descs[j]);
+      if (lj.dtype != li.dtype || lj.g != li.g || lj.v != li.v ||
+          lj.exact != li.exact || lj.wmode != li.wmode) {
+        continue;
+      }
+      launched[j] = true;
+      group.d[group.n] = descs[j];
+      group.d[group.n].task_begin = tasks;
+      tasks += descs[j].num_bags;
+      ++group.n;
+    }
+    group.total_tasks = tasks;
+    e = xse::LaunchPool(li, group, s, &launches);
+    if (e != cudaSuccess) return CudaError(e, "pooling launch");
+  }
+  g_last_launches = launches;
+
+  // Read back this call's status into stack memory and resolve it in the
+  // reference's order of checks.
+  alignas(16) unsigned char host_buf[kNoAllocStatusBytes];
+  e = cudaMemcpyAsync(host_buf, scratch, xse::DevStatusBytes(n),
+                      cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return CudaError(e, "scratch read-back");
+  const xse::DevStatus* st = reinterpret_cast<const xse::DevStatus*>(host_buf);
+  for (int32_t i = 0; i < n; ++i) {
+    const unsigned int flags = st->req[i].flags;
+    const char* msg = nullptr;
+    if (flags & xse::kErrBadOffsets) {
+      msg = "Row pointers must be non-negative and monotonic.";
+    } else if (flags & xse::kErrLastExceedsIds) {
+      msg = "Final row pointer exceeds embedding IDs size.";
+    } else if (flags & xse::kErrLastExceedsWeights) {
+      msg = "Final row pointer exceeds weights size.";
+    }
+    if (msg != nullptr) {
+      return SetError(XSE_INVALID_ARGUMENT, "FP32 embedding-bag request %d: %s",
+                      i, msg);
+    }
+    if (flags & xse::kErrBadId) {
+      const int64_t index = static_cast<int64_t>(~st->req[i].inv_min_bad_index);
+      int64_t id = 0;
+      if (descs[i].ids64) {
+        e = cudaMemcpy(&id, static_cast<const int64_t*>(descs[i].ids) + index,
+                       sizeof(id), cudaMemcpyDeviceToHost);
+      } else {
+        int32_t id32 = 0;
+        e = cudaMemcpy(&id32,
+                       static_cast<const int32_t*>(descs[i].ids) + index,
+                       sizeof(id32), cudaMemcpyDeviceToHost);
+        id = id32;
+      }
+      if (e != cudaSuccess) return CudaError(e, "id read-back");
+      return SetError(XSE_INVALID_ARGUMENT,
+                      "FP32 embedding-bag request %d: Embedding ID (%" PRId64
+                      ") at index %" PRId64 " is out of bounds [0, %" PRId64
+                      ").",
+                      i, id, index, tables[i]->vocab);
+    }
+  }
+  return Ok();
+}
