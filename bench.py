@@ -44,6 +44,9 @@ BATCH = 8192
 BAG = 20
 SEED = 0
 ROTATE = 8  # distinct input/output sets cycled between steps (> L2 in all)
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one step's
+# pooling kernels, from an ncu capture of this workload on a B200.
+POOL_DRAM_BYTES_PER_STEP = 314.98e6
 ROW_BYTES = DIM * 2
 WORKLOAD = ("multi_table_bf16: 8 bf16 tables x 500,000 x 128 per GPU, batch "
             "8192, 20 ids per bag, uniform ids, tables 0-3 per-id weighted "
@@ -484,13 +487,14 @@ def main():
                                                   1000.0) / 1e9,
         "roofline": {
             "bound": "hbm",
-            "kernel": "PoolVecKernel<bf16, G=16, V=1>",
+            "kernel": "PoolVecKernel<bf16, G=16, V=1, exact> (one launch "
+                      "per weighting mode)",
             "achieved": achieved,
             "peak": peak,
             "peak_kind": peak_kind,
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": None,
+            "traffic": POOL_DRAM_BYTES_PER_STEP,
             "algorithmic_bytes_per_launch": bytes_step,
             "avg_launch_ms": pool_avg_ms,
         },

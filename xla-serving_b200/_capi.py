@@ -147,6 +147,45 @@ SIGNATURES = {
 }
 
 
+HB_INVALID, HB_S32, HB_S64, HB_F32 = 0, 1, 2, 3
+HB_MAX_RANK = 8
+
+
+class HostBufferStruct(ctypes.Structure):
+  _fields_ = [
+      ("data", ctypes.c_void_p),
+      ("dtype", ctypes.c_int32),
+      ("rank", ctypes.c_int32),
+      ("dims", ctypes.c_int64 * HB_MAX_RANK),
+  ]
+
+
+_HBP = ctypes.POINTER(HostBufferStruct)
+_STRS = ctypes.POINTER(ctypes.c_char_p)
+
+# Operator layer (include/xse_ops.h).
+SIGNATURES.update({
+    "xse_host_buffer_alloc": (_I, [_I32, _I32, ctypes.POINTER(_I64), _HBP]),
+    "xse_host_buffer_free": (None, [_HBP]),
+    "xse_resource_load": (_I, [_STRS, _STRS, _I32, _I32, _P]),
+    "xse_resource_create": (_I, [_I32, _P]),
+    "xse_resource_destroy": (None, [_P]),
+    "xse_resource_engine": (_P, [_P]),
+    "xse_resource_embedding_dim": (_I, [_P, ctypes.c_char_p,
+                                        ctypes.POINTER(_I32)]),
+    "xse_resource_register_embedding_dim": (_I, [_P, ctypes.c_char_p, _I32]),
+    "xse_lookup_transform_create": (_I, [_P, _STRS, _I32, _I32, _STRS, _I32,
+                                         _I64, _P]),
+    "xse_lookup_transform_destroy": (None, [_P]),
+    "xse_lookup_transform_run": (_I, [_P, _HBP, _I32, _HBP, _I32, _HBP, _I32,
+                                      _HBP, _P]),
+    "xse_dense_lookup_transform_create": (_I, [_P, _STRS, _I32, _I64, _STRS,
+                                               _I32, _P]),
+    "xse_dense_lookup_transform_destroy": (None, [_P]),
+    "xse_dense_lookup_transform_run": (_I, [_P, _HBP, _I32, _HBP, _P]),
+})
+
+
 def _load():
   if not os.path.exists(LIB_PATH):
     raise ImportError(

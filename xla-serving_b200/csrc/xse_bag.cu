@@ -629,44 +629,53 @@ __global__ void __launch_bounds__(kThreads)
 // Group validation (ValidateEmbeddingBagInput, embedding_bag.cc:99-133).
 // Offsets must start >= 0 and never decrease; the final offset must not
 // exceed the ids (or weights); every id in [first, last) must be in
-// [0, vocab). One work item per offset and per id position, consecutive
-// items on consecutive threads (coalesced); each thread keeps the first and
-// last offsets of the request it is in.
+// [0, vocab). A request's offsets followed by its id positions are cut into
+// chunks of kValidateChunk elements; a warp checks one chunk, lane l taking
+// elements l, l+32, ... (coalesced), and looks up the chunk's request once.
+constexpr int kValidateChunk = 256;
+
 __global__ void __launch_bounds__(kThreads)
     ValidateKernel(const __grid_constant__ PoolParams p, int64_t total_work) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int t = -1;
-  int64_t first = 0, last = 0;
-  for (int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-       w < total_work; w += stride) {
-    const int t0 = t < 0 ? 0 : t;
-    const int tn = AdvanceWork(p, t0, w);
-    const BagDesc& d = p.d[tn];
-    if (tn != t) {
-      t = tn;
-      first = LoadIndex(d.offsets, d.offs64, 0);
-      last = LoadIndex(d.offsets, d.offs64, d.num_bags);
-    }
-    const int64_t i = w - d.work_begin;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+  int t = 0;
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) +
+                   threadIdx.x / 32;
+       c < total_work; c += warps) {
+    t = AdvanceWork(p, t, c);
+    const BagDesc& d = p.d[t];
     const int64_t num_offsets = d.num_bags + 1;
-    if (i < num_offsets) {
-      const int64_t cur = LoadIndex(d.offsets, d.offs64, i);
-      const bool bad =
-          i == 0 ? cur < 0 : LoadIndex(d.offsets, d.offs64, i - 1) > cur;
-      if (bad) RecordError(p.status, d.slot, kErrBadOffsets);
-      if (i == num_offsets - 1) {
-        if (cur > d.num_ids) RecordError(p.status, d.slot, kErrLastExceedsIds);
-        if (d.weights != nullptr && cur > d.num_weights) {
-          RecordError(p.status, d.slot, kErrLastExceedsWeights);
+    const int64_t elems = num_offsets + d.num_ids;
+    const int64_t i0 = (c - d.work_begin) * kValidateChunk;
+    const int64_t first = LoadIndex(d.offsets, d.offs64, 0);
+    const int64_t last = LoadIndex(d.offsets, d.offs64, d.num_bags);
+    unsigned int flags = 0;
+    int64_t bad_pos = -1;
+#pragma unroll 4
+    for (int k = 0; k < kValidateChunk / 32; ++k) {
+      const int64_t i = i0 + k * 32 + lane;
+      if (i >= elems) break;
+      if (i < num_offsets) {
+        const int64_t cur = LoadIndex(d.offsets, d.offs64, i);
+        if (i == 0 ? cur < 0 : LoadIndex(d.offsets, d.offs64, i - 1) > cur) {
+          flags |= kErrBadOffsets;
+        }
+        if (i == num_offsets - 1) {
+          if (cur > d.num_ids) flags |= kErrLastExceedsIds;
+          if (d.weights != nullptr && cur > d.num_weights) {
+            flags |= kErrLastExceedsWeights;
+          }
+        }
+      } else if (d.ids != nullptr) {
+        const int64_t pos = i - num_offsets;
+        if (pos >= first && pos < last && bad_pos < 0) {
+          const int64_t id = LoadIndex(d.ids, d.ids64, pos);
+          if (id < 0 || id >= d.vocab) bad_pos = pos;
         }
       }
-    } else if (d.ids != nullptr) {
-      const int64_t pos = i - num_offsets;
-      if (pos >= first && pos < last) {
-        const int64_t id = LoadIndex(d.ids, d.ids64, pos);
-        if (id < 0 || id >= d.vocab) RecordBadId(p.status, d.slot, pos);
-      }
     }
+    if (flags != 0) RecordError(p.status, d.slot, flags);
+    if (bad_pos >= 0) RecordBadId(p.status, d.slot, bad_pos);
   }
 }
 
@@ -803,7 +812,7 @@ int64_t TasksFor(const Layout& layout, int64_t num_bags) {
 }
 
 int64_t ValidationWork(int64_t num_bags, int64_t num_ids) {
-  return num_bags + 1 + num_ids;
+  return (num_bags + 1 + num_ids + kValidateChunk - 1) / kValidateChunk;
 }
 
 cudaError_t LaunchPool(const Layout& layout, const PoolParams& p,
@@ -820,7 +829,7 @@ cudaError_t LaunchPool(const Layout& layout, const PoolParams& p,
 cudaError_t LaunchValidate(const PoolParams& p, int64_t total_work,
                            cudaStream_t stream) {
   if (total_work <= 0) return cudaSuccess;
-  const int grid = GridFor(ValidateKernel, total_work, kThreads);
+  const int grid = GridFor(ValidateKernel, total_work, kThreads / 32);
   ValidateKernel<<<grid, kThreads, 0, stream>>>(p, total_work);
   return cudaGetLastError();
 }

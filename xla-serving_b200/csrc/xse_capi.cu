@@ -62,6 +62,16 @@ int CudaError(cudaError_t e, const char* what) {
   return SetError(XSE_INTERNAL, "%s: %s", what, cudaGetErrorString(e));
 }
 
+}  // namespace
+
+namespace xse {
+void SetLastErrorMessage(const char* message) {
+  g_last_error = message != nullptr ? message : "";
+}
+}  // namespace xse
+
+namespace {
+
 struct Table {
   std::string name;
   int32_t dtype = 0, combine = 1, dim = 0;

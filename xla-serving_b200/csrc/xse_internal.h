@@ -101,6 +101,9 @@ cudaError_t LaunchPool(const Layout& layout, const PoolParams& p,
 cudaError_t LaunchInterleaveScaleBias(const float* scale, const float* bias,
                                       float2* out, int64_t n,
                                       cudaStream_t stream);
+// Sets the calling thread's message returned by xse_last_error().
+void SetLastErrorMessage(const char* message);
+
 cudaError_t LaunchDotInteraction(const float* dense, const float* pooled,
                                  int64_t batch, int num_tables, int dim,
                                  float* out, cudaStream_t stream);

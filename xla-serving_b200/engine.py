@@ -96,16 +96,27 @@ class EmbeddingEngine:
   def __init__(self, device=0):
     self.device = device
     self._handle = ctypes.c_void_p()
+    self._owned = True
     opts = C.EngineOptions(device=device, reserved=0)
     C.check(C.lib.xse_engine_create(ctypes.byref(opts),
                                     ctypes.byref(self._handle)))
     self._adopted = {}  # table name -> tensors kept alive
 
+  @classmethod
+  def borrow(cls, handle, device=0):
+    """A non-owning handle on an engine owned elsewhere (a resource's)."""
+    self = cls.__new__(cls)
+    self.device = device
+    self._handle = ctypes.c_void_p(handle)
+    self._owned = False
+    self._adopted = {}
+    return self
+
   def close(self):
-    if self._handle:
+    if self._handle and self._owned:
       C.lib.xse_engine_destroy(self._handle)
-      self._handle = ctypes.c_void_p()
-      self._adopted.clear()
+    self._handle = ctypes.c_void_p()
+    self._adopted.clear()
 
   def __del__(self):
     try:
