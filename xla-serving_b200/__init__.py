@@ -8,6 +8,7 @@ fails if the CUDA library is missing.
 """
 
 from . import _capi
+from . import ops
 from ._capi import XseError
 from .engine import (BagRequest, EmbeddingEngine, Status, dot_interaction,
                      last_launch_count, stream_handle)

@@ -158,6 +158,16 @@ bool Uninitialized(const xse_host_buffer& b) {
 
 size_t AlignUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// True for page-locked host memory (copied by DMA without staging).
+bool IsPinned(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();  // clear the sticky-free error of the query
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
 // A device arena that only grows (reused across calls of one operator).
 struct DeviceArena {
   int device = 0;
@@ -622,23 +632,33 @@ int RunGroup(xse_engine* engine, Staging* staging,
     return Fail(XSE_RESOURCE_EXHAUSTED, "pinned staging allocation failed");
   }
   char* host_in = static_cast<char*>(in_block->ptr);
-  for (size_t i = 0; i < n; ++i) {
-    const Prepared& p = prep[i];
-    if (p.num_ids > 0) {
-      std::memcpy(host_in + ids_at[i], p.ids,
-                  p.num_ids * (p.ids_type == XSE_INDEX_I64 ? 8 : 4));
-    }
-    if (p.num_row_pointers > 0) {
-      std::memcpy(host_in + rp_at[i], p.row_pointers, p.num_row_pointers * 4);
-    }
-    if (p.num_weights > 0) {
-      std::memcpy(host_in + w_at[i], p.weights, p.num_weights * 4);
-    }
-  }
   char* dev_in = static_cast<char*>(staging->dev.ptr);
   char* dev_out = dev_in + AlignUp(in_bytes, 256);
-  cudaError_t e = cudaMemcpyAsync(dev_in, host_in, in_bytes,
-                                  cudaMemcpyHostToDevice, stream);
+  // Inputs already in pinned memory go straight to the device; the others
+  // are gathered into the pinned staging block and sent in one transfer.
+  cudaError_t e = cudaSuccess;
+  size_t lo = SIZE_MAX, hi = 0;
+  auto stage = [&](const void* src, size_t at, size_t bytes) {
+    if (bytes == 0 || e != cudaSuccess) return;
+    if (IsPinned(src)) {
+      e = cudaMemcpyAsync(dev_in + at, src, bytes, cudaMemcpyHostToDevice,
+                          stream);
+    } else {
+      std::memcpy(host_in + at, src, bytes);
+      lo = std::min(lo, at);
+      hi = std::max(hi, at + bytes);
+    }
+  };
+  for (size_t i = 0; i < n; ++i) {
+    const Prepared& p = prep[i];
+    stage(p.ids, ids_at[i], p.num_ids * (p.ids_type == XSE_INDEX_I64 ? 8 : 4));
+    stage(p.row_pointers, rp_at[i], p.num_row_pointers * 4);
+    stage(p.weights, w_at[i], p.num_weights * 4);
+  }
+  if (e == cudaSuccess && hi > lo) {
+    e = cudaMemcpyAsync(dev_in + lo, host_in + lo, hi - lo,
+                        cudaMemcpyHostToDevice, stream);
+  }
   std::vector<xse_bag_request> reqs(n);
   for (size_t i = 0; i < n; ++i) {
     const Prepared& p = prep[i];

@@ -71,8 +71,53 @@ def _buffer_array(items):
   return arr, bufs
 
 
-def _take_outputs(outs, n):
-  """Copies the library's pinned output buffers into numpy and frees them."""
+class PinnedBuffer(HostBuffer):
+  """A host buffer in the library's pinned memory, viewed as numpy.
+
+  Inputs in pinned memory are copied to the device by DMA without the
+  operators' host-side staging copy; operator outputs are pinned buffers.
+  Free with close() (the numpy view dies with it).
+  """
+
+  def __init__(self, shape=None, dtype=np.float32, struct=None):
+    # pylint: disable=super-init-not-called
+    if struct is None:
+      shape = tuple(int(d) for d in shape)
+      struct = C.HostBufferStruct()
+      dims = (ctypes.c_int64 * max(len(shape), 1))(*shape)
+      C.check(C.lib.xse_host_buffer_alloc(_NP_TO_HB[np.dtype(dtype)],
+                                          len(shape), dims,
+                                          ctypes.byref(struct)))
+    self.struct = struct
+    shape = tuple(struct.dims[k] for k in range(struct.rank))
+    dtype = _HB_TO_NP[struct.dtype]
+    count = int(np.prod(shape)) if shape else 1
+    if struct.data and count:
+      raw = (ctypes.c_char * (count * np.dtype(dtype).itemsize)).from_address(
+          struct.data)
+      self.array = np.frombuffer(raw, dtype=dtype, count=count).reshape(shape)
+    else:
+      self.array = np.zeros(shape, dtype=dtype)
+
+  def close(self):
+    if self.struct is not None and self.struct.data:
+      self.array = None
+      C.lib.xse_host_buffer_free(ctypes.byref(self.struct))
+    self.struct = None
+
+  def __del__(self):
+    try:
+      self.close()
+    except Exception:  # pylint: disable=broad-except
+      pass
+
+
+def _take_outputs(outs, n, copy=True):
+  """Copies the library's pinned output buffers into numpy and frees them;
+  with copy=False returns them as PinnedBuffer objects instead."""
+  if not copy:
+    return [PinnedBuffer(struct=C.HostBufferStruct.from_buffer_copy(outs[i]))
+            for i in range(n)]
   results = []
   for i in range(n):
     o = outs[i]
@@ -239,8 +284,10 @@ class CpuEmbeddingLookupTransform:
         1 if dense_lookup else 0, _names(outputs), len(outputs),
         embedding_dim, ctypes.byref(self._handle)))
 
-  def __call__(self, ids, row_pointers=(), weights=(), *, stream=None
-               ) -> List[np.ndarray]:
+  def __call__(self, ids, row_pointers=(), weights=(), *, stream=None,
+               copy=True) -> List[np.ndarray]:
+    """Pooled [batch, dim] float32 outputs, one per feature. copy=False
+    returns the pinned outputs as PinnedBuffer objects (caller closes)."""
     ids_arr, keep_i = _buffer_array(ids)
     rp_arr, keep_r = _buffer_array(row_pointers)
     w_arr, keep_w = _buffer_array(weights)
@@ -251,7 +298,7 @@ class CpuEmbeddingLookupTransform:
         len(keep_w), outs, stream_handle(stream))
     del keep_i, keep_r, keep_w
     C.check(rc)
-    return _take_outputs(outs, n)
+    return _take_outputs(outs, n, copy)
 
   def close(self):
     if self._handle:
@@ -283,7 +330,8 @@ class DenseCpuEmbeddingLookupTransform:
         resource.handle, _names(self.feature_names), len(self.feature_names),
         pad_value, _names(outputs), len(outputs), ctypes.byref(self._handle)))
 
-  def __call__(self, dense_ids, *, stream=None) -> List[np.ndarray]:
+  def __call__(self, dense_ids, *, stream=None, copy=True
+               ) -> List[np.ndarray]:
     if not isinstance(dense_ids, (list, tuple)):
       dense_ids = [dense_ids]
     arr, keep = _buffer_array(dense_ids)
@@ -293,7 +341,7 @@ class DenseCpuEmbeddingLookupTransform:
                                               outs, stream_handle(stream))
     del keep
     C.check(rc)
-    return _take_outputs(outs, n)
+    return _take_outputs(outs, n, copy)
 
   def close(self):
     if self._handle:
