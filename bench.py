@@ -184,18 +184,29 @@ def sum_over_ranks(value, world):
 
 
 class Workload:
-  """Tables, rotating inputs and outputs of one rank, on its GPU."""
+  """Tables, rotating inputs and outputs of one rank, on its GPU.
 
-  def __init__(self, xse, rank, world):
-    from xla_serving_b200 import synth  # pylint: disable=import-outside-toplevel
+  With N ranks the 8N tables are placed table-wise (global table t on rank
+  t mod N, so each rank holds 8); each rank pools its tables for the whole
+  batch and the exchange returns every sample block to its owner."""
+
+  def __init__(self, xse, rank, world, exchange="a2a"):
+    from xla_serving_b200 import sharding, synth  # pylint: disable=import-outside-toplevel
     self.xse = xse
     self.world = world
     self.engine = xse.EmbeddingEngine(torch.cuda.current_device())
-    self.specs = synth.multi_table_specs()
+    self.plan = sharding.ShardPlan(world, rank)
+    total = NUM_TABLES * world
+    self.global_tables = self.plan.tables_of(rank, total)
+    specs = synth.multi_table_specs()
+    self.specs = []
     self.tables = []
-    for k, spec in enumerate(self.specs):
-      g = rank * NUM_TABLES + k
+    for k, g in enumerate(self.global_tables):
+      spec = specs[k]
+      spec = synth.TableSpec(f"table_{g}", spec.vocab, spec.dim, spec.dtype,
+                             spec.combine, spec.weighted)
       rows, _, _ = synth.synth_table(xse._capi.DT_BF16, VOCAB, DIM, SEED, g)
+      self.specs.append(spec)
       self.tables.append(rows)
       self.engine.add_table(spec.name, rows, spec.combine, adopt=True)
       self.engine.register_feature(spec.name, spec.name)
@@ -203,16 +214,25 @@ class Workload:
     for v in range(ROTATE):
       batch = []
       for k, spec in enumerate(self.specs):
-        batch.append(synth.synth_batch(spec, rank * NUM_TABLES + k, BATCH,
+        batch.append(synth.synth_batch(spec, self.global_tables[k], BATCH,
                                        BAG, BAG, SEED, 0.0, variant=v))
       self.inputs.append(batch)
-    self.pooled = [torch.empty((BATCH, NUM_TABLES, DIM), dtype=torch.float32,
-                               device="cuda") for _ in range(ROTATE)]
-    self.recv = ([torch.empty_like(p) for p in self.pooled]
-                 if world > 1 else None)
-    self.requests = [self._requests(self.inputs[v], self.pooled[v])
-                     for v in range(ROTATE)]
-    self.status = xse.Status(NUM_TABLES)
+    self.status = xse.Status(NUM_TABLES * world)
+    self.pooler = sharding.engine_pooler(self.engine, self.status)
+    if world == 1:
+      self.pooled = [torch.empty((BATCH, NUM_TABLES, DIM), dtype=torch.float32,
+                                 device="cuda") for _ in range(ROTATE)]
+      self.requests = [self._requests(self.inputs[v], self.pooled[v])
+                       for v in range(ROTATE)]
+    else:
+      self.exchange = sharding.TablewiseExchange(
+          self.plan, BATCH, total, DIM, self.pooler, device="cuda",
+          mode=exchange)
+      self.steps = []
+      for v in range(ROTATE):
+        feats = [(spec.name, fb.ids, fb.offsets, fb.weights)
+                 for spec, fb in zip(self.specs, self.inputs[v])]
+        self.steps.append(self.exchange.schedule(feats))
     torch.cuda.synchronize()
 
   def _requests(self, batch, pooled):
@@ -226,14 +246,214 @@ class Workload:
 
   def step(self, i):
     v = i % ROTATE
-    self.engine.execute_batch(self.requests[v], status=self.status)
-    launches = self.xse.last_launch_count()
-    if self.world > 1:
-      dist.all_to_all_single(self.recv[v], self.pooled[v])
-    return launches
+    before = self.pooler.launches
+    if self.world == 1:
+      self.pooler(self.requests[v])
+    else:
+      self.exchange.run(self.steps[v])
+    return self.pooler.launches - before
 
   def ids_per_step(self):
     return NUM_TABLES * BATCH * BAG
+
+  def close(self):
+    if self.world > 1:
+      self.exchange.check()
+      self.exchange.close()
+    self.status.close()
+    self.engine.close()
+
+
+# DLRM forward workload: 26 fp32 tables x 128, rows log-uniform in
+# [1e4, 1e7], batch 16384, bag lengths U[1,100], Zipf(1.05) ids, sum pooling,
+# 13 dense features N(0,1), bottom MLP 13-512-256-128, dot interaction (479),
+# top MLP 479-1024-1024-512-256-1 with sigmoid.
+DLRM_TABLES = 26
+DLRM_DIM = 128
+DLRM_BATCH = 16384
+DLRM_LEN = (1, 100)
+DLRM_ALPHA = 1.05
+DLRM_ROTATE = 4
+DLRM_TABLE_STREAM = 100  # synth table-stream offset (independent of above)
+DLRM_WORKLOAD = ("dlrm_forward: 26 fp32 tables x 128 (rows log-uniform in "
+                 "[1e4, 1e7]), batch 16384, bag lengths U[1,100], Zipf(1.05) "
+                 "ids, sum pooling; 13 dense features N(0,1); bottom MLP "
+                 "13-512-256-128 ReLU; dot interaction 128+351=479; top MLP "
+                 "479-1024-1024-512-256-1 sigmoid; fp32")
+
+
+class DlrmWorkload:
+  """One DLRM forward per step on this rank's GPU (a full replica: every
+  rank holds all 26 tables and runs its own batch)."""
+
+  def __init__(self, xse, rank):
+    from xla_serving_b200 import dlrm, synth  # pylint: disable=import-outside-toplevel
+    self.xse = xse
+    self.engine = xse.EmbeddingEngine(torch.cuda.current_device())
+    self.rows = synth.log_uniform_rows(DLRM_TABLES, 1e4, 1e7, SEED)
+    names, self.tables = [], []
+    for t in range(DLRM_TABLES):
+      rows, _, _ = synth.synth_table(xse._capi.DT_F32, self.rows[t], DLRM_DIM,
+                                     SEED, DLRM_TABLE_STREAM + t)
+      name = f"sparse_{t}"
+      self.tables.append(rows)
+      self.engine.add_table(name, rows, "SUM", adopt=True)
+      self.engine.register_feature(name, name)
+      names.append(name)
+    self.model = dlrm.DLRM(self.engine, names, dim=DLRM_DIM, seed=SEED)
+    gen = torch.Generator(device="cuda").manual_seed(SEED + rank)
+    self.sets = []
+    self.nnz = []
+    for v in range(DLRM_ROTATE):
+      ids, offsets = [], []
+      for t in range(DLRM_TABLES):
+        spec = synth.TableSpec(names[t], self.rows[t], DLRM_DIM,
+                               xse._capi.DT_F32, "SUM")
+        fb = synth.synth_batch(spec, DLRM_TABLE_STREAM + 64 * rank + t,
+                               DLRM_BATCH, DLRM_LEN[0], DLRM_LEN[1], SEED,
+                               DLRM_ALPHA, variant=v)
+        ids.append(fb.ids)
+        offsets.append(fb.offsets)
+      reqs, _ = self.model.requests(ids, offsets)
+      dense = torch.randn((DLRM_BATCH, 13), generator=gen, device="cuda")
+      self.sets.append((dense, reqs, ids, offsets))
+      self.nnz.append(sum(int(i.numel()) for i in ids))
+    self.status = xse.Status(DLRM_TABLES)
+    torch.cuda.synchronize()
+
+  def step(self, i):
+    dense, reqs, _, _ = self.sets[i % DLRM_ROTATE]
+    self.model.engine.execute_batch(reqs, status=self.status)
+    launches = self.xse.last_launch_count()
+    self.model.tower.forward(dense, self.model.pooled_buffer(DLRM_BATCH))
+    # Own kernels of the tower: interaction and sigmoid head (the six ReLU
+    # layers are cuBLASLt GEMMs).
+    return launches + 2
+
+  def pool_bytes(self, v):
+    """Algorithmic bytes of variant v's pooled lookup."""
+    return (self.nnz[v] * (DLRM_DIM * 4 + 8) +
+            (DLRM_BATCH + 1) * 8 * DLRM_TABLES +
+            DLRM_BATCH * DLRM_TABLES * DLRM_DIM * 4)
+
+  def close(self):
+    self.status.close()
+    self.engine.close()
+
+
+class DlrmHostInputs:
+  """End-to-end DLRM forward through DLRM.forward with host inputs: per step
+  the ids, offsets and dense features are copied from pinned host memory
+  into the device tensors the requests point at, and the predictions are
+  read back into pinned host memory."""
+
+  def __init__(self, wl):
+    self.wl = wl
+    self.host = []
+    for dense, _, ids, offsets in wl.sets:
+      self.host.append(([x.cpu().pin_memory() for x in ids],
+                        [x.cpu().pin_memory() for x in offsets],
+                        dense.cpu().pin_memory()))
+    self.h2d_bytes = sum(x.numel() * x.element_size()
+                         for lst in self.host[0][:2] for x in lst)
+    self.h2d_bytes += self.host[0][2].numel() * 4
+    self.pred = torch.empty(DLRM_BATCH, dtype=torch.float32).pin_memory()
+    self.d2h_bytes = DLRM_BATCH * 4
+
+  def step(self, i):
+    v = i % DLRM_ROTATE
+    dense, reqs, ids, offsets = self.wl.sets[v]
+    h_ids, h_offs, h_dense = self.host[v]
+    for dst, src in zip(ids, h_ids):
+      dst.copy_(src, non_blocking=True)
+    for dst, src in zip(offsets, h_offs):
+      dst.copy_(src, non_blocking=True)
+    dense.copy_(h_dense, non_blocking=True)
+    pred = self.wl.model.forward(dense, requests=reqs)
+    self.pred.copy_(pred, non_blocking=True)
+    torch.cuda.current_stream().synchronize()
+
+
+def measure_dlrm(xse, args, world, local):
+  """Samples/s of the DLRM forward (whole job: every rank runs its own
+  batch), its pooled-lookup roofline and its end-to-end rate."""
+  wl = DlrmWorkload(xse, int(os.environ.get("RANK", "0")))
+  host = DlrmHostInputs(wl)
+  for i in range(max(args.warmup, 3)):
+    wl.step(i)
+  wl.status.wait()
+  torch.cuda.synchronize()
+  barrier(world, local)
+  stream = torch.cuda.current_stream()
+  start = torch.cuda.Event(enable_timing=True)
+  end = torch.cuda.Event(enable_timing=True)
+  wl.engine.set_profiling(True)
+  launches = 0
+  start.record(stream)
+  for i in range(args.dlrm_steps):
+    launches += wl.step(i)
+  end.record(stream)
+  torch.cuda.synchronize()
+  barrier(world, local)
+  wl.status.wait()
+  ms = max_over_ranks(start.elapsed_time(end), world)
+  pool_ms, pool_n = wl.engine.profile_read()
+  wl.engine.set_profiling(False)
+  samples = sum_over_ranks(DLRM_BATCH * args.dlrm_steps, world)
+  ids = sum_over_ranks(sum(wl.nnz[i % DLRM_ROTATE]
+                           for i in range(args.dlrm_steps)), world)
+  pool_bytes = sum(wl.pool_bytes(i % DLRM_ROTATE)
+                   for i in range(args.dlrm_steps)) / args.dlrm_steps
+  pool_avg = pool_ms / max(pool_n, 1)
+  peak, peak_kind = measured_peaks()
+  for i in range(3):
+    host.step(i)
+  barrier(world, local)
+  e_start = torch.cuda.Event(enable_timing=True)
+  e_end = torch.cuda.Event(enable_timing=True)
+  e_steps = max(args.dlrm_steps // 4, 5)
+  e_start.record(stream)
+  for i in range(e_steps):
+    host.step(i)
+  e_end.record(stream)
+  torch.cuda.synchronize()
+  barrier(world, local)
+  e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+  e_samples = sum_over_ranks(DLRM_BATCH * e_steps, world)
+  result = {
+      "metric": "DLRM-fwd samples/sec",
+      "value": samples / (ms / 1000.0),
+      "unit": "samples/s",
+      "n_gpus": world,
+      "steps": args.dlrm_steps,
+      "ms_per_step": ms / args.dlrm_steps,
+      "ids_per_s": ids / (ms / 1000.0),
+      "dtype": "fp32",
+      "parallelism": ("single GPU" if world == 1 else
+                      f"{world} data-parallel replicas (tables replicated, "
+                      "no collective)"),
+      "config": {"workload": DLRM_WORKLOAD, "batch_per_gpu": DLRM_BATCH,
+                 "table_rows": wl.rows,
+                 "l2": f"{sum(wl.rows) * DLRM_DIM * 4 / 1e9:.1f} GB of tables "
+                       f"and {DLRM_ROTATE} rotating input sets per GPU"},
+      "pool_roofline": {
+          "bound": "hbm", "achieved": pool_bytes / (pool_avg / 1000.0) / 1e9,
+          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+          "frac": pool_bytes / (pool_avg / 1000.0) / 1e9 / peak,
+          "algorithmic_bytes_per_launch": pool_bytes,
+          "avg_launch_ms": pool_avg,
+          "note": "Zipf(1.05) hot rows hit L2, so algorithmic GB/s can "
+                  "exceed DRAM bandwidth"},
+      "gpu_launches": launches,
+      "e2e": {"value": e_samples / (e_ms / 1000.0), "unit": "samples/s",
+              "h2d_bytes_per_step": host.h2d_bytes,
+              "d2h_bytes_per_step": host.d2h_bytes,
+              "path": "DLRM.forward with ids, offsets and dense features "
+                      "copied from pinned host memory and predictions "
+                      "copied back, synchronous per step"},
+  }
+  wl.close()
+  return result
 
 
 class HostInputs:
@@ -391,6 +611,14 @@ def main():
   ap.add_argument("--e2e-steps", type=int, default=200)
   ap.add_argument("--cpu-seconds", type=float, default=10.0)
   ap.add_argument("--no-cpu-baseline", action="store_true")
+  ap.add_argument("--exchange", default="a2a",
+                  choices=["a2a", "pipelined", "peer"],
+                  help="N>1: one NCCL all-to-all after pooling, per-block "
+                       "NCCL send/recv overlapped with the pooling, or "
+                       "pooled rows stored into the owners' buffers over "
+                       "NVLink by the pooling kernel")
+  ap.add_argument("--dlrm-steps", type=int, default=40,
+                  help="timed DLRM forward steps (0: skip the DLRM forward)")
   args = ap.parse_args()
   if args.warmup < 3:
     args.warmup = 3
@@ -401,7 +629,7 @@ def main():
   world, rank, local = init_distributed()
   torch.cuda.set_device(local)
   xse = load_package()
-  wl = Workload(xse, rank, world)
+  wl = Workload(xse, rank, world, args.exchange)
   host = HostInputs(wl)
   clocks = ClockSampler(local)
   clocks.start()
@@ -443,6 +671,9 @@ def main():
   torch.cuda.synchronize()
   barrier(world, local)
   e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end), world)
+  dlrm_result = None
+  if args.dlrm_steps > 0:
+    dlrm_result = measure_dlrm(xse, args, world, local)
   clock_info = clocks.stop()
 
   ids_total = sum_over_ranks(wl.ids_per_step() * args.steps, world)
@@ -481,10 +712,18 @@ def main():
             "tables_total": NUM_TABLES * world,
             "accumulate": "fp32",
             "parallelism": ("single GPU" if world == 1 else
-                            f"table-wise x{world}, NCCL all-to-all of pooled "
-                            "outputs"),
+                            f"table-wise x{world} (table t on rank t mod "
+                            f"{world}), pooled sample blocks returned to "
+                            "their owners by " +
+                            {"pipelined": "per-block NCCL send/recv "
+                                          "overlapped with the pooling",
+                             "a2a": "one NCCL all-to-all",
+                             "peer": "the pooling kernel's own stores into "
+                                     "the owners' buffers over NVLink (CUDA "
+                                     "IPC) and a flag barrier"}[
+                                         args.exchange]),
             "l2": "inputs larger than L2: 1.0 GB of tables per GPU and "
-                  f"{ROTATE} rotating id/offset/weight/output sets",
+                  f"{ROTATE} rotating id/offset/weight sets",
             "validation": "strict (separate validation kernel each step)",
         },
         "hbm_gbs_algorithmic_step": bytes_step / (elapsed_ms / args.steps /
@@ -513,13 +752,13 @@ def main():
                     "call, synchronous per step",
         },
         "gpu_launches": launches,
+        "dlrm_forward": dlrm_result,
         "cpu_baseline": base,
         "clocks": clock_info,
     }
     print(json.dumps(line), flush=True)
   host.close()
-  wl.status.close()
-  wl.engine.close()
+  wl.close()
   if world > 1:
     dist.destroy_process_group()
 

@@ -8,7 +8,9 @@ fails if the CUDA library is missing.
 """
 
 from . import _capi
+from . import dlrm
 from . import ops
+from . import sharding
 from ._capi import XseError
 from .engine import (BagRequest, EmbeddingEngine, Status, dot_interaction,
                      last_launch_count, stream_handle)

@@ -186,6 +186,36 @@ SIGNATURES.update({
 })
 
 
+# DLRM dense tower (include/xse_dlrm.h).
+ACT_NONE, ACT_RELU, ACT_SIGMOID = 0, 1, 2
+MATH_FP32, MATH_BF16X9, MATH_TF32 = 0, 1, 2
+SIGNATURES.update({
+    "xse_linear_forward": (_I, [_P, _I64, _I32, _I64, _P, _P, _I32, _I32,
+                                _I32, _P, _I64, _P]),
+    "xse_dot_interaction_strided": (_I, [_P, _I64, _P, _I64, _I64, _I32, _I32,
+                                         _P, _I64, _P]),
+})
+
+
+# Peer-memory exchange (include/xse_peer.h).
+PEER_MAX_RANKS = 8
+
+
+class IpcHandle(ctypes.Structure):
+  _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
+SIGNATURES.update({
+    "xse_peer_group_create": (_I, [_I32, _I32, _I32, _I64, _P,
+                                   ctypes.POINTER(IpcHandle)]),
+    "xse_peer_group_connect": (_I, [_P, ctypes.POINTER(IpcHandle), _I32]),
+    "xse_peer_group_buffer": (_P, [_P, _I32]),
+    "xse_peer_group_barrier": (_I, [_P, _I64, _P]),
+    "xse_peer_group_check": (_I, [_P, _P]),
+    "xse_peer_group_destroy": (None, [_P]),
+})
+
+
 def _load():
   if not os.path.exists(LIB_PATH):
     raise ImportError(

@@ -24,6 +24,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "../../include/xse_dlrm.h"
 #include "../../include/xse_emb.h"
 #include "xse_internal.h"
 
@@ -68,6 +69,7 @@ namespace xse {
 void SetLastErrorMessage(const char* message) {
   g_last_error = message != nullptr ? message : "";
 }
+void SetLastLaunchCount(int32_t launches) { g_last_launches = launches; }
 }  // namespace xse
 
 namespace {
@@ -946,18 +948,39 @@ int xse_status_wait(xse_status* status, void* stream) {
 int xse_dot_interaction(const float* dense, const float* pooled,
                         int64_t batch, int32_t num_tables, int32_t dim,
                         float* out, void* stream) {
+  const int64_t rows = static_cast<int64_t>(num_tables) + 1;
+  return xse_dot_interaction_strided(
+      dense, dim, pooled, static_cast<int64_t>(num_tables) * dim, batch,
+      num_tables, dim, out, dim + rows * (rows - 1) / 2, stream);
+}
+
+int xse_dot_interaction_strided(const float* dense, int64_t dense_stride,
+                                const float* pooled, int64_t pooled_stride,
+                                int64_t batch, int32_t num_tables,
+                                int32_t dim, float* out, int64_t out_stride,
+                                void* stream) {
   g_last_launches = 0;
   if (batch < 0 || num_tables < 1 || dim < 1) {
     return SetError(XSE_INVALID_ARGUMENT,
                     "Interaction needs batch >= 0, at least one table and a "
                     "positive dimension.");
   }
+  const int64_t rows = static_cast<int64_t>(num_tables) + 1;
+  const int64_t width = dim + rows * (rows - 1) / 2;
+  if (dense_stride < dim || pooled_stride < static_cast<int64_t>(num_tables) * dim ||
+      out_stride < width) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Interaction strides must cover a row: dense >= %d, "
+                    "pooled >= %lld, out >= %lld.", dim,
+                    static_cast<long long>(num_tables) * dim,
+                    static_cast<long long>(width));
+  }
   if (batch > 0 && (dense == nullptr || pooled == nullptr || out == nullptr)) {
     return SetError(XSE_INVALID_ARGUMENT, "Interaction buffers must be non-null.");
   }
   const cudaError_t e = xse::LaunchDotInteraction(
-      dense, pooled, batch, num_tables, dim, out,
-      static_cast<cudaStream_t>(stream));
+      dense, dense_stride, pooled, pooled_stride, batch, num_tables, dim, out,
+      out_stride, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return CudaError(e, "interaction launch");
   g_last_launches = batch > 0 ? 1 : 0;
   return Ok();

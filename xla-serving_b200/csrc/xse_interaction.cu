@@ -43,8 +43,10 @@ __device__ __forceinline__ float ReduceScatter32(float (&v)[32]) {
 template <int R, int CPL>
 __global__ void __launch_bounds__(kInteractionThreads)
     DotInteractionKernel(const float* __restrict__ dense,
-                         const float* __restrict__ pooled, int64_t batch,
-                         float* __restrict__ out) {
+                         int64_t dense_stride,
+                         const float* __restrict__ pooled,
+                         int64_t pooled_stride, int64_t batch,
+                         float* __restrict__ out, int64_t out_stride) {
   constexpr int T = R - 1;
   constexpr int D = 32 * CPL;
   constexpr int P = R * (R - 1) / 2;
@@ -57,8 +59,8 @@ __global__ void __launch_bounds__(kInteractionThreads)
                    threadIdx.x / 32;
        b < batch; b += warps) {
     float z[R][CPL];
-    const float* dense_row = dense + b * D + lane * CPL;
-    const float* pooled_rows = pooled + b * T * D + lane * CPL;
+    const float* dense_row = dense + b * dense_stride + lane * CPL;
+    const float* pooled_rows = pooled + b * pooled_stride + lane * CPL;
 #pragma unroll
     for (int i = 0; i < R; ++i) {
       const float* src = i == 0 ? dense_row : pooled_rows + (i - 1) * D;
@@ -76,9 +78,10 @@ __global__ void __launch_bounds__(kInteractionThreads)
         for (int c = 0; c < CPL; ++c) z[i][c] = __ldg(src + c);
       }
     }
-    float* o = out + b * W;
+    float* o = out + b * out_stride;
 #pragma unroll
     for (int c = 0; c < CPL; ++c) o[lane * CPL + c] = z[0][c];
+    for (int64_t c = W + lane; c < out_stride; c += 32) o[c] = 0.0f;
 
     float v[32];
     int q = 0;
@@ -104,21 +107,25 @@ __global__ void __launch_bounds__(kInteractionThreads)
 }
 
 // Any shape: one thread per output element of a sample, row order as above.
-__global__ void DotInteractionGenericKernel(const float* __restrict__ dense,
-                                            const float* __restrict__ pooled,
-                                            int64_t batch, int num_tables,
-                                            int dim, float* __restrict__ out) {
+__global__ void DotInteractionGenericKernel(
+    const float* __restrict__ dense, int64_t dense_stride,
+    const float* __restrict__ pooled, int64_t pooled_stride, int64_t batch,
+    int num_tables, int dim, float* __restrict__ out, int64_t out_stride) {
   const int rows = num_tables + 1;
   const int64_t pairs = static_cast<int64_t>(rows) * (rows - 1) / 2;
   const int64_t width = dim + pairs;
-  const int64_t total = batch * width;
+  const int64_t total = batch * out_stride;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        e < total; e += stride) {
-    const int64_t b = e / width;
-    const int64_t k = e % width;
+    const int64_t b = e / out_stride;
+    const int64_t k = e % out_stride;
+    if (k >= width) {
+      out[e] = 0.0f;
+      continue;
+    }
     if (k < dim) {
-      out[e] = dense[b * dim + k];
+      out[e] = dense[b * dense_stride + k];
       continue;
     }
     // Decode pair index k - dim into (i, j), i < j, row-major.
@@ -129,9 +136,9 @@ __global__ void DotInteractionGenericKernel(const float* __restrict__ dense,
       ++i;
     }
     const int j = i + 1 + static_cast<int>(rem);
-    const float* zi = i == 0 ? dense + b * dim
-                             : pooled + (b * num_tables + i - 1) * dim;
-    const float* zj = pooled + (b * num_tables + j - 1) * dim;
+    const float* zi = i == 0 ? dense + b * dense_stride
+                             : pooled + b * pooled_stride + (i - 1) * dim;
+    const float* zj = pooled + b * pooled_stride + (j - 1) * dim;
     float s = 0.0f;
     for (int c = 0; c < dim; ++c) s = fmaf(zi[c], zj[c], s);
     out[e] = s;
@@ -140,28 +147,31 @@ __global__ void DotInteractionGenericKernel(const float* __restrict__ dense,
 
 }  // namespace
 
-cudaError_t LaunchDotInteraction(const float* dense, const float* pooled,
+cudaError_t LaunchDotInteraction(const float* dense, int64_t dense_stride,
+                                 const float* pooled, int64_t pooled_stride,
                                  int64_t batch, int num_tables, int dim,
-                                 float* out, cudaStream_t stream) {
+                                 float* out, int64_t out_stride,
+                                 cudaStream_t stream) {
   if (batch <= 0) return cudaSuccess;
   const bool aligned =
       ((reinterpret_cast<uintptr_t>(dense) |
-        reinterpret_cast<uintptr_t>(pooled)) & 15u) == 0;
+        reinterpret_cast<uintptr_t>(pooled)) & 15u) == 0 &&
+      dense_stride % 4 == 0 && pooled_stride % 4 == 0;
   if (aligned && num_tables == 26 && dim == 128) {
     const int64_t warps_per_block = kInteractionThreads / 32;
     int64_t blocks = (batch + warps_per_block - 1) / warps_per_block;
     if (blocks > 148 * 64) blocks = 148 * 64;
     DotInteractionKernel<27, 4><<<static_cast<int>(blocks),
                                   kInteractionThreads, 0, stream>>>(
-        dense, pooled, batch, out);
+        dense, dense_stride, pooled, pooled_stride, batch, out, out_stride);
     return cudaGetLastError();
   }
-  const int64_t rows = num_tables + 1;
-  const int64_t total = batch * (dim + rows * (rows - 1) / 2);
+  const int64_t total = batch * out_stride;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
   DotInteractionGenericKernel<<<static_cast<int>(blocks), 256, 0, stream>>>(
-      dense, pooled, batch, num_tables, dim, out);
+      dense, dense_stride, pooled, pooled_stride, batch, num_tables, dim, out,
+      out_stride);
   return cudaGetLastError();
 }
 

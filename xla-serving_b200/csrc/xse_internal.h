@@ -104,9 +104,14 @@ cudaError_t LaunchInterleaveScaleBias(const float* scale, const float* bias,
 // Sets the calling thread's message returned by xse_last_error().
 void SetLastErrorMessage(const char* message);
 
-cudaError_t LaunchDotInteraction(const float* dense, const float* pooled,
+cudaError_t LaunchDotInteraction(const float* dense, int64_t dense_stride,
+                                 const float* pooled, int64_t pooled_stride,
                                  int64_t batch, int num_tables, int dim,
-                                 float* out, cudaStream_t stream);
+                                 float* out, int64_t out_stride,
+                                 cudaStream_t stream);
+
+// Sets what xse_last_launch_count() reports for this thread.
+void SetLastLaunchCount(int32_t launches);
 
 }  // namespace xse
 

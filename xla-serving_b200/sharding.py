@@ -1,0 +1,409 @@
+"""Embedding tables sharded across the GPUs of one node, one process per GPU.
+
+The reference engine keeps every table in one host's memory
+(data/cpu_embedding/cc/cpu_embedding_engine.h:41-103); tables larger than one
+GPU's HBM are split here in the two standard ways, with the pooled outputs
+exchanged over NVLink by NCCL (through torch.distributed):
+
+* Table-wise: table t lives on rank t mod W. The ids of a table are given to
+  its owner for the whole batch (model-parallel input layout). Each rank pools
+  its T_local tables for all B samples into blocks [W][B/W][T_local][D], block
+  s holding the samples owned by rank s (samples [s B/W, (s+1) B/W)); an
+  all-to-all returns every block to its owner, which ends with the blocks
+  [B/W][T_q][D] of every source rank q (row k of block q is global table
+  q + k W).
+* Row-wise: every table's rows are split into W contiguous windows of the
+  (permuted) row space; rank r holds rows [r V / W, (r+1) V / W) of each
+  table and sees all ids. Ids outside the window are skipped by the pooling
+  kernel, while bag lengths and weight sums still count every id, so the
+  per-rank partial sums add up to the full bag. A reduce-scatter (sum) leaves
+  rank r with recv[B/W][T][D] for its samples. Sums of partials differ from
+  the single-table CSR-order sum by rounding only.
+
+The exchanges are pipelined with the pooling: the table-wise path pools the
+block for rank r+j, hands it to NCCL (send to r+j, receive from r-j, the
+shifted pairwise schedule, deadlock-free) and pools the next block while it
+is in flight; the row-wise path splits the batch into chunks and
+reduce-scatters chunk c while chunk c+1 is pooled.
+
+A bag request over samples [b0, b1) of a CSR batch is the same ids and
+weights with the offsets slice [b0, b1] (absolute offsets, first entry may be
+above zero, as the reference's EmbeddingBagInput allows,
+data/cpu_embedding/cc/embedding_bag.h:66-72), so sample blocks need no copies.
+"""
+
+import ctypes
+import dataclasses
+from typing import Callable, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _capi as C
+from .engine import BagRequest, last_launch_count, stream_handle
+
+
+@dataclasses.dataclass(frozen=True)
+class ShardPlan:
+  """Placement of tables, rows and samples over `world` ranks."""
+
+  world: int
+  rank: int
+
+  def __post_init__(self):
+    if self.world < 1 or not 0 <= self.rank < self.world:
+      raise ValueError(f"bad rank {self.rank} of world {self.world}")
+
+  def table_owner(self, table: int) -> int:
+    return table % self.world
+
+  def tables_of(self, rank: int, num_tables: int) -> List[int]:
+    """Global indices of the tables rank `rank` holds (table-wise)."""
+    return list(range(rank, num_tables, self.world))
+
+  def row_window(self, vocab: int, rank: Optional[int] = None
+                 ) -> Tuple[int, int]:
+    """Rows [begin, end) of a `vocab`-row table held by `rank` (row-wise)."""
+    r = self.rank if rank is None else rank
+    return vocab * r // self.world, vocab * (r + 1) // self.world
+
+  def block_size(self, batch: int) -> int:
+    if batch % self.world:
+      raise ValueError(
+          f"batch {batch} must split evenly over {self.world} ranks")
+    return batch // self.world
+
+  def sample_block(self, batch: int, rank: int) -> Tuple[int, int]:
+    """Samples [begin, end) owned by `rank`."""
+    n = self.block_size(batch)
+    return rank * n, (rank + 1) * n
+
+
+def slice_request(req: BagRequest, bag_begin: int, bag_end: int,
+                  output: torch.Tensor, output_stride: int = 0) -> BagRequest:
+  """The request for bags [bag_begin, bag_end) of `req`, writing `output`."""
+  return BagRequest(req.feature_name, req.ids,
+                    req.offsets[bag_begin:bag_end + 1], output, req.weights,
+                    output_stride)
+
+
+Pooler = Callable[[Sequence[BagRequest]], None]
+
+
+class engine_pooler:  # pylint: disable=invalid-name
+  """A pooler running each group on `engine`. With a `status` the groups run
+  asynchronously (no host wait per group; read the result with
+  status.wait() after the exchange). `launches` counts the kernels the
+  groups launched."""
+
+  def __init__(self, engine, status=None, fused=False):
+    self.engine = engine
+    self.status = status
+    self.fused = fused
+    self.launches = 0
+
+  def __call__(self, reqs):
+    self.engine.execute_batch(reqs, status=self.status, fused=self.fused)
+    self.launches += last_launch_count()
+
+
+class DevicePointer:
+  """A raw device address standing in for a tensor as a bag request output
+  (a peer's buffer mapped into this process)."""
+
+  def __init__(self, address: int):
+    self.address = address
+
+  def data_ptr(self) -> int:
+    return self.address
+
+
+class _CudaArray:
+  """__cuda_array_interface__ over raw fp32 device memory, for torch views."""
+
+  def __init__(self, address, shape):
+    self.__cuda_array_interface__ = {
+        "shape": tuple(shape), "typestr": "<f4", "data": (address, False),
+        "version": 3, "strides": None}
+
+
+class PeerGroup:
+  """Buffers of all ranks mapped into every rank, plus a stream-ordered flag
+  barrier (include/xse_peer.h). Handles travel over torch.distributed."""
+
+  def __init__(self, plan: ShardPlan, nbytes: int, device: int, group=None):
+    self.plan = plan
+    self.nbytes = nbytes
+    self._handle = ctypes.c_void_p()
+    mine = C.IpcHandle()
+    C.check(C.lib.xse_peer_group_create(device, plan.world, plan.rank, nbytes,
+                                        ctypes.byref(self._handle),
+                                        ctypes.byref(mine)))
+    gathered = [None] * plan.world
+    dist.all_gather_object(gathered, bytes(mine.bytes), group=group)
+    handles = (C.IpcHandle * plan.world)()
+    for q, raw in enumerate(gathered):
+      ctypes.memmove(handles[q].bytes, raw, len(raw))
+    C.check(C.lib.xse_peer_group_connect(self._handle, handles, plan.world))
+    self.group = group
+
+  def address(self, rank: int) -> int:
+    return C.lib.xse_peer_group_buffer(self._handle, rank)
+
+  def local_view(self, offset_bytes: int, shape) -> torch.Tensor:
+    """fp32 tensor over this rank's buffer."""
+    return torch.as_tensor(
+        _CudaArray(self.address(self.plan.rank) + offset_bytes, shape),
+        device="cuda")
+
+  def barrier(self, stream=None, spin_limit=0):
+    C.check(C.lib.xse_peer_group_barrier(self._handle, spin_limit,
+                                         stream_handle(stream)))
+
+  def check(self, stream=None):
+    C.check(C.lib.xse_peer_group_check(self._handle, stream_handle(stream)))
+
+  def close(self):
+    if self._handle:
+      torch.cuda.synchronize()
+      dist.barrier(group=self.group)  # every rank is done with the others'
+      C.lib.xse_peer_group_destroy(self._handle)
+      self._handle = ctypes.c_void_p()
+
+
+MODES = ("a2a", "pipelined", "peer")
+
+
+class TablewiseExchange:
+  """Pools this rank's tables for the whole batch and returns each sample
+  block to its owning rank.
+
+  features (to schedule()): (feature name, ids, offsets, weights) of the
+  local tables, in local table order, each over the whole batch.
+  pool: runs a group of bag requests on the current stream
+  (engine_pooler(engine, status) on the GPU).
+  After run(), recv_from(q) is [B/W, T_q, D]: the pooled rows of rank q's
+  tables (global tables q, q + W, ...) for this rank's samples.
+
+  Modes:
+    a2a: one group of whole-batch requests into send, then one NCCL
+      all-to-all.
+    pipelined: a group per destination block, each handed to NCCL
+      send/recv (shifted pairwise schedule) while the next is pooled.
+    peer: one group whose requests write every block straight into its
+      owner's receive buffer over NVLink (CUDA IPC mappings), then one flag
+      barrier; receive buffers alternate between two slots so a step's
+      stores never overwrite the rows the previous step delivered.
+  """
+
+  def __init__(self, plan: ShardPlan, batch: int, num_tables: int, dim: int,
+               pool: Pooler, device=None, group=None, mode="a2a"):
+    if mode not in MODES:
+      raise ValueError(f"unknown exchange mode {mode!r}")
+    self.plan = plan
+    self.batch = batch
+    self.num_tables = num_tables
+    self.dim = dim
+    self.pool = pool
+    self.group = group
+    self.mode = mode
+    self.block = plan.block_size(batch)
+    w = plan.world
+    self.counts = [len(plan.tables_of(q, num_tables)) for q in range(w)]
+    self.num_local = self.counts[plan.rank]
+    self.recv_sizes = [self.block * c * dim for c in self.counts]
+    self.recv_offsets = [sum(self.recv_sizes[:q]) for q in range(w)]
+    total = self.block * num_tables * dim
+    self.peers = None
+    self.send = None
+    self._slot = 0
+    if mode == "peer" and w > 1:
+      dev = torch.cuda.current_device() if device is None else (
+          torch.device(device).index or torch.cuda.current_device())
+      self.peers = PeerGroup(plan, 2 * total * 4, dev, group)
+      self._slots = [self.peers.local_view(s * total * 4, (total,))
+                     for s in range(2)]
+    else:
+      self.send = torch.empty((w, self.block, self.num_local, dim),
+                              dtype=torch.float32, device=device)
+      self._slots = [torch.empty(total, dtype=torch.float32, device=device)]
+
+  @property
+  def recv(self) -> torch.Tensor:
+    return self._slots[self._slot]
+
+  def recv_from(self, q: int, slot: Optional[int] = None) -> torch.Tensor:
+    buf = self._slots[self._slot if slot is None else slot]
+    at = self.recv_offsets[q]
+    return buf[at:at + self.recv_sizes[q]].view(self.block, self.counts[q],
+                                                self.dim)
+
+  def sample_major(self, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The received rows as [B/W, T, D] in global table order."""
+    if out is None:
+      out = torch.empty((self.block, self.num_tables, self.dim),
+                        dtype=torch.float32, device=self.recv.device)
+    for q in range(self.plan.world):
+      out[:, q::self.plan.world, :] = self.recv_from(q)
+    return out
+
+  def block_requests(self, features, dest: int, out):
+    """Requests pooling the samples of rank `dest` into out, a [B/W, T_local,
+    D] tensor or the DevicePointer of one."""
+    b0, b1 = self.plan.sample_block(self.batch, dest)
+    row = self.num_local * self.dim
+    reqs = []
+    for k, (name, ids, offsets, weights) in enumerate(features):
+      base = BagRequest(name, ids, offsets, None, weights)
+      if isinstance(out, DevicePointer):
+        dst = DevicePointer(out.address + 4 * k * self.dim)
+      else:
+        dst = out[:, k, :]
+      reqs.append(slice_request(base, b0, b1, dst, row))
+    return reqs
+
+  def schedule(self, features):
+    """The request groups of one exchange, built once and reused by run().
+
+    a2a: [(None, whole-batch requests writing send)] (send [W][B/W][T_local]
+    [D] is [B][T_local][D] in sample order). pipelined: [(dest, requests)]
+    for rank+1, rank+2, ..., then the own block pooled straight into recv.
+    peer: one group per receive slot, each writing every rank's slot."""
+    if len(features) != self.num_local:
+      raise ValueError(f"rank {self.plan.rank} holds {self.num_local} tables, "
+                       f"got {len(features)} features")
+    w, r = self.plan.world, self.plan.rank
+    if w == 1:
+      return [(r, self.block_requests(features, r, self.recv_from(r)))]
+    if self.mode == "a2a":
+      whole = self.send.view(self.batch, self.num_local, self.dim)
+      reqs = [BagRequest(name, ids, offsets, whole[:, k, :], weights,
+                         self.num_local * self.dim)
+              for k, (name, ids, offsets, weights) in enumerate(features)]
+      return [(None, reqs)]
+    if self.mode == "pipelined":
+      steps = []
+      for j in range(1, w):
+        dest = (r + j) % w
+        steps.append((dest, self.block_requests(features, dest,
+                                                self.send[dest])))
+      steps.append((r, self.block_requests(features, r, self.recv_from(r))))
+      return steps
+    total = self.block * self.num_tables * self.dim
+    groups = []
+    for slot in range(2):
+      reqs = []
+      for dest in range(w):
+        # Rank dest's slot holds [q][B/W][T_q][D]; this rank writes block r.
+        at = 4 * (slot * total + self.recv_offsets[r])
+        reqs += self.block_requests(
+            features, dest, DevicePointer(self.peers.address(dest) + at))
+      groups.append((slot, reqs))
+    return groups
+
+  def run(self, steps):
+    """Pools and exchanges the groups of schedule(); on return the current
+    stream is ordered after the exchange (recv is ready for work queued on
+    it)."""
+    w, r = self.plan.world, self.plan.rank
+    if w == 1:
+      for _, reqs in steps:
+        self.pool(reqs)
+      return self.recv
+    if self.mode == "a2a":
+      self.pool(steps[0][1])
+      send_size = self.block * self.num_local * self.dim
+      dist.all_to_all_single(self.recv, self.send.view(-1),
+                             output_split_sizes=self.recv_sizes,
+                             input_split_sizes=[send_size] * w,
+                             group=self.group)
+      return self.recv
+    if self.mode == "pipelined":
+      works = []
+      for j, (dest, reqs) in enumerate(steps):
+        self.pool(reqs)
+        if dest != r:
+          src = (r - (j + 1)) % w
+          ops = [dist.P2POp(dist.isend, self.send[dest], dest, self.group),
+                 dist.P2POp(dist.irecv, self.recv_from(src), src, self.group)]
+          works.extend(dist.batch_isend_irecv(ops))
+      for work in works:
+        work.wait()
+      return self.recv
+    slot = 1 - self._slot
+    self.pool(steps[slot][1])
+    self.peers.barrier()
+    self._slot = slot
+    return self.recv
+
+  def check(self):
+    """Raises if a peer barrier gave up waiting (peer mode)."""
+    if self.peers is not None:
+      self.peers.check()
+
+  def close(self):
+    if self.peers is not None:
+      self._slots = []
+      self.peers.close()
+      self.peers = None
+
+
+class RowwiseExchange:
+  """Pools every table against this rank's row windows into partial sums
+  and reduce-scatters them so that each rank ends with its samples' full
+  pooled rows: recv [B/W, T, D].
+
+  features: (feature name, ids, offsets, weights) per table over the whole
+  batch (every rank sees all ids).
+  chunks: the batch is pooled and reduce-scattered in this many pieces
+  (block size divisible by it); chunk c of every rank's block is pooled
+  together, so each reduce-scatter moves a [W][B/(W chunks)][T][D] piece.
+  """
+
+  def __init__(self, plan: ShardPlan, batch: int, num_tables: int, dim: int,
+               pool: Pooler, chunks: int = 1, device=None, group=None):
+    self.plan = plan
+    self.batch = batch
+    self.num_tables = num_tables
+    self.dim = dim
+    self.pool = pool
+    self.group = group
+    self.block = plan.block_size(batch)
+    if chunks < 1 or self.block % chunks:
+      raise ValueError(f"block of {self.block} samples does not split into "
+                       f"{chunks} chunks")
+    self.chunks = chunks
+    self.piece = self.block // chunks
+    self.partial = torch.empty((chunks, plan.world, self.piece, num_tables,
+                                dim), dtype=torch.float32, device=device)
+    self.recv = torch.empty((self.block, num_tables, dim),
+                            dtype=torch.float32, device=device)
+
+  def chunk_requests(self, features, c: int) -> List[BagRequest]:
+    reqs = []
+    for s in range(self.plan.world):
+      b0 = s * self.block + c * self.piece
+      out = self.partial[c, s]
+      for k, (name, ids, offsets, weights) in enumerate(features):
+        base = BagRequest(name, ids, offsets, None, weights)
+        reqs.append(slice_request(base, b0, b0 + self.piece, out[:, k, :],
+                                  self.num_tables * self.dim))
+    return reqs
+
+  def schedule(self, features) -> List[List[BagRequest]]:
+    return [self.chunk_requests(features, c) for c in range(self.chunks)]
+
+  def run(self, steps):
+    works = []
+    for c, reqs in enumerate(steps):
+      self.pool(reqs)
+      out = self.recv[c * self.piece:(c + 1) * self.piece]
+      if self.plan.world == 1:
+        out.copy_(self.partial[c, 0])
+        continue
+      works.append(dist.reduce_scatter_tensor(
+          out.view(-1), self.partial[c].view(-1), group=self.group,
+          async_op=True))
+    for work in works:
+      work.wait()
+    return self.recv
