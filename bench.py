@@ -10,8 +10,13 @@ pooling kernel).
 
 With N GPUs (torchrun, one process per GPU, NCCL) every rank holds 8 such
 tables (8N tables in all, table-wise sharded) and pools them for the whole
-batch; an NCCL all-to-all then returns each sample block to its owning rank
-(weak scaling: fixed work per GPU).
+batch; each sample block goes to its owning rank (weak scaling: fixed work
+per GPU). By default the pooling kernel stores the blocks straight into the
+owners' buffers over NVLink and a flag barrier ends the step (--exchange
+peer); --exchange a2a / pipelined use NCCL instead.
+
+Each run also times the DLRM forward (26 fp32 tables, batch 16384 per GPU,
+data-parallel replicas at N > 1) and reports it under "dlrm_forward".
 
 Prints one JSON line (rank 0). `--impl reference` times the CPU restatement
 of the reference's embedding-bag (the reference itself cannot be built here)
@@ -190,7 +195,7 @@ class Workload:
   t mod N, so each rank holds 8); each rank pools its tables for the whole
   batch and the exchange returns every sample block to its owner."""
 
-  def __init__(self, xse, rank, world, exchange="a2a"):
+  def __init__(self, xse, rank, world, exchange="peer"):
     from xla_serving_b200 import sharding, synth  # pylint: disable=import-outside-toplevel
     self.xse = xse
     self.world = world
@@ -602,6 +607,242 @@ def run_reference(args):
   print(json.dumps(line), flush=True)
 
 
+# The reference configurations other than the default, as `--workload` runs
+# (one JSON line each; the default multi-table run is the headline line).
+CONFIGS = {
+    "zipf_single": dict(
+        desc="zipf_single: 1 fp32 table 1,000,000 x 64, batch 4096, bag "
+             "lengths U[1,32], Zipf(1.05) ids, sum pooling",
+        tables=1, dtype="f32", vocab=1_000_000, dim=64, batch=4096,
+        lengths=(1, 32), alpha=1.05, sharding="table", rotate=64),
+    "sharded_tablewise": dict(
+        desc="sharded_tablewise: 64 bf16 tables 20,000,000 x 128 (327 GB) "
+             "placed table-wise (table t on rank t mod N; 8 tables, the "
+             "per-GPU slice at N=8, when N=1), batch 65536, bag lengths "
+             "U[1,64], Zipf(1.1) ids, sum pooling",
+        tables=64, tables_n1=8, dtype="bf16", vocab=20_000_000, dim=128,
+        batch=65536, lengths=(1, 64), alpha=1.1, sharding="table", rotate=2),
+    "int8_rowwise": dict(
+        desc="int8_rowwise: 26 int8 row-wise tables 10,000,000 x 256 with "
+             "per-row fp32 scale U(1e-3,1e-2) and bias U(-0.1,0.1), rows "
+             "split row-wise over the N ranks, batch 32768, bag lengths "
+             "U[1,80], Zipf(1.05) ids, sum pooling with in-kernel dequant, "
+             "partial sums reduce-scattered",
+        tables=26, dtype="i8", vocab=10_000_000, dim=256, batch=32768,
+        lengths=(1, 80), alpha=1.05, sharding="row", rotate=2),
+}
+_ELEM = {"f32": 4, "bf16": 2, "i8": 1}
+
+
+class ConfigWorkload:
+  """Tables, inputs and the exchange of one CONFIGS entry on this rank."""
+
+  def __init__(self, xse, cfg, rank, world, exchange):
+    from xla_serving_b200 import sharding, synth  # pylint: disable=import-outside-toplevel
+    C = xse._capi
+    self.xse, self.cfg, self.world = xse, cfg, world
+    dt = {"f32": C.DT_F32, "bf16": C.DT_BF16, "i8": C.DT_I8_ROWWISE}[
+        cfg["dtype"]]
+    self.dtype = dt
+    self.engine = xse.EmbeddingEngine(torch.cuda.current_device())
+    self.plan = sharding.ShardPlan(world, rank)
+    num_tables = cfg["tables"] if world > 1 else cfg.get("tables_n1",
+                                                           cfg["tables"])
+    self.num_tables = num_tables
+    rowwise = cfg["sharding"] == "row"
+    local = (list(range(num_tables)) if rowwise else
+             self.plan.tables_of(rank, num_tables))
+    self.local = local
+    vocab, dim = cfg["vocab"], cfg["dim"]
+    lo, hi = self.plan.row_window(vocab) if rowwise else (0, vocab)
+    self.window = (lo, hi)
+    self.tables = []
+    for g in local:
+      rows, scale, bias = synth.synth_table(dt, vocab, dim, SEED, 200 + g,
+                                            row0=lo, nrows=hi - lo)
+      name = f"t{g}"
+      self.engine.add_table(name, rows, "SUM", scale=scale, bias=bias,
+                            vocab=vocab, row_begin=lo if rowwise else 0,
+                            row_end=hi if rowwise else 0, adopt=True)
+      self.tables.append((rows, scale, bias))
+      self.engine.register_feature(name, name)
+    self.inputs = []
+    self.nnz = []
+    for v in range(cfg["rotate"]):
+      feats = []
+      nnz = 0
+      for g in local:
+        spec = synth.TableSpec(f"t{g}", vocab, dim, dt, "SUM")
+        fb = synth.synth_batch(spec, 200 + g, cfg["batch"], cfg["lengths"][0],
+                               cfg["lengths"][1], SEED, cfg["alpha"],
+                               variant=v)
+        feats.append((spec.name, fb.ids, fb.offsets, None))
+        nnz += fb.ids.numel()
+      self.inputs.append(feats)
+      self.nnz.append(nnz)
+    n_req = len(local) * (world if rowwise else 1)
+    self.status = xse.Status(max(n_req, 1))
+    self.pooler = sharding.engine_pooler(self.engine, self.status)
+    if rowwise:
+      self.exchange = sharding.RowwiseExchange(
+          self.plan, cfg["batch"], len(local), dim, self.pooler,
+          device="cuda")
+    else:
+      self.exchange = sharding.TablewiseExchange(
+          self.plan, cfg["batch"], num_tables, dim, self.pooler,
+          device="cuda", mode=exchange)
+    self.steps = [self.exchange.schedule(f) for f in self.inputs]
+    torch.cuda.synchronize()
+
+  def step(self, i):
+    before = self.pooler.launches
+    self.exchange.run(self.steps[i % len(self.steps)])
+    return self.pooler.launches - before
+
+  def pool_bytes(self, v):
+    """Algorithmic bytes of variant v's pooling on this rank: every id's row
+    (int8 rows plus their 8-byte scale/bias) and id, the offsets, the fp32
+    outputs."""
+    cfg = self.cfg
+    row = cfg["dim"] * _ELEM[cfg["dtype"]] + (8 if cfg["dtype"] == "i8" else 0)
+    t = len(self.local)
+    return (self.nnz[v] * (row + 8) + (cfg["batch"] + 1) * 8 * t +
+            cfg["batch"] * t * cfg["dim"] * 4)
+
+  def close(self):
+    if hasattr(self.exchange, "close"):
+      self.exchange.check()
+      self.exchange.close()
+    self.status.close()
+    self.engine.close()
+
+
+def config_cpu_baseline(wl, seconds):
+  """The oracle on this host's cores over a bounded sample: the first
+  table's first 4M rows (or all rows) copied to the host, Zipf ids over that
+  subset, the config's bag lengths, for about `seconds`."""
+  sys.path.insert(0, ROOT)
+  from oracle import oracle  # pylint: disable=import-outside-toplevel
+  from xla_serving_b200 import synth  # pylint: disable=import-outside-toplevel
+  cfg = wl.cfg
+  cores = oracle.host_cores()
+  sub = min(cfg["vocab"], 4_000_000)
+  rows, scale, bias = synth.synth_table(wl.dtype, cfg["vocab"], cfg["dim"],
+                                        SEED, 200, nrows=sub)
+  if cfg["dtype"] == "bf16":
+    table = rows.view(torch.int16).cpu().numpy().view(np.uint16)
+    odt = oracle.BF16
+  elif cfg["dtype"] == "i8":
+    table = rows.cpu().numpy()
+    odt = oracle.I8_ROWWISE
+  else:
+    table = rows.cpu().numpy()
+    odt = oracle.F32
+  sc = None if scale is None else scale.cpu().numpy()
+  bi = None if bias is None else bias.cpu().numpy()
+  del rows
+  spec = synth.TableSpec("cpu", sub, cfg["dim"], wl.dtype, "SUM")
+  bags = []
+  for k in range(4):
+    fb = synth.synth_batch(spec, 900 + k, cfg["batch"], cfg["lengths"][0],
+                           cfg["lengths"][1], SEED, cfg["alpha"])
+    bags.append(oracle.Bag(table, fb.ids.cpu().numpy(),
+                           fb.offsets.cpu().numpy(), None, "SUM", odt, sc, bi))
+  oracle.embedding_bag_batch(bags[:1], num_threads=cores)
+  reps, t0 = 0, time.perf_counter()
+  while True:
+    oracle.embedding_bag_batch([bags[reps % 4]], num_threads=cores)
+    reps += 1
+    el = time.perf_counter() - t0
+    if el >= seconds:
+      break
+  ids = sum(len(bags[i % 4].ids) for i in range(reps))
+  return {"value": ids / el, "unit": "ids/s", "cores": cores, "kind": "port",
+          "sample": f"{reps} batches of {cfg['batch']} bags over the first "
+                    f"{sub:,} rows of one table ({cfg['dtype']}"
+                    f"{', dequantized per row' if cfg['dtype'] == 'i8' else ''}"
+                    f") in {el:.1f} s"}
+
+
+def run_config(args, name):
+  cfg = CONFIGS[name]
+  world, rank, local = init_distributed()
+  torch.cuda.set_device(local)
+  xse = load_package()
+  wl = ConfigWorkload(xse, cfg, rank, world, args.exchange)
+  clocks = ClockSampler(local)
+  clocks.start()
+  for i in range(args.warmup):
+    wl.step(i)
+  wl.status.wait()
+  torch.cuda.synchronize()
+  barrier(world, local)
+  stream = torch.cuda.current_stream()
+  start = torch.cuda.Event(enable_timing=True)
+  end = torch.cuda.Event(enable_timing=True)
+  wl.engine.set_profiling(True)
+  launches = 0
+  start.record(stream)
+  for i in range(args.steps):
+    launches += wl.step(i)
+  end.record(stream)
+  torch.cuda.synchronize()
+  barrier(world, local)
+  wl.status.wait()
+  ms = max_over_ranks(start.elapsed_time(end), world)
+  pool_ms, pool_n = wl.engine.profile_read()
+  wl.engine.set_profiling(False)
+  clock_info = clocks.stop()
+  rowwise = cfg["sharding"] == "row"
+  # ids/s counts every id occurrence once: row-wise ranks all see all ids.
+  ids_rank = sum(wl.nnz[i % len(wl.nnz)] for i in range(args.steps))
+  ids = ids_rank if rowwise else sum_over_ranks(ids_rank, world)
+  pool_bytes = sum(wl.pool_bytes(i % len(wl.nnz))
+                   for i in range(args.steps)) / args.steps
+  pool_launch_ms = pool_ms / max(pool_n, 1)
+  pool_step_ms = pool_ms / args.steps
+  peak, peak_kind = measured_peaks()
+  base = None
+  if world == 1 and not args.no_cpu_baseline:
+    base = config_cpu_baseline(wl, args.cpu_seconds)
+  if rank == 0:
+    line = {
+        "metric": "embedding-bag ids/sec", "value": ids / (ms / 1000.0),
+        "unit": "ids/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak" if name == "zipf_single" else "strong",
+        "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": "synthetic (seeded counter RNG)",
+        "config": {"workload": cfg["desc"], "global_batch": cfg["batch"],
+                   "tables_total": wl.num_tables,
+                   "tables_per_gpu": len(wl.local),
+                   "rows_per_gpu": wl.window[1] - wl.window[0],
+                   "parallelism": ("single GPU" if world == 1 else
+                                   ("row-wise windows + NCCL reduce-scatter"
+                                    if rowwise else
+                                    f"table-wise, {args.exchange} exchange")),
+                   "l2": f"{cfg['rotate']} rotating input sets; tables "
+                         "far larger than L2 (Zipf hot rows hit it)"},
+        "roofline": {
+            "bound": "hbm",
+            "achieved": pool_bytes / (pool_step_ms / 1000.0) / 1e9,
+            "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+            "frac": pool_bytes / (pool_step_ms / 1000.0) / 1e9 / peak,
+            "algorithmic_bytes_per_step": pool_bytes,
+            "pool_ms_per_step": pool_step_ms,
+            "avg_launch_ms": pool_launch_ms,
+            "traffic": None},
+        "gpu_launches": launches,
+        "cpu_baseline": base,
+        "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+  wl.close()
+  if world > 1:
+    dist.destroy_process_group()
+
+
 def main():
   ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
   ap.add_argument("--gpus", type=int, default=1)
@@ -611,7 +852,7 @@ def main():
   ap.add_argument("--e2e-steps", type=int, default=200)
   ap.add_argument("--cpu-seconds", type=float, default=10.0)
   ap.add_argument("--no-cpu-baseline", action="store_true")
-  ap.add_argument("--exchange", default="a2a",
+  ap.add_argument("--exchange", default="peer",
                   choices=["a2a", "pipelined", "peer"],
                   help="N>1: one NCCL all-to-all after pooling, per-block "
                        "NCCL send/recv overlapped with the pooling, or "
@@ -619,11 +860,18 @@ def main():
                        "NVLink by the pooling kernel")
   ap.add_argument("--dlrm-steps", type=int, default=40,
                   help="timed DLRM forward steps (0: skip the DLRM forward)")
+  ap.add_argument("--workload", default="multi_table",
+                  choices=["multi_table"] + sorted(CONFIGS),
+                  help="multi_table (the headline line, with the DLRM "
+                       "forward) or one of the other reference configs")
   args = ap.parse_args()
   if args.warmup < 3:
     args.warmup = 3
   if args.impl == "reference":
     run_reference(args)
+    return
+  if args.workload != "multi_table":
+    run_config(args, args.workload)
     return
 
   world, rank, local = init_distributed()

@@ -63,7 +63,12 @@ struct ElemsPerVec<2> {
 #define XSE_POOL_ROWS 4
 #endif
 #ifndef XSE_POOL_MIN_BLOCKS
-#define XSE_POOL_MIN_BLOCKS 4
+#define XSE_POOL_MIN_BLOCKS 3
+#endif
+// Rows of the next batch of a chunk prefetched into L2 while the current
+// batch is in flight.
+#ifndef XSE_POOL_PREFETCH
+#define XSE_POOL_PREFETCH 1
 #endif
 
 // Rows gathered per batch (in flight per lane, times V vectors each).
@@ -114,14 +119,28 @@ __device__ __forceinline__ int64_t LoadIndex(const void* base, int is64,
               : static_cast<int64_t>(__ldg(static_cast<const int*>(base) + i));
 }
 
-// Read-only 16-byte row load that does not allocate in L1 (rows are touched
-// once per id; reuse of hot rows comes from L2).
+// Read-only 16-byte row load. XSE_POOL_L1 selects its L1 policy: 0 does not
+// allocate in L1 (reuse of rows comes from L2 only), 1 caches in L1 (hot
+// rows of skewed id streams are then served by the SM that reads them).
+#ifndef XSE_POOL_L1
+#define XSE_POOL_L1 0
+#endif
 __device__ __forceinline__ uint4 LoadRowVec(const uint4* p) {
   uint4 r;
+#if XSE_POOL_L1 == 1
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+#else
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
+#endif
   return r;
+}
+
+__device__ __forceinline__ void PrefetchRowVec(const uint4* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 __device__ __forceinline__ float I8At(uint32_t w, int k) {
@@ -284,7 +303,7 @@ __device__ __forceinline__ void AddGathered(
 template <int DT, int G, int V, bool EXACT, int WM, typename Hook>
 __device__ __forceinline__ void FullBatch(
     const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
-    int my_row, float my_w, int j0,
+    int my_row, float my_w, int j0, int cnt,
     u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, Hook&& hook) {
   constexpr int U = RowsInFlight<DT, V>::value;
   const int stride = EXACT ? G * V : row_vecs;
@@ -304,6 +323,22 @@ __device__ __forceinline__ void FullBatch(
       }
     }
   }
+#if XSE_POOL_PREFETCH
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int j = j0 + U + u;
+    if (j < cnt) {
+      const int r = __shfl_sync(gmask, my_row, j, G);
+      const uint4* src = rows + static_cast<int64_t>(r) * stride;
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        if (EXACT || gl + v * G < row_vecs) PrefetchRowVec(src + v * G);
+      }
+    }
+  }
+#else
+  (void)cnt;
+#endif
   hook();  // runs while this batch's rows are in flight
 #pragma unroll
   for (int u = 0; u < U; ++u) {
@@ -526,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, V>::value)
         if (__all_sync(gmask, gl >= cnt || my_row >= 0)) {
           for (; j0 + U <= cnt; j0 += U) {
             FullBatch<DT, G, V, EXACT, WM>(d, rows, row_vecs, gl, gmask,
-                                           my_row, my_w, j0, acc, &wsum,
+                                           my_row, my_w, j0, cnt, acc, &wsum,
                                            prefetch);
           }
         }

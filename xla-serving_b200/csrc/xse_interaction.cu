@@ -47,7 +47,6 @@ __global__ void __launch_bounds__(kInteractionThreads)
                          const float* __restrict__ pooled,
                          int64_t pooled_stride, int64_t batch,
                          float* __restrict__ out, int64_t out_stride) {
-  constexpr int T = R - 1;
   constexpr int D = 32 * CPL;
   constexpr int P = R * (R - 1) / 2;
   constexpr int W = D + P;

@@ -374,10 +374,13 @@ class RowwiseExchange:
                        f"{chunks} chunks")
     self.chunks = chunks
     self.piece = self.block // chunks
-    self.partial = torch.empty((chunks, plan.world, self.piece, num_tables,
-                                dim), dtype=torch.float32, device=device)
     self.recv = torch.empty((self.block, num_tables, dim),
                             dtype=torch.float32, device=device)
+    if plan.world == 1:  # nothing to reduce: pool straight into recv
+      self.partial = self.recv.view(chunks, 1, self.piece, num_tables, dim)
+    else:
+      self.partial = torch.empty((chunks, plan.world, self.piece, num_tables,
+                                  dim), dtype=torch.float32, device=device)
 
   def chunk_requests(self, features, c: int) -> List[BagRequest]:
     reqs = []
@@ -399,7 +402,6 @@ class RowwiseExchange:
       self.pool(reqs)
       out = self.recv[c * self.piece:(c + 1) * self.piece]
       if self.plan.world == 1:
-        out.copy_(self.partial[c, 0])
         continue
       works.append(dist.reduce_scatter_tensor(
           out.view(-1), self.partial[c].view(-1), group=self.group,
