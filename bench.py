@@ -291,11 +291,13 @@ class DlrmWorkload:
   """One DLRM forward per step on this rank's GPU (a full replica: every
   rank holds all 26 tables and runs its own batch)."""
 
-  def __init__(self, xse, rank):
+  def __init__(self, xse, rank, max_rows=None):
     from xla_serving_b200 import dlrm, synth  # pylint: disable=import-outside-toplevel
     self.xse = xse
     self.engine = xse.EmbeddingEngine(torch.cuda.current_device())
     self.rows = synth.log_uniform_rows(DLRM_TABLES, 1e4, 1e7, SEED)
+    if max_rows:  # smaller tables, for profiler captures
+      self.rows = [min(r, int(max_rows)) for r in self.rows]
     names, self.tables = [], []
     for t in range(DLRM_TABLES):
       rows, _, _ = synth.synth_table(xse._capi.DT_F32, self.rows[t], DLRM_DIM,
@@ -305,7 +307,11 @@ class DlrmWorkload:
       self.engine.add_table(name, rows, "SUM", adopt=True)
       self.engine.register_feature(name, name)
       names.append(name)
-    self.model = dlrm.DLRM(self.engine, names, dim=DLRM_DIM, seed=SEED)
+    # Dense layers as three TF32 tensor-core GEMMs over hi/lo split operands
+    # (fp32-level accuracy; tests/test_dlrm_gpu.py holds them to the fp32
+    # layer's tolerance).
+    self.model = dlrm.DLRM(self.engine, names, dim=DLRM_DIM, seed=SEED,
+                           math=dlrm.MATH_TF32X3)
     gen = torch.Generator(device="cuda").manual_seed(SEED + rank)
     self.sets = []
     self.nnz = []
@@ -382,7 +388,7 @@ class DlrmHostInputs:
 def measure_dlrm(xse, args, world, local):
   """Samples/s of the DLRM forward (whole job: every rank runs its own
   batch), its pooled-lookup roofline and its end-to-end rate."""
-  wl = DlrmWorkload(xse, int(os.environ.get("RANK", "0")))
+  wl = DlrmWorkload(xse, int(os.environ.get("RANK", "0")), args.dlrm_max_rows)
   host = DlrmHostInputs(wl)
   for i in range(max(args.warmup, 3)):
     wl.step(i)
@@ -433,7 +439,9 @@ def measure_dlrm(xse, args, world, local):
       "steps": args.dlrm_steps,
       "ms_per_step": ms / args.dlrm_steps,
       "ids_per_s": ids / (ms / 1000.0),
-      "dtype": "fp32",
+      "dtype": "fp32 (tables, pooling, interaction); dense layers as 3xTF32 "
+               "tensor-core GEMMs (hi/lo split operands, fp32-level "
+               "accuracy)",
       "parallelism": ("single GPU" if world == 1 else
                       f"{world} data-parallel replicas (tables replicated, "
                       "no collective)"),
@@ -843,6 +851,26 @@ def run_config(args, name):
     dist.destroy_process_group()
 
 
+def run_dlrm_only(args):
+  """The DLRM forward alone, as its own JSON line."""
+  world, rank, local = init_distributed()
+  torch.cuda.set_device(local)
+  xse = load_package()
+  clocks = ClockSampler(local)
+  clocks.start()
+  result = measure_dlrm(xse, args, world, local)
+  result["clocks"] = clocks.stop()
+  result["warmup"] = args.warmup
+  result["higher_is_better"] = True
+  result["scaling"] = "weak"
+  result["vs_baseline"] = None
+  result["data"] = "synthetic (seeded counter RNG)"
+  if rank == 0:
+    print(json.dumps(result), flush=True)
+  if world > 1:
+    dist.destroy_process_group()
+
+
 def main():
   ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
   ap.add_argument("--gpus", type=int, default=1)
@@ -860,15 +888,21 @@ def main():
                        "NVLink by the pooling kernel")
   ap.add_argument("--dlrm-steps", type=int, default=40,
                   help="timed DLRM forward steps (0: skip the DLRM forward)")
+  ap.add_argument("--dlrm-max-rows", type=float, default=None,
+                  help="cap the DLRM tables' rows (profiler captures)")
   ap.add_argument("--workload", default="multi_table",
-                  choices=["multi_table"] + sorted(CONFIGS),
+                  choices=["multi_table", "dlrm"] + sorted(CONFIGS),
                   help="multi_table (the headline line, with the DLRM "
-                       "forward) or one of the other reference configs")
+                       "forward), dlrm (the DLRM forward alone) or one of "
+                       "the other reference configs")
   args = ap.parse_args()
   if args.warmup < 3:
     args.warmup = 3
   if args.impl == "reference":
     run_reference(args)
+    return
+  if args.workload == "dlrm":
+    run_dlrm_only(args)
     return
   if args.workload != "multi_table":
     run_config(args, args.workload)

@@ -50,6 +50,26 @@ int xse_linear_forward(const float* x, int64_t rows, int32_t in_dim,
                        int32_t out_dim, int32_t activation, int32_t math,
                        float* y, int64_t y_stride, void* stream);
 
+/* hi = src rounded to TF32 (round to nearest, ties away from zero) and
+ * lo = src - hi (exact), for a [rows, cols] block with row stride `stride`
+ * (the same stride in hi and lo). */
+int xse_tf32_split(const float* src, int64_t rows, int32_t cols,
+                   int64_t stride, float* hi, float* lo, void* stream);
+
+/* y = act(x K + bias) from split operands (x = x_hi + x_lo, K = k_hi + k_lo
+ * as made by xse_tf32_split) as three TF32 tensor-core GEMMs accumulated in
+ * fp32: y = x_lo k_hi + x_hi k_lo + x_hi k_hi (+ bias, then act). The hi
+ * parts are exact in TF32 and the dropped x_lo k_lo term is below 2^-22 of
+ * |x||K|, so the result has fp32-level accuracy. act: XSE_ACT_NONE or
+ * XSE_ACT_RELU. Layouts as xse_linear_forward; x_hi and x_lo share
+ * x_stride, k_hi and k_lo are [in_dim, out_dim]. */
+int xse_linear_forward_tf32x3(const float* x_hi, const float* x_lo,
+                              int64_t rows, int32_t in_dim, int64_t x_stride,
+                              const float* k_hi, const float* k_lo,
+                              const float* bias, int32_t out_dim,
+                              int32_t activation, float* y, int64_t y_stride,
+                              void* stream);
+
 /* The dot interaction of xse_emb.h's xse_dot_interaction with strides:
  * dense rows every dense_stride floats, pooled samples every pooled_stride
  * floats ([T, dim] each, contiguous), output rows every out_stride floats

@@ -79,7 +79,7 @@ int32_t xse_abi_version(void);
 /* ---------------------------------------------------------------------------
  * Engine: tables and feature specs resident in HBM.
  * Replaces CpuEmbeddingEngine (data/cpu_embedding/cc/cpu_embedding_engine.h:
- * 27-89) and the table type EmbeddingTable (embedding_table.h:25-82).
+ * 41-103) and the table type EmbeddingTable (embedding_table.h:39-96).
  * ------------------------------------------------------------------------- */
 typedef struct xse_engine xse_engine;
 
@@ -110,19 +110,19 @@ typedef struct {
   int64_t row_end;
 } xse_table_desc;
 
-/* Replaces EmbeddingTable::Create (embedding_table.cc:42-56) followed by
- * CpuEmbeddingEngine::AddLocalTable (cpu_embedding_engine.cc:57-67):
+/* Replaces EmbeddingTable::Create (embedding_table.cc:56-70) followed by
+ * CpuEmbeddingEngine::AddLocalTable (cpu_embedding_engine.cc:71-81):
  * XSE_ALREADY_EXISTS on a duplicate name. */
 int xse_engine_add_table(xse_engine* engine, const xse_table_desc* table);
 
 /* Replaces CpuEmbeddingEngine::RegisterFeatureSpec (cpu_embedding_engine.cc:
- * 46-55) with FeatureSpec{name, table_name, max_sequence_length}
+ * 60-69) with FeatureSpec{name, table_name, max_sequence_length}
  * (feature_spec.h:25-29). */
 int xse_engine_register_feature(xse_engine* engine, const char* feature,
                                 const char* table,
                                 int32_t max_sequence_length);
 
-/* Replaces CpuEmbeddingEngine::Clear (cpu_embedding_engine.cc:69-75). */
+/* Replaces CpuEmbeddingEngine::Clear (cpu_embedding_engine.cc:83-89). */
 int xse_engine_clear(xse_engine* engine);
 
 typedef struct {
@@ -144,7 +144,7 @@ int xse_engine_feature_table(xse_engine* engine, const char* feature,
 /* ---------------------------------------------------------------------------
  * Pooled lookup.
  * Replaces CpuEmbeddingEngine::ExecuteBatch(Span<FeatureBatchInput<float>>)
- * (cpu_embedding_engine.h:62-65, cpu_embedding_engine.cc:154-203) and
+ * (cpu_embedding_engine.h:55-62,79, cpu_embedding_engine.cc:168-217) and
  * internal::ExecuteEmbeddingBagBatch (embedding_bag.h:87-90). Inputs and
  * outputs are device memory owned by the caller.
  * ------------------------------------------------------------------------- */

@@ -55,7 +55,7 @@ void xse_host_buffer_free(xse_host_buffer* buffer);
  * ------------------------------------------------------------------------- */
 typedef struct xse_resource xse_resource;
 
-/* LoadImpl (cpu_embedding_resource.cc:215-239): assets are (name, path)
+/* LoadImpl (cpu_embedding_resource.cc:229-253): assets are (name, path)
  * pairs; the one named "__jce_manifest__" is the CpuEmbeddingManifest text
  * proto, every other asset a raw little-endian table "<name>.bin" of
  * vocab_size x embedding_dim elements. The manifest's optional per-table
@@ -72,7 +72,7 @@ int xse_resource_create(int32_t device, xse_resource** out);
 void xse_resource_destroy(xse_resource* resource);
 /* The engine the resource owns (CpuEmbeddingEngineResource::Get). */
 xse_engine* xse_resource_engine(xse_resource* resource);
-/* GetEmbeddingDim (cpu_embedding_resource.cc:241-249). */
+/* GetEmbeddingDim (cpu_embedding_resource.cc:255-263). */
 int xse_resource_embedding_dim(xse_resource* resource, const char* feature,
                                int32_t* dim);
 /* RegisterEmbeddingDimForTest (cpu_embedding_resource.h:42-45). */
@@ -84,7 +84,7 @@ int xse_resource_register_embedding_dim(xse_resource* resource,
  * ------------------------------------------------------------------------- */
 typedef struct xse_lookup_transform xse_lookup_transform;
 
-/* Create (cpu_embedding_lookup_transform.cc:73-137). */
+/* Create (cpu_embedding_lookup_transform.cc:87-151). */
 int xse_lookup_transform_create(xse_resource* resource,
                                 const char* const* feature_names,
                                 int32_t num_features, int32_t dense_lookup,
@@ -95,7 +95,7 @@ int xse_lookup_transform_create(xse_resource* resource,
 void xse_lookup_transform_destroy(xse_lookup_transform* transform);
 
 /* operator()(ids, row_pointers, weights) (cpu_embedding_lookup_transform.cc:
- * 230-342): one entry per feature in each list (row_pointers and weights
+ * 244-356, checks as ValidateLookupInputs :159-242): one entry per feature in each list (row_pointers and weights
  * are ignored with dense_lookup). On success writes num_features pinned F32
  * outputs of shape [batch, dim] into outputs (free each with
  * xse_host_buffer_free). `stream` is the CUDA stream to run on (NULL: the
@@ -114,7 +114,7 @@ int xse_lookup_transform_run(xse_lookup_transform* transform,
  * ------------------------------------------------------------------------- */
 typedef struct xse_dense_lookup_transform xse_dense_lookup_transform;
 
-/* Create (dense_cpu_embedding_lookup_transform.cc:62-85). */
+/* Create (dense_cpu_embedding_lookup_transform.cc:76-99). */
 int xse_dense_lookup_transform_create(xse_resource* resource,
                                       const char* const* feature_names,
                                       int32_t num_features, int64_t pad_value,
@@ -124,7 +124,7 @@ int xse_dense_lookup_transform_create(xse_resource* resource,
 void xse_dense_lookup_transform_destroy(xse_dense_lookup_transform* t);
 
 /* operator()(dense_ids_list) (dense_cpu_embedding_lookup_transform.cc:
- * 134-254): per feature a [batch, seq] S32/S64 buffer; ids equal to
+ * 148-268): per feature a [batch, seq] S32/S64 buffer; ids equal to
  * pad_value are dropped and an all-pad row keeps one pad_value id. Writes
  * num_features pinned F32 [batch, dim] outputs. */
 int xse_dense_lookup_transform_run(xse_dense_lookup_transform* transform,

@@ -300,7 +300,7 @@ std::vector<Task> BuildTasks(const std::vector<Request>& reqs, int threads) {
 }
 
 // A persistent worker pool (the reference keeps an Eigen::ThreadPool alive
-// in the engine, cpu_embedding_engine.cc:37-42), so that timing does not pay
+// in the engine, cpu_embedding_engine.cc:51-56), so that timing does not pay
 // thread creation per call.
 class WorkerPool {
  public:
@@ -589,7 +589,7 @@ int oracle_dense_to_csr(const void* dense, int32_t dense_i64, int64_t batch,
                         int32_t* row_pointers, int64_t* num_ids, char* err,
                         int32_t errlen) {
   // DenseCpuEmbeddingLookupTransform::operator() (dense_cpu_embedding_lookup_
-  // transform.cc:152-206): keep non-pad ids; an all-pad row keeps one pad id;
+  // transform.cc:186-225): keep non-pad ids; an all-pad row keeps one pad id;
   // int32 row pointers with an overflow check.
   const int64_t elements = batch * seq;
   if (elements > std::numeric_limits<int32_t>::max()) {
@@ -627,7 +627,7 @@ int oracle_dense_to_csr(const void* dense, int32_t dense_i64, int64_t batch,
 int oracle_dense_lookup_row_pointers(int64_t batch, int64_t valency,
                                      int32_t* row_pointers, char* err,
                                      int32_t errlen) {
-  // cpu_embedding_lookup_transform.cc:284-302.
+  // cpu_embedding_lookup_transform.cc:297-316.
   if (batch < 0 || valency < 0) {
     return Fail(ORACLE_INVALID_ARGUMENT, err, errlen,
                 "Dense embedding IDs dimensions must be non-negative.");

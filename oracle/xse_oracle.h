@@ -78,7 +78,7 @@ int oracle_assemble_bf16_accumulate(const uint16_t* table, int64_t vocab,
                                     char* err, int32_t errlen);
 
 /* DenseCpuEmbeddingLookupTransform CSR build (dense_cpu_embedding_lookup_
- * transform.cc:183-206). dense is [batch, seq] int32 or int64. Writes ids
+ * transform.cc:186-225). dense is [batch, seq] int32 or int64. Writes ids
  * (capacity >= batch*seq + batch) and batch+1 int32 row pointers; returns the
  * number of ids through *num_ids. */
 int oracle_dense_to_csr(const void* dense, int32_t dense_i64, int64_t batch,
@@ -87,7 +87,7 @@ int oracle_dense_to_csr(const void* dense, int32_t dense_i64, int64_t batch,
                         int32_t errlen);
 
 /* Dense row-pointer generation for dense_lookup (cpu_embedding_lookup_
- * transform.cc:278-302), including its int32 overflow guards. */
+ * transform.cc:297-316), including its int32 overflow guards. */
 int oracle_dense_lookup_row_pointers(int64_t batch, int64_t valency,
                                      int32_t* row_pointers, char* err,
                                      int32_t errlen);

@@ -120,8 +120,10 @@ def test_dot_interaction_strided_rejects_short_strides(xse):
   assert rc == C.INVALID_ARGUMENT and "strides" in C.last_error()
 
 
-def test_dense_tower_matches_float64(dlrm):
-  tower = dlrm.DenseTower(seed=3)
+@pytest.mark.parametrize("math", ["fp32", "tf32x3"])
+def test_dense_tower_matches_float64(xse, dlrm, math):
+  code = xse._capi.MATH_FP32 if math == "fp32" else dlrm.MATH_TF32X3
+  tower = dlrm.DenseTower(seed=3, math=code)
   rng = np.random.default_rng(5)
   batch = 96
   dense = rng.standard_normal((batch, 13)).astype(np.float32)
@@ -132,6 +134,33 @@ def test_dense_tower_matches_float64(dlrm):
   assert got.shape == (batch,)
   np.testing.assert_allclose(got, want, rtol=0, atol=1e-4)
   assert np.all((got > 0) & (got < 1))
+
+
+@pytest.mark.parametrize("rows,in_dim,out_dim,act", [
+    (300, 480, 1024, 1), (77, 1024, 512, 1), (64, 256, 128, 0),
+    (1, 128, 256, 1)])
+def test_linear_forward_tf32x3(xse, dlrm, rows, in_dim, out_dim, act):
+  """Three TF32 GEMMs over split operands: fp32-level accuracy (the same
+  1e-5 magnitude-relative bound as the fp32 layer)."""
+  rng = np.random.default_rng(rows + in_dim)
+  x = rng.standard_normal((rows, in_dim)).astype(np.float32)
+  kernel = rng.uniform(-0.1, 0.1, (in_dim, out_dim)).astype(np.float32)
+  bias = rng.uniform(-0.1, 0.1, out_dim).astype(np.float32)
+  xd, kd = torch.from_numpy(x).cuda(), torch.from_numpy(kernel).cuda()
+  xh, xl = torch.empty_like(xd), torch.empty_like(xd)
+  kh, kl = torch.empty_like(kd), torch.empty_like(kd)
+  dlrm.tf32_split(xd, xh, xl)
+  dlrm.tf32_split(kd, kh, kl)
+  # the split is exact and hi has at most 11 significant bits
+  torch.testing.assert_close(xh + xl, xd, rtol=0, atol=0)
+  assert torch.all((xh.view(torch.int32) & 0x1FFF) == 0)
+  layer = dlrm.DenseLayer(kd, torch.from_numpy(bias).cuda(), act)
+  out = torch.empty((rows, out_dim), device="cuda")
+  dlrm.linear_tf32x3(xh, xl, kh, kl, layer, out)
+  torch.cuda.synchronize()
+  want, bound = host_linear(x, kernel, bias, act)
+  np.testing.assert_array_less(np.abs(out.cpu().numpy() - want),
+                               1e-5 * bound + 1e-6)
 
 
 def test_dlrm_forward_end_to_end(xse, dlrm):

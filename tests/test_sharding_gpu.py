@@ -134,3 +134,48 @@ def test_sharded_two_gpus(mode):
       np.testing.assert_allclose(got[r], exp, rtol=1e-5, atol=1e-6)
     else:
       np.testing.assert_array_equal(got[r], exp)
+
+
+def _barrier_timeout_main(rank, world, port, results):
+  """Rank 1 never reaches the barrier: rank 0's bounded wait gives up and
+  the group reports DEADLINE_EXCEEDED; the context stays usable."""
+  os.environ["MASTER_ADDR"] = "127.0.0.1"
+  os.environ["MASTER_PORT"] = str(port)
+  torch.cuda.set_device(rank)
+  dist.init_process_group("nccl", rank=rank, world_size=world,
+                          timeout=timedelta(seconds=60),
+                          device_id=torch.device("cuda", rank))
+  try:
+    from conftest import load_package  # pylint: disable=import-outside-toplevel
+    xse = load_package()
+    plan = xse.sharding.ShardPlan(world, rank)
+    group = xse.sharding.PeerGroup(plan, 1024, rank)
+    group.barrier()  # both ranks: passes
+    group.check()
+    if rank == 0:
+      group.barrier(spin_limit=2000)  # rank 1 never comes: ~ms, then gives up
+      try:
+        group.check()
+        results[rank] = "no error"
+      except xse.XseError as e:
+        results[rank] = (e.code, e.message)
+      x = torch.ones(4, device="cuda")
+      results["usable"] = float((x * 2).sum().item())
+    dist.barrier()
+    group.close()
+  finally:
+    dist.destroy_process_group()
+
+
+def test_peer_barrier_gives_up_when_a_rank_never_arrives(xse):
+  if torch.cuda.device_count() < 2:
+    pytest.skip("needs two GPUs")
+  with mp.get_context("spawn").Manager() as manager:
+    results = manager.dict()
+    mp.start_processes(_barrier_timeout_main,
+                       args=(2, _free_port(), results), nprocs=2,
+                       start_method="spawn")
+    got = dict(results)
+  assert got[0][0] == xse._capi.DEADLINE_EXCEEDED
+  assert "gave up" in got[0][1]
+  assert got["usable"] == 8.0

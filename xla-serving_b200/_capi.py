@@ -194,6 +194,9 @@ SIGNATURES.update({
                                 _I32, _P, _I64, _P]),
     "xse_dot_interaction_strided": (_I, [_P, _I64, _P, _I64, _I64, _I32, _I32,
                                          _P, _I64, _P]),
+    "xse_tf32_split": (_I, [_P, _I64, _I32, _I64, _P, _P, _P]),
+    "xse_linear_forward_tf32x3": (_I, [_P, _P, _I64, _I32, _I64, _P, _P, _P,
+                                       _I32, _I32, _P, _I64, _P]),
 })
 
 

@@ -397,7 +397,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
                     n, st->capacity);
   }
   // Resolve specs and tables under the same lock order as Clear
-  // (cpu_embedding_engine.cc:161-186).
+  // (cpu_embedding_engine.cc:174-200).
   std::vector<std::shared_ptr<Table>> tables(static_cast<size_t>(n));
   {
     std::lock_guard<std::mutex> spec_lock(engine->specs_mu);

@@ -454,7 +454,7 @@ int CombineFromManifest(const std::string& mode, const std::string& table,
   return XSE_OK;
 }
 
-// LoadCpuEmbeddingEngine (cpu_embedding_resource.cc:83-211).
+// LoadCpuEmbeddingEngine (cpu_embedding_resource.cc:97-225).
 int LoadResource(xse_resource* res, const std::string& manifest_path,
                  const std::unordered_map<std::string, std::string>& tables) {
   std::string text;
@@ -582,7 +582,7 @@ struct Prepared {
   int32_t dim = 0;
   int64_t out_elems = 0;
   // Shape of the output host buffer (AllocateOutput,
-  // cpu_embedding_lookup_transform.cc:47-56).
+  // cpu_embedding_lookup_transform.cc:61-70).
   int32_t out_rank = 2;
   int64_t out_dims[2] = {0, 0};
 };
@@ -736,7 +736,7 @@ struct xse_dense_lookup_transform {
 
 namespace {
 
-// ValidateLookupInputs (cpu_embedding_lookup_transform.cc:145-228).
+// ValidateLookupInputs (cpu_embedding_lookup_transform.cc:159-242).
 int ValidateLookupInputs(const xse_host_buffer& ids,
                          const xse_host_buffer& rp,
                          const xse_host_buffer& w) {
@@ -948,7 +948,7 @@ int xse_lookup_transform_create(xse_resource* resource,
                                 int64_t embedding_dim,
                                 xse_lookup_transform** out) {
   // CpuEmbeddingLookupTransform::Create (cpu_embedding_lookup_transform.cc:
-  // 73-137).
+  // 87-151).
   if (out == nullptr) return Fail(XSE_INVALID_ARGUMENT, "out is null");
   if (resource == nullptr) {
     return Fail(XSE_INVALID_ARGUMENT,
@@ -1014,7 +1014,7 @@ int xse_lookup_transform_run(xse_lookup_transform* t,
                              int32_t num_weights, xse_host_buffer* outputs,
                              void* stream) {
   // CpuEmbeddingLookupTransform::operator() (cpu_embedding_lookup_
-  // transform.cc:230-342).
+  // transform.cc:244-356).
   if (t == nullptr || outputs == nullptr) {
     return Fail(XSE_INVALID_ARGUMENT, "transform and outputs must be non-null");
   }
@@ -1119,7 +1119,7 @@ int xse_dense_lookup_transform_create(xse_resource* resource,
                                       int32_t num_output_names,
                                       xse_dense_lookup_transform** out) {
   // DenseCpuEmbeddingLookupTransform::Create (dense_cpu_embedding_lookup_
-  // transform.cc:62-85).
+  // transform.cc:76-99).
   if (out == nullptr) return Fail(XSE_INVALID_ARGUMENT, "out is null");
   if (resource == nullptr) {
     return Fail(XSE_INVALID_ARGUMENT,
@@ -1161,7 +1161,7 @@ int xse_dense_lookup_transform_run(xse_dense_lookup_transform* t,
                                    int32_t num_inputs,
                                    xse_host_buffer* outputs, void* stream) {
   // DenseCpuEmbeddingLookupTransform::operator() (dense_cpu_embedding_
-  // lookup_transform.cc:134-254).
+  // lookup_transform.cc:148-268).
   if (t == nullptr || outputs == nullptr) {
     return Fail(XSE_INVALID_ARGUMENT, "transform and outputs must be non-null");
   }
@@ -1206,7 +1206,7 @@ int xse_dense_lookup_transform_run(xse_dense_lookup_transform* t,
                   fname, d.dtype);
     }
     // Keep non-pad ids; an all-pad row keeps one pad id
-    // (dense_cpu_embedding_lookup_transform.cc:183-206).
+    // (dense_cpu_embedding_lookup_transform.cc:197-212).
     Prepared& p = prep[f];
     p.active_ids.reserve(static_cast<size_t>(num_elements));
     p.generated_rp.reserve(static_cast<size_t>(batch) + 1);

@@ -26,6 +26,10 @@ from .engine import BagRequest, EmbeddingEngine, Status, stream_handle
 
 BOTTOM_MLP = (512, 256, 128)
 TOP_MLP = (1024, 1024, 512, 256, 1)
+# Dense-layer arithmetic of the tower: C.MATH_FP32 (CUDA-core fp32 GEMMs),
+# C.MATH_TF32 (one TF32 GEMM: reduced precision), or MATH_TF32X3 (three TF32
+# tensor-core GEMMs over hi/lo split operands: fp32-level accuracy).
+MATH_TF32X3 = 3
 
 
 def interaction_width(num_tables, dim):
@@ -59,6 +63,24 @@ def init_dense_layers(in_dim, dims, rng, last_sigmoid):
     layers.append((kernel, bias, act))
     prev = out
   return layers
+
+
+def tf32_split(x, hi, lo, stream=None):
+  """hi = x rounded to TF32, lo = x - hi (2-D tensors of x's layout)."""
+  C.check(C.lib.xse_tf32_split(x.data_ptr(), x.shape[0], x.shape[1],
+                               x.stride(0), hi.data_ptr(), lo.data_ptr(),
+                               stream_handle(stream)))
+
+
+def linear_tf32x3(x_hi, x_lo, k_hi, k_lo, layer: DenseLayer, out, *,
+                  stream=None):
+  """out = act(x K + b) from split operands (xse_linear_forward_tf32x3)."""
+  C.check(C.lib.xse_linear_forward_tf32x3(
+      x_hi.data_ptr(), x_lo.data_ptr(), x_hi.shape[0], k_hi.shape[0],
+      x_hi.stride(0), k_hi.data_ptr(), k_lo.data_ptr(), layer.bias.data_ptr(),
+      k_hi.shape[1], layer.activation, out.data_ptr(), out.stride(0),
+      stream_handle(stream)))
+  return out
 
 
 def linear(x, layer: DenseLayer, out, *, math=C.MATH_FP32, stream=None):
@@ -98,6 +120,17 @@ class DenseTower:
       k = self.top[0].kernel
       self.top[0].kernel = torch.cat(
           [k, torch.zeros((pad, k.shape[1]), dtype=k.dtype, device=k.device)])
+    # Split-TF32 layers: every layer whose input width is a multiple of 4
+    # except the 1-wide sigmoid head (own fp32 kernel); the 13-wide first
+    # bottom layer stays on fp32 FMA (0.6 % of the tower's FLOPs).
+    self._split = {}
+    if math == MATH_TF32X3:
+      for layer in self.bottom + self.top:
+        k = layer.kernel
+        if k.shape[0] % 4 == 0 and layer.activation != C.ACT_SIGMOID:
+          hi, lo = torch.empty_like(k), torch.empty_like(k)
+          tf32_split(k, hi, lo)
+          self._split[id(layer)] = (hi, lo)
     self.device = device
     self.math = math
     self._buffers = {}
@@ -118,6 +151,9 @@ class DenseTower:
           "inter": torch.empty((batch, self.width_stride), **f),
           "top": [torch.empty((batch, l.kernel.shape[1]), **f)
                   for l in self.top],
+          # split inputs of the widest layer, reused by every split layer
+          "hi": torch.empty(batch * max(self.width_stride, 1024), **f),
+          "lo": torch.empty(batch * max(self.width_stride, 1024), **f),
       }
       self._buffers[batch] = bufs
     return bufs
@@ -129,7 +165,7 @@ class DenseTower:
     bufs = self._buffers_for(batch)
     x = dense
     for layer, out in zip(self.bottom, bufs["bottom"]):
-      x = linear(x, layer, out, math=self.math, stream=stream)
+      x = self._layer(x, layer, out, bufs, stream)
     inter = bufs["inter"]
     C.check(C.lib.xse_dot_interaction_strided(
         x.data_ptr(), x.stride(0), pooled.data_ptr(), pooled.stride(0), batch,
@@ -137,8 +173,21 @@ class DenseTower:
         stream_handle(stream)))
     x = inter
     for layer, out in zip(self.top, bufs["top"]):
-      x = linear(x, layer, out, math=self.math, stream=stream)
+      x = self._layer(x, layer, out, bufs, stream)
     return x.view(-1)
+
+  def _layer(self, x, layer, out, bufs, stream):
+    split = self._split.get(id(layer))
+    if split is not None and x.stride(0) != layer.kernel.shape[0]:
+      split = None  # the split buffers are dense [rows, in]
+    if split is None:
+      math = C.MATH_FP32 if self.math == MATH_TF32X3 else self.math
+      return linear(x, layer, out, math=math, stream=stream)
+    rows, width = x.shape[0], layer.kernel.shape[0]
+    hi = bufs["hi"][:rows * width].view(rows, width)
+    lo = bufs["lo"][:rows * width].view(rows, width)
+    tf32_split(x[:, :width], hi, lo, stream)
+    return linear_tf32x3(hi, lo, split[0], split[1], layer, out, stream=stream)
 
   def reference_forward(self, dense, pooled):
     """The same forward in float64 torch on the host, for tests."""

@@ -1,7 +1,7 @@
 """Python handle on the B200 embedding engine (C ABI in include/xse_emb.h).
 
 Mirrors CpuEmbeddingEngine (data/cpu_embedding/cc/cpu_embedding_engine.h:
-27-89) of openxla/xla-serving: tables and feature specs are registered once,
+41-103) of openxla/xla-serving: tables and feature specs are registered once,
 then groups of CSR lookups run in one call. Tensors are torch CUDA tensors;
 torch is used only for device memory and streams, all compute runs in the
 engine's CUDA kernels.
@@ -54,7 +54,7 @@ def combine_code(combine):
 @dataclasses.dataclass
 class BagRequest:
   """One feature's CSR lookup (CpuEmbeddingEngine::FeatureBatchInput,
-  cpu_embedding_engine.h:41-48), on device memory."""
+  cpu_embedding_engine.h:55-62), on device memory."""
 
   feature_name: str
   ids: torch.Tensor
