@@ -645,9 +645,11 @@ _ELEM = {"f32": 4, "bf16": 2, "i8": 1}
 class ConfigWorkload:
   """Tables, inputs and the exchange of one CONFIGS entry on this rank."""
 
-  def __init__(self, xse, cfg, rank, world, exchange):
+  def __init__(self, xse, cfg, rank, world, exchange, max_rows=None):
     from xla_serving_b200 import sharding, synth  # pylint: disable=import-outside-toplevel
     C = xse._capi
+    if max_rows:  # smaller tables, for profiler captures
+      cfg = dict(cfg, vocab=min(cfg["vocab"], int(max_rows)))
     self.xse, self.cfg, self.world = xse, cfg, world
     dt = {"f32": C.DT_F32, "bf16": C.DT_BF16, "i8": C.DT_I8_ROWWISE}[
         cfg["dtype"]]
@@ -777,7 +779,7 @@ def run_config(args, name):
   world, rank, local = init_distributed()
   torch.cuda.set_device(local)
   xse = load_package()
-  wl = ConfigWorkload(xse, cfg, rank, world, args.exchange)
+  wl = ConfigWorkload(xse, cfg, rank, world, args.exchange, args.max_rows)
   clocks = ClockSampler(local)
   clocks.start()
   for i in range(args.warmup):
@@ -822,7 +824,10 @@ def run_config(args, name):
         "scaling": "weak" if name == "zipf_single" else "strong",
         "vs_baseline": None,
         "dtype": cfg["dtype"], "data": "synthetic (seeded counter RNG)",
-        "config": {"workload": cfg["desc"], "global_batch": cfg["batch"],
+        "config": {"workload": cfg["desc"] + (
+                       f" (rows capped at {int(args.max_rows):,} for a "
+                       "profiler capture)" if args.max_rows else ""),
+                   "global_batch": cfg["batch"],
                    "tables_total": wl.num_tables,
                    "tables_per_gpu": len(wl.local),
                    "rows_per_gpu": wl.window[1] - wl.window[0],
@@ -890,6 +895,9 @@ def main():
                   help="timed DLRM forward steps (0: skip the DLRM forward)")
   ap.add_argument("--dlrm-max-rows", type=float, default=None,
                   help="cap the DLRM tables' rows (profiler captures)")
+  ap.add_argument("--max-rows", type=float, default=None,
+                  help="cap the tables' rows of a --workload config "
+                       "(profiler captures)")
   ap.add_argument("--workload", default="multi_table",
                   choices=["multi_table", "dlrm"] + sorted(CONFIGS),
                   help="multi_table (the headline line, with the DLRM "

@@ -332,3 +332,32 @@ def test_dtype_table_views(xse):
   info = eng.table_info("t")
   assert (info.vocab, info.dim, info.combine) == (4, 8, 2)
   eng.close()
+
+
+@pytest.mark.parametrize("dtype,dim", [(oracle.F32, 64), (oracle.BF16, 128),
+                                       (oracle.F32, 128), (oracle.BF16, 64)])
+def test_large_launch_parity(xse, dtype, dim):
+  """Launches larger than one wave of lane groups take the throughput
+  kernel (4 rows in flight); small ones take the latency variant (8). Both
+  must give the oracle's bits: a 16,000-bag batch (weighted mean and plain
+  sum) against the small-batch result of the same bags."""
+  rng = np.random.default_rng(dim + 7 * dtype)
+  vocab = 50_000
+  host, dev, scale, bias = random_table(rng, dtype, vocab, dim)
+  eng = xse.EmbeddingEngine(0)
+  for combine in ("SUM", "MEAN"):
+    eng.add_table(f"t_{combine}", dev, combine)
+    eng.register_feature(f"f_{combine}", f"t_{combine}")
+  ids, offsets = random_csr(rng, vocab, 16_000, 30)
+  w = rng.uniform(0, 1, len(ids)).astype(np.float32)
+  for combine, weights in (("SUM", None), ("MEAN", w)):
+    got = eng.pool(f"f_{combine}", to_dev(ids), to_dev(offsets),
+                   None if weights is None else to_dev(weights))
+    want = oracle_pool(host, dtype, ids, offsets, weights, combine, scale,
+                       bias)
+    assert_bitwise(got.cpu().numpy(), want, f"large {combine}")
+    # The first 200 bags alone (a small launch) give the same rows.
+    small = eng.pool(f"f_{combine}", to_dev(ids), to_dev(offsets[:201]),
+                     None if weights is None else to_dev(weights))
+    assert_bitwise(small.cpu().numpy(), want[:200], f"small {combine}")
+  eng.close()

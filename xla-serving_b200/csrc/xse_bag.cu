@@ -300,12 +300,11 @@ __device__ __forceinline__ void AddGathered(
 // Full batch of U rows of a chunk whose ids all contribute: no per-row
 // checks. Lanes past the end of a non-exact row add zeros to accumulator
 // lanes that are never stored.
-template <int DT, int G, int V, bool EXACT, int WM, typename Hook>
+template <int DT, int G, int V, bool EXACT, int WM, int U, typename Hook>
 __device__ __forceinline__ void FullBatch(
     const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
     int my_row, float my_w, int j0, int cnt,
     u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, Hook&& hook) {
-  constexpr int U = RowsInFlight<DT, V>::value;
   const int stride = EXACT ? G * V : row_vecs;
   uint4 raw[U][V];
   float2 sb[U];
@@ -354,12 +353,11 @@ __device__ __forceinline__ void FullBatch(
 
 // General batch: up to U rows (positions j0..j0+n-1 of the chunk), skipping
 // ids that contribute nothing.
-template <int DT, int G, int V, bool EXACT, int WM, typename Hook>
+template <int DT, int G, int V, bool EXACT, int WM, int U, typename Hook>
 __device__ __forceinline__ void GatherBatch(
     const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
     int my_row, float my_w, int j0, int n,
     u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, Hook&& hook) {
-  constexpr int U = RowsInFlight<DT, V>::value;
   const int stride = EXACT ? G * V : row_vecs;
   uint4 raw[U][V];
   float2 sb[U];
@@ -484,11 +482,17 @@ __device__ __forceinline__ void LoadChunk(const BagDesc& d, int64_t pos,
 // or the first of the next bag -- is loaded while the current chunk's first
 // rows are in flight, so a bag's dependent loads (offsets, then ids, then
 // rows) overlap the previous bag's row gathers.
-template <int DT, int G, int V, bool EXACT, int WM>
-__global__ void __launch_bounds__(kThreads, MinBlocks<DT, V>::value)
+//
+// UR selects the rows in flight per batch: 0 takes the throughput setting
+// (RowsInFlight, sized for MinBlocks resident blocks); a deep setting (a
+// whole id chunk) serves launches too small to fill the GPU, where each
+// group pools one or two bags and every batch is a full memory round trip.
+template <int DT, int G, int V, bool EXACT, int WM, int UR>
+__global__ void __launch_bounds__(kThreads,
+                                  UR == 0 ? MinBlocks<DT, V>::value : 2)
     PoolVecKernel(const __grid_constant__ PoolParams p) {
   constexpr int PPV = ElemsPerVec<DT>::value / 2;
-  constexpr int U = RowsInFlight<DT, V>::value;
+  constexpr int U = UR == 0 ? RowsInFlight<DT, V>::value : UR;
   constexpr int kGroupsPerBlock = kThreads / G;
   if (!p.fused_checks && p.status->group_error != 0) return;
 
@@ -560,14 +564,14 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, V>::value)
         int j0 = 0;
         if (__all_sync(gmask, gl >= cnt || my_row >= 0)) {
           for (; j0 + U <= cnt; j0 += U) {
-            FullBatch<DT, G, V, EXACT, WM>(d, rows, row_vecs, gl, gmask,
+            FullBatch<DT, G, V, EXACT, WM, U>(d, rows, row_vecs, gl, gmask,
                                            my_row, my_w, j0, cnt, acc, &wsum,
                                            prefetch);
           }
         }
         for (; j0 < cnt; j0 += U) {
           const int n = cnt - j0 < U ? cnt - j0 : U;
-          GatherBatch<DT, G, V, EXACT, WM>(d, rows, row_vecs, gl, gmask,
+          GatherBatch<DT, G, V, EXACT, WM, U>(d, rows, row_vecs, gl, gmask,
                                            my_row, my_w, j0, n, acc, &wsum,
                                            prefetch);
         }
@@ -759,11 +763,32 @@ void AssignTasks(PoolParams* p, int runs) {
   p->total_tasks = tasks;
 }
 
+// Rows in flight of the latency-bound variant (twice the throughput
+// setting; register-limited to 2 resident blocks per SM).
+template <int DT, int G, int V>
+constexpr int DeepRows() {
+  return (DT == 2 || V != 1) ? 0 : (G < 8 ? G : 8);
+}
+
 template <int DT, int G, int V, bool EXACT, int WM>
 cudaError_t LaunchVec(const PoolParams& in, cudaStream_t stream) {
   PoolParams p = in;
   AssignTasks(&p, 1);
-  auto kernel = PoolVecKernel<DT, G, V, EXACT, WM>;
+  auto kernel = PoolVecKernel<DT, G, V, EXACT, WM, 0>;
+  constexpr int kDeep = DeepRows<DT, G, V>();
+  if constexpr (kDeep > 0) {
+    // Fewer bags than one wave of the throughput kernel's groups: every
+    // group pools about one bag, so latency (round trips per bag), not
+    // bandwidth, sets the time; gather a whole chunk per round trip.
+    const int64_t wave = static_cast<int64_t>(SmCount()) *
+                         BlocksPerSm(kernel) * (kThreads / G);
+    if (p.total_tasks <= wave) {
+      auto deep = PoolVecKernel<DT, G, V, EXACT, WM, kDeep>;
+      const int grid = GridFor(deep, p.total_tasks, kThreads / G);
+      deep<<<grid, kThreads, 0, stream>>>(p);
+      return cudaGetLastError();
+    }
+  }
   const int grid = GridFor(kernel, p.total_tasks, kThreads / G);
   kernel<<<grid, kThreads, 0, stream>>>(p);
   return cudaGetLastError();
