@@ -51,7 +51,7 @@ SEED = 0
 ROTATE = 8  # distinct input/output sets cycled between steps (> L2 in all)
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one step's
 # pooling kernels, from an ncu capture of this workload on a B200.
-POOL_DRAM_BYTES_PER_STEP = 314.98e6
+POOL_DRAM_BYTES_PER_STEP = 311.03e6
 ROW_BYTES = DIM * 2
 WORKLOAD = ("multi_table_bf16: 8 bf16 tables x 500,000 x 128 per GPU, batch "
             "8192, 20 ids per bag, uniform ids, tables 0-3 per-id weighted "
@@ -334,12 +334,11 @@ class DlrmWorkload:
 
   def step(self, i):
     dense, reqs, _, _ = self.sets[i % DLRM_ROTATE]
-    self.model.engine.execute_batch(reqs, status=self.status)
-    launches = self.xse.last_launch_count()
-    self.model.tower.forward(dense, self.model.pooled_buffer(DLRM_BATCH))
-    # Own kernels of the tower: interaction and sigmoid head (the six ReLU
-    # layers are cuBLASLt GEMMs).
-    return launches + 2
+    self.model.forward(dense, requests=reqs, status=self.status)
+    # Own kernels: the pooling launch (fused checks), the interaction, the
+    # sigmoid head and one operand split per split-TF32 layer (the GEMMs are
+    # cuBLASLt's).
+    return 1 + 2 + len(self.model.tower._split)
 
   def pool_bytes(self, v):
     """Algorithmic bytes of variant v's pooled lookup."""

@@ -252,5 +252,9 @@ class DLRM:
       requests, pooled = self.requests(ids, offsets, weights)
     else:
       pooled = self.pooled_buffer(dense.shape[0])
-    self.engine.execute_batch(requests, stream=stream, status=status)
+    # Fused checks: the pooled rows are internal to the forward, so a
+    # failing group need not leave them untouched (the error is still
+    # raised, or reported by status.wait()); no separate validation pass.
+    self.engine.execute_batch(requests, stream=stream, status=status,
+                              fused=True)
     return self.tower.forward(dense, pooled, stream=stream)
