@@ -83,9 +83,9 @@ float RowValue(const oracle_request& r, int64_t id, int64_t c) {
     case ORACLE_BF16:
       return Bf16ToFloat(static_cast<const uint16_t*>(r.table)[at]);
     default: {
+      // Row-wise dequantisation q * scale + bias with one rounding.
       const float q = static_cast<float>(static_cast<const int8_t*>(r.table)[at]);
-      const float scaled = q * r.scale[id];
-      return scaled + r.bias[id];
+      return std::fmaf(q, r.scale[id], r.bias[id]);
     }
   }
 }

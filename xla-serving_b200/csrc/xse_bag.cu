@@ -71,10 +71,14 @@ struct ElemsPerVec<2> {
 #define XSE_POOL_PREFETCH 1
 #endif
 
+#ifndef XSE_POOL_I8_ROWS
+#define XSE_POOL_I8_ROWS 2
+#endif
+
 // Rows gathered per batch (in flight per lane, times V vectors each).
 template <int DT, int V>
 struct RowsInFlight {
-  static constexpr int base = DT == 2 ? XSE_POOL_ROWS / 2 : XSE_POOL_ROWS;
+  static constexpr int base = DT == 2 ? XSE_POOL_I8_ROWS : XSE_POOL_ROWS;
   static constexpr int value = V >= base ? 1 : base / V;
 };
 
@@ -112,6 +116,11 @@ __device__ __forceinline__ u64 Mul2(u64 a, u64 b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ u64 Fma2(u64 a, u64 b, u64 c) {
+  u64 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
 
 __device__ __forceinline__ int64_t LoadIndex(const void* base, int is64,
                                              int64_t i) {
@@ -143,11 +152,6 @@ __device__ __forceinline__ void PrefetchRowVec(const uint4* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
-__device__ __forceinline__ float I8At(uint32_t w, int k) {
-  // Sign-extend byte k of w.
-  return __int2float_rn(static_cast<int>(w << (24 - 8 * k)) >> 24);
-}
-
 // Products are scalar mul.rn.f32, which PTX never contracts into an FMA; a
 // packed mul.rn.f32x2 feeding a packed add can be fused by the assembler,
 // which would round once instead of twice and break bit parity.
@@ -156,7 +160,10 @@ __device__ __forceinline__ u64 MulPair(float a, float lo, float hi) {
 }
 
 // One 16-byte row vector as fp32 pairs: int8 rows dequantized as
-// float(q)*scale + bias, each step rounded separately.
+// fma(float(q), scale, bias) (one rounding). A byte b becomes float(b)
+// exactly by placing b + 128 (b ^ 0x80) in the low mantissa bits of 2^23
+// (one byte permute) and subtracting 2^23 + 128; pairs then take one packed
+// fma.
 template <int DT>
 __device__ __forceinline__ void UnpackPairs(
     const uint4& r, float scale, u64 b2,
@@ -169,10 +176,18 @@ __device__ __forceinline__ void UnpackPairs(
 #pragma unroll
     for (int k = 0; k < 4; ++k) x[k] = PackBits(w[k] << 16, w[k] & 0xffff0000u);
   } else {
+    constexpr uint32_t kTwo23 = 0x4B000000u;         // 2^23
+    const u64 neg_magic = PackF(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+    const u64 s2 = PackF(scale, scale);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      x[2 * k] = Add2(MulPair(scale, I8At(w[k], 0), I8At(w[k], 1)), b2);
-      x[2 * k + 1] = Add2(MulPair(scale, I8At(w[k], 2), I8At(w[k], 3)), b2);
+      const uint32_t t = w[k] ^ 0x80808080u;
+      const u64 lo = PackBits(__byte_perm(t, kTwo23, 0x7440),
+                              __byte_perm(t, kTwo23, 0x7441));
+      const u64 hi = PackBits(__byte_perm(t, kTwo23, 0x7442),
+                              __byte_perm(t, kTwo23, 0x7443));
+      x[2 * k] = Fma2(Add2(lo, neg_magic), s2, b2);
+      x[2 * k + 1] = Fma2(Add2(hi, neg_magic), s2, b2);
     }
   }
 }
@@ -644,7 +659,7 @@ __global__ void __launch_bounds__(kThreads)
               const float2 sb = __ldg(d.scale_bias + r);
               const float q = __int2float_rn(
                   __ldg(static_cast<const signed char*>(d.rows) + at));
-              x = __fadd_rn(__fmul_rn(q, sb.x), sb.y);
+              x = __fmaf_rn(q, sb.x, sb.y);
             }
             acc[k] = weighted ? __fadd_rn(acc[k], __fmul_rn(w, x))
                               : __fadd_rn(acc[k], x);
