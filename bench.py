@@ -255,8 +255,17 @@ class Workload:
     if self.world == 1:
       self.pooler(self.requests[v])
     else:
-      self.exchange.run(self.steps[v])
+      # Nothing reads the received rows here: each step's barrier overlaps
+      # the next step's pooling; finish() waits for the last one.
+      self.exchange.run(self.steps[v], wait=False)
+      if self.exchange.peers is not None:
+        return self.pooler.launches - before + 1  # the barrier kernel
     return self.pooler.launches - before
+
+  def finish(self):
+    """Orders the current stream after every exchange issued so far."""
+    if self.world > 1:
+      self.exchange.ready()
 
   def ids_per_step(self):
     return NUM_TABLES * BATCH * BAG
@@ -650,6 +659,7 @@ class ConfigWorkload:
     if max_rows:  # smaller tables, for profiler captures
       cfg = dict(cfg, vocab=min(cfg["vocab"], int(max_rows)))
     self.xse, self.cfg, self.world = xse, cfg, world
+    self.sharding = sharding
     dt = {"f32": C.DT_F32, "bf16": C.DT_BF16, "i8": C.DT_I8_ROWWISE}[
         cfg["dtype"]]
     self.dtype = dt
@@ -689,8 +699,9 @@ class ConfigWorkload:
         nnz += fb.ids.numel()
       self.inputs.append(feats)
       self.nnz.append(nnz)
-    n_req = len(local) * (world if rowwise else 1)
-    self.status = xse.Status(max(n_req, 1))
+    # Requests per group: every table once per destination block (row-wise
+    # chunks and the peer exchange); fewer for the other modes.
+    self.status = xse.Status(max(len(local) * world, 1))
     self.pooler = sharding.engine_pooler(self.engine, self.status)
     if rowwise:
       self.exchange = sharding.RowwiseExchange(
@@ -705,8 +716,17 @@ class ConfigWorkload:
 
   def step(self, i):
     before = self.pooler.launches
-    self.exchange.run(self.steps[i % len(self.steps)])
-    return self.pooler.launches - before
+    if isinstance(self.exchange, self.sharding.TablewiseExchange):
+      self.exchange.run(self.steps[i % len(self.steps)], wait=False)
+      extra = 1 if self.exchange.peers is not None else 0
+    else:
+      self.exchange.run(self.steps[i % len(self.steps)])
+      extra = 0
+    return self.pooler.launches - before + extra
+
+  def finish(self):
+    if isinstance(self.exchange, self.sharding.TablewiseExchange):
+      self.exchange.ready()
 
   def pool_bytes(self, v):
     """Algorithmic bytes of variant v's pooling on this rank: every id's row
@@ -783,6 +803,7 @@ def run_config(args, name):
   clocks.start()
   for i in range(args.warmup):
     wl.step(i)
+  wl.finish()
   wl.status.wait()
   torch.cuda.synchronize()
   barrier(world, local)
@@ -794,6 +815,7 @@ def run_config(args, name):
   start.record(stream)
   for i in range(args.steps):
     launches += wl.step(i)
+  wl.finish()
   end.record(stream)
   torch.cuda.synchronize()
   barrier(world, local)
@@ -925,6 +947,7 @@ def main():
 
   for i in range(args.warmup):
     wl.step(i)
+  wl.finish()
   wl.status.wait()
   torch.cuda.synchronize()
   barrier(world, local)
@@ -939,6 +962,7 @@ def main():
   start.record(stream)
   for i in range(args.steps):
     launches += wl.step(i)
+  wl.finish()
   end.record(stream)
   torch.cuda.synchronize()
   barrier(world, local)

@@ -172,6 +172,10 @@ class PeerGroup:
 
 
 MODES = ("a2a", "pipelined", "peer")
+# Receive slots of the peer exchange: a step may overwrite a slot once the
+# barrier of the step after its previous use has passed on every rank, so
+# three slots let one step's barrier overlap the next step's pooling.
+PEER_SLOTS = 3
 
 
 class TablewiseExchange:
@@ -192,8 +196,8 @@ class TablewiseExchange:
       send/recv (shifted pairwise schedule) while the next is pooled.
     peer: one group whose requests write every block straight into its
       owner's receive buffer over NVLink (CUDA IPC mappings), then one flag
-      barrier; receive buffers alternate between two slots so a step's
-      stores never overwrite the rows the previous step delivered.
+      barrier (on a side stream); receive buffers rotate over PEER_SLOTS
+      slots so a step's stores never overwrite rows still being read.
   """
 
   def __init__(self, plan: ShardPlan, batch: int, num_tables: int, dim: int,
@@ -217,12 +221,15 @@ class TablewiseExchange:
     self.peers = None
     self.send = None
     self._slot = 0
+    self._step = -1
     if mode == "peer" and w > 1:
       dev = torch.cuda.current_device() if device is None else (
           torch.device(device).index or torch.cuda.current_device())
-      self.peers = PeerGroup(plan, 2 * total * 4, dev, group)
+      self.peers = PeerGroup(plan, PEER_SLOTS * total * 4, dev, group)
       self._slots = [self.peers.local_view(s * total * 4, (total,))
-                     for s in range(2)]
+                     for s in range(PEER_SLOTS)]
+      self._side = torch.cuda.Stream()
+      self._done = [None] * PEER_SLOTS
     else:
       self.send = torch.empty((w, self.block, self.num_local, dim),
                               dtype=torch.float32, device=device)
@@ -291,7 +298,7 @@ class TablewiseExchange:
       return steps
     total = self.block * self.num_tables * self.dim
     groups = []
-    for slot in range(2):
+    for slot in range(PEER_SLOTS):
       reqs = []
       for dest in range(w):
         # Rank dest's slot holds [q][B/W][T_q][D]; this rank writes block r.
@@ -301,10 +308,13 @@ class TablewiseExchange:
       groups.append((slot, reqs))
     return groups
 
-  def run(self, steps):
-    """Pools and exchanges the groups of schedule(); on return the current
-    stream is ordered after the exchange (recv is ready for work queued on
-    it)."""
+  def run(self, steps, wait=True):
+    """Pools and exchanges the groups of schedule(). With wait (default) the
+    current stream is ordered after the exchange on return (recv is ready
+    for work queued on it). Peer mode with wait=False leaves the barrier on
+    a side stream so the next step's pooling overlaps it; call ready()
+    before reading recv. Either way the rows of a step must be consumed
+    (their readers queued) before the next run()."""
     w, r = self.plan.world, self.plan.rank
     if w == 1:
       for _, reqs in steps:
@@ -330,11 +340,35 @@ class TablewiseExchange:
       for work in works:
         work.wait()
       return self.recv
-    slot = 1 - self._slot
+    i = self._step + 1
+    slot = i % PEER_SLOTS
+    main = torch.cuda.current_stream()
+    # Step i overwrites the slot of step i - PEER_SLOTS on every rank. Each
+    # rank queued that step's readers before its own pooling of step
+    # i - PEER_SLOTS + 1, which the barrier of that step waited for.
+    prev = self._done[(i - PEER_SLOTS + 1) % PEER_SLOTS]
+    if i >= PEER_SLOTS - 1 and prev is not None:
+      main.wait_event(prev)
     self.pool(steps[slot][1])
-    self.peers.barrier()
+    pooled = torch.cuda.Event()
+    pooled.record(main)
+    self._side.wait_event(pooled)
+    self.peers.barrier(stream=self._side)
+    done = torch.cuda.Event()
+    done.record(self._side)
+    self._done[slot] = done
+    self._step = i
     self._slot = slot
+    if wait:
+      main.wait_event(done)
     return self.recv
+
+  def ready(self, stream=None):
+    """Orders `stream` (the current one by default) after the last
+    exchange's barrier."""
+    if self.peers is not None and self._done[self._slot] is not None:
+      (stream or torch.cuda.current_stream()).wait_event(
+          self._done[self._slot])
 
   def check(self):
     """Raises if a peer barrier gave up waiting (peer mode)."""
