@@ -401,3 +401,86 @@ def test_pinned_and_pageable_inputs(ops):
     got.close()
   for b in pinned:
     b.close()
+
+
+def test_concurrent_calls_from_threads(ops):
+  """Calls of one transform from several threads on their own streams run
+  concurrently (each takes its own staging slot); every call's outputs
+  match the oracle bit for bit."""
+  import threading  # pylint: disable=import-outside-toplevel
+  import torch  # pylint: disable=import-outside-toplevel
+  rng = np.random.default_rng(21)
+  vocab, dim = 4000, 32
+  table = rng.standard_normal((vocab, dim)).astype(np.float32)
+  res = make_resource(ops, {"table0": (table, "MEAN")})
+  t = ops.CpuEmbeddingLookupTransform(res, ["feature0"])
+  cases = []
+  for k in range(12):
+    lengths = rng.integers(0, 30, 300)
+    rp = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    ids = rng.integers(0, vocab, int(rp[-1])).astype(np.int64)
+    w = rng.random(len(ids)).astype(np.float32)
+    cases.append((ids, rp, w, oracle.embedding_bag(table, ids, rp, w,
+                                                   "MEAN")))
+  results = [None] * len(cases)
+  errors = []
+
+  def worker(start):
+    try:
+      stream = torch.cuda.Stream()
+      for k in range(start, len(cases), 3):
+        ids, rp, w, _ = cases[k]
+        results[k], = t([ids], [rp], [w], stream=stream)
+    except Exception as e:  # pylint: disable=broad-except
+      errors.append(e)
+
+  threads = [threading.Thread(target=worker, args=(s,)) for s in range(3)]
+  for th in threads:
+    th.start()
+  for th in threads:
+    th.join()
+  assert not errors, errors
+  for k, case in enumerate(cases):
+    np.testing.assert_array_equal(results[k], case[3])
+
+
+@pytest.mark.parametrize("dtype,batch,seq,pad", [
+    (np.int32, 5000, 37, 0), (np.int64, 1200, 300, 7), (np.int32, 3, 1, 5),
+    (np.int64, 4097, 2, -1)])
+def test_dense_transform_device_csr(ops, dtype, batch, seq, pad):
+  """The CSR built on the device (pad filter, all-pad rows keeping one pad
+  id, scanned row pointers) pools to the oracle's CSR + pooling bit for
+  bit, across multi-block scans, both id types and odd shapes."""
+  rng = np.random.default_rng(batch + seq)
+  vocab, dim = 997, 24
+  table = rng.standard_normal((vocab, dim)).astype(np.float32)
+  res = ops.CpuEmbeddingResource.empty()
+  res.engine.add_table("t", table, "MEAN")
+  res.engine.register_feature("f", "t")
+  res.register_embedding_dim("f", dim)
+  t = ops.DenseCpuEmbeddingLookupTransform(res, "f", pad_value=pad)
+  dense = rng.integers(0, vocab, (batch, seq)).astype(dtype)
+  dense[rng.random((batch, seq)) < 0.4] = pad
+  dense[rng.random(batch) < 0.05] = pad  # some all-pad rows
+  if pad < 0:
+    dense[dense == pad] = 3  # an out-of-range pad must never be kept
+  got, = t([dense])
+  ids, rp = oracle.dense_to_csr(dense, pad)
+  want = oracle.embedding_bag(table, ids, rp, None, "MEAN")
+  np.testing.assert_array_equal(got, want)
+
+
+def test_dense_transform_bad_id_message_from_device_csr(ops, xse):
+  """An out-of-range id is reported at its position in the CSR (after the
+  pad filter), exactly as when the CSR is built on the host."""
+  res = ops.CpuEmbeddingResource.empty()
+  res.engine.add_table("t", np.ones((10, 4), np.float32), "SUM")
+  res.engine.register_feature("f", "t")
+  res.register_embedding_dim("f", 4)
+  t = ops.DenseCpuEmbeddingLookupTransform(res, "f", pad_value=0)
+  dense = np.array([[1, 0, 2], [0, 0, 0], [3, 42, 0]], np.int64)
+  with pytest.raises(xse.XseError) as e:
+    t([dense])
+  # CSR ids: [1, 2, 0 (all-pad row), 3, 42] -> 42 at index 4.
+  assert e.value.message == ("FP32 embedding-bag request 0: Embedding ID (42) "
+                             "at index 4 is out of bounds [0, 10).")

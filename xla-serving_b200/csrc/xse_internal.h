@@ -110,6 +110,17 @@ cudaError_t LaunchDotInteraction(const float* dense, int64_t dense_stride,
                                  float* out, int64_t out_stride,
                                  cudaStream_t stream);
 
+// Dense ids -> CSR on the device (csrc/xse_dense_csr.cu): scratch bytes for
+// `batch` rows, the conversion (rp: batch + 1 int32, ids: capacity
+// batch * max(seq, 1) int64), and dense_lookup row pointers b * valency.
+size_t DenseCsrScratchBytes(int64_t batch);
+cudaError_t LaunchDenseToCsr(const void* dense, int is64, int64_t batch,
+                             int64_t seq, int64_t pad, int32_t* rp,
+                             int64_t* ids, void* scratch,
+                             size_t scratch_bytes, cudaStream_t stream);
+cudaError_t LaunchRowPointers(int32_t* rp, int64_t batch, int64_t valency,
+                              cudaStream_t stream);
+
 // Sets what xse_last_launch_count() reports for this thread.
 void SetLastLaunchCount(int32_t launches);
 

@@ -574,8 +574,6 @@ struct Prepared {
   int32_t ids_type = XSE_INDEX_I64;
   int64_t num_ids = 0;
   const int32_t* row_pointers = nullptr;  // host
-  std::vector<int32_t> generated_rp;       // dense lookups
-  std::vector<int64_t> active_ids;         // dense transform CSR
   int64_t num_row_pointers = 0;
   const float* weights = nullptr;
   int64_t num_weights = 0;
@@ -585,25 +583,80 @@ struct Prepared {
   // cpu_embedding_lookup_transform.cc:61-70).
   int32_t out_rank = 2;
   int64_t out_dims[2] = {0, 0};
+  // Dense [batch_size, dense_seq] ids (DenseCpuEmbeddingLookupTransform):
+  // `ids` holds them as given; the CSR (pad filter, all-pad rule, row
+  // pointers) is built on the device.
+  bool device_csr = false;
+  int64_t dense_seq = 0;
+  int64_t pad_value = 0;
+  // dense_lookup: row pointers b * valency are generated on the device.
+  int64_t device_rp_valency = -1;
 };
 
-// Device and pinned buffers of one operator, reused across calls.
+// Device buffers and the status block of one call in flight.
 struct Staging {
   int device = 0;
   DeviceArena dev;
+  xse_status* status = nullptr;
+  int32_t status_capacity = 0;
+  bool busy = false;
+  ~Staging() {
+    if (status != nullptr) xse_status_destroy(status);
+  }
+};
+
+// The staging slots of one operator. Each call takes a free slot (the pool
+// grows on demand), so calls from several threads on different streams run
+// concurrently: one call's input copies overlap another's output copies.
+struct StagingPool {
+  int device = 0;
   std::mutex mu;
+  std::vector<std::unique_ptr<Staging>> slots;
+
+  Staging* Acquire() {
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto& s : slots) {
+      if (!s->busy) {
+        s->busy = true;
+        return s.get();
+      }
+    }
+    slots.push_back(std::make_unique<Staging>());
+    Staging* s = slots.back().get();
+    s->device = device;
+    s->dev.device = device;
+    s->busy = true;
+    return s;
+  }
+  void Release(Staging* s) {
+    std::lock_guard<std::mutex> lock(mu);
+    s->busy = false;
+  }
+};
+
+class StagingLease {
+ public:
+  explicit StagingLease(StagingPool* pool) : pool_(pool), s_(pool->Acquire()) {}
+  ~StagingLease() { pool_->Release(s_); }
+  Staging* get() const { return s_; }
+
+ private:
+  StagingPool* pool_;
+  Staging* s_;
 };
 
 // Stages every feature's inputs in one pinned buffer, copies them to the
 // device in one transfer, runs the group and copies all outputs back in one
 // transfer. On success fills `outputs`; on failure nothing is returned.
-int RunGroup(xse_engine* engine, Staging* staging,
+int RunGroup(xse_engine* engine, StagingPool* staging_pool,
              const std::vector<std::string>& features,
              std::vector<Prepared>& prep, xse_host_buffer* outputs,
              cudaStream_t stream) {
   const size_t n = prep.size();
-  // Layout of the staged inputs and of the outputs.
-  std::vector<size_t> ids_at(n), rp_at(n), w_at(n), out_at(n);
+  // Layout of the staged inputs, of the outputs and of device-only CSR
+  // buffers (ids and scan scratch of dense features).
+  std::vector<size_t> ids_at(n), rp_at(n), w_at(n), out_at(n), csr_at(n),
+      scratch_at(n), scratch_bytes(n);
   size_t in_bytes = 0;
   for (size_t i = 0; i < n; ++i) {
     const Prepared& p = prep[i];
@@ -617,12 +670,34 @@ int RunGroup(xse_engine* engine, Staging* staging,
   size_t out_bytes = 0;
   for (size_t i = 0; i < n; ++i) {
     out_at[i] = out_bytes;
-    out_bytes = AlignUp(out_bytes + prep[i].out_elems * 4, 64);
+    out_bytes = AlignUp(out_bytes + prep[i].out_elems * 4, 256);
   }
-  std::lock_guard<std::mutex> lock(staging->mu);
+  size_t csr_bytes = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const Prepared& p = prep[i];
+    if (!p.device_csr) continue;
+    csr_at[i] = csr_bytes;
+    csr_bytes = AlignUp(
+        csr_bytes + p.batch_size * std::max<int64_t>(p.dense_seq, 1) * 8, 256);
+    scratch_bytes[i] = xse::DenseCsrScratchBytes(p.batch_size);
+    scratch_at[i] = csr_bytes;
+    csr_bytes = AlignUp(csr_bytes + scratch_bytes[i], 256);
+  }
+  StagingLease lease(staging_pool);
+  Staging* staging = lease.get();
   DeviceGuard guard(staging->device);
-  int code = staging->dev.Reserve(in_bytes + out_bytes + 64);
+  int code = staging->dev.Reserve(AlignUp(in_bytes, 256) +
+                                  AlignUp(out_bytes, 256) + csr_bytes + 64);
   if (code != XSE_OK) return code;
+  if (staging->status_capacity < static_cast<int32_t>(n)) {
+    if (staging->status != nullptr) xse_status_destroy(staging->status);
+    staging->status = nullptr;
+    staging->status_capacity = 0;
+    code = xse_status_create(std::max<int32_t>(static_cast<int32_t>(n), 8),
+                             &staging->status);
+    if (code != XSE_OK) return FailFromEngine(code);
+    staging->status_capacity = std::max<int32_t>(static_cast<int32_t>(n), 8);
+  }
   PinnedPool& pool = PinnedPool::Get();
   PinnedBlock* in_block = pool.Acquire(std::max<size_t>(in_bytes, 64));
   PinnedBlock* out_block = pool.Acquire(std::max<size_t>(out_bytes, 64));
@@ -634,6 +709,7 @@ int RunGroup(xse_engine* engine, Staging* staging,
   char* host_in = static_cast<char*>(in_block->ptr);
   char* dev_in = static_cast<char*>(staging->dev.ptr);
   char* dev_out = dev_in + AlignUp(in_bytes, 256);
+  char* dev_csr = dev_out + AlignUp(out_bytes, 256);
   // Inputs already in pinned memory go straight to the device; the others
   // are gathered into the pinned staging block and sent in one transfer.
   cudaError_t e = cudaSuccess;
@@ -652,12 +728,29 @@ int RunGroup(xse_engine* engine, Staging* staging,
   for (size_t i = 0; i < n; ++i) {
     const Prepared& p = prep[i];
     stage(p.ids, ids_at[i], p.num_ids * (p.ids_type == XSE_INDEX_I64 ? 8 : 4));
-    stage(p.row_pointers, rp_at[i], p.num_row_pointers * 4);
+    if (p.row_pointers != nullptr) {
+      stage(p.row_pointers, rp_at[i], p.num_row_pointers * 4);
+    }
     stage(p.weights, w_at[i], p.num_weights * 4);
   }
   if (e == cudaSuccess && hi > lo) {
     e = cudaMemcpyAsync(dev_in + lo, host_in + lo, hi - lo,
                         cudaMemcpyHostToDevice, stream);
+  }
+  // Row pointers (and dense features' CSR ids) built on the device.
+  for (size_t i = 0; i < n && e == cudaSuccess; ++i) {
+    const Prepared& p = prep[i];
+    int32_t* rp = reinterpret_cast<int32_t*>(dev_in + rp_at[i]);
+    if (p.device_csr) {
+      e = xse::LaunchDenseToCsr(
+          dev_in + ids_at[i], p.ids_type == XSE_INDEX_I64 ? 1 : 0,
+          p.batch_size, p.dense_seq, p.pad_value, rp,
+          reinterpret_cast<int64_t*>(dev_csr + csr_at[i]),
+          dev_csr + scratch_at[i], scratch_bytes[i], stream);
+    } else if (p.device_rp_valency >= 0) {
+      e = xse::LaunchRowPointers(rp, p.batch_size, p.device_rp_valency,
+                                 stream);
+    }
   }
   std::vector<xse_bag_request> reqs(n);
   for (size_t i = 0; i < n; ++i) {
@@ -668,6 +761,11 @@ int RunGroup(xse_engine* engine, Staging* staging,
     r.ids_type = p.ids_type;
     r.offsets_type = XSE_INDEX_I32;
     r.num_ids = p.num_ids;
+    if (p.device_csr) {
+      r.ids = dev_csr + csr_at[i];
+      r.ids_type = XSE_INDEX_I64;
+      r.num_ids = p.batch_size * std::max<int64_t>(p.dense_seq, 1);
+    }
     r.offsets = dev_in + rp_at[i];
     r.num_offsets = p.num_row_pointers;
     r.weights = p.num_weights > 0
@@ -678,16 +776,28 @@ int RunGroup(xse_engine* engine, Staging* staging,
     r.output_stride = 0;
   }
   if (e == cudaSuccess) {
+    // Asynchronous group on this call's own status block: the output copy
+    // is queued right behind the pooling, and the status read-back (which
+    // waits for the stream) decides whether the outputs are returned.
     code = xse_engine_execute_batch(engine, reqs.data(),
                                     static_cast<int32_t>(n), stream,
-                                    XSE_EXEC_STRICT, nullptr);
+                                    XSE_EXEC_STRICT | XSE_EXEC_ASYNC,
+                                    staging->status);
     if (code != XSE_OK) {
+      cudaStreamSynchronize(stream);
       pool.Release(in_block);
       pool.Release(out_block);
       return FailFromEngine(code);
     }
     e = cudaMemcpyAsync(out_block->ptr, dev_out, out_bytes,
                         cudaMemcpyDeviceToHost, stream);
+    code = xse_status_wait(staging->status, stream);
+    if (code != XSE_OK) {
+      cudaStreamSynchronize(stream);
+      pool.Release(in_block);
+      pool.Release(out_block);
+      return FailFromEngine(code);
+    }
   }
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   pool.Release(in_block);
@@ -723,7 +833,7 @@ struct xse_lookup_transform {
   std::vector<std::string> output_feature_names;
   bool dense_lookup = false;
   int64_t embedding_dim = 128;
-  Staging staging;
+  StagingPool staging;
 };
 
 struct xse_dense_lookup_transform {
@@ -731,7 +841,7 @@ struct xse_dense_lookup_transform {
   std::vector<std::string> feature_names;
   int64_t pad_value = 0;
   std::vector<std::string> output_feature_names;
-  Staging staging;
+  StagingPool staging;
 };
 
 namespace {
@@ -1078,11 +1188,9 @@ int xse_lookup_transform_run(xse_lookup_transform* t,
                     "Batch volume (batch_size * valency) exceeds INT32_MAX "
                     "bounds.");
       }
-      p.generated_rp.resize(static_cast<size_t>(p.batch_size) + 1);
-      for (int64_t b = 0; b <= p.batch_size; ++b) {
-        p.generated_rp[b] = static_cast<int32_t>(b * valency);
-      }
-      p.row_pointers = p.generated_rp.data();
+      // Row pointers b * valency, generated on the device.
+      p.device_rp_valency = valency;
+      p.row_pointers = nullptr;
       p.num_row_pointers = p.batch_size + 1;
     } else {
       const int code =
@@ -1206,40 +1314,24 @@ int xse_dense_lookup_transform_run(xse_dense_lookup_transform* t,
                   fname, d.dtype);
     }
     // Keep non-pad ids; an all-pad row keeps one pad id
-    // (dense_cpu_embedding_lookup_transform.cc:197-212).
-    Prepared& p = prep[f];
-    p.active_ids.reserve(static_cast<size_t>(num_elements));
-    p.generated_rp.reserve(static_cast<size_t>(batch) + 1);
-    p.generated_rp.push_back(0);
-    for (int64_t b = 0; b < batch; ++b) {
-      int32_t active = 0;
-      for (int64_t j = 0; j < seq; ++j) {
-        const int64_t id =
-            d.dtype == XSE_HB_S64
-                ? static_cast<const int64_t*>(d.data)[b * seq + j]
-                : static_cast<const int32_t*>(d.data)[b * seq + j];
-        if (id != t->pad_value) {
-          p.active_ids.push_back(id);
-          ++active;
-        }
-      }
-      if (active == 0) {
-        p.active_ids.push_back(t->pad_value);
-        active = 1;
-      }
-      const int64_t next = static_cast<int64_t>(p.generated_rp.back()) + active;
-      if (next > INT32_MAX) {
-        return Fail(XSE_INVALID_ARGUMENT,
-                    "Row pointer offset overflowed int32_t.");
-      }
-      p.generated_rp.push_back(static_cast<int32_t>(next));
+    // (dense_cpu_embedding_lookup_transform.cc:197-212): built on the device
+    // from the dense buffer as given. Each row keeps at most max(seq, 1) ids,
+    // so the row pointers stay within the checked element count (the
+    // reference's int32 overflow check cannot fire past the checks above).
+    if (batch * std::max<int64_t>(seq, 1) > INT32_MAX) {
+      return Fail(XSE_INVALID_ARGUMENT,
+                  "Row pointer offset overflowed int32_t.");
     }
-    p.ids = p.active_ids.data();
-    p.ids_type = XSE_INDEX_I64;
-    p.num_ids = static_cast<int64_t>(p.active_ids.size());
-    p.row_pointers = p.generated_rp.data();
-    p.num_row_pointers = static_cast<int64_t>(p.generated_rp.size());
+    Prepared& p = prep[f];
+    p.ids = d.data;
+    p.ids_type = d.dtype == XSE_HB_S64 ? XSE_INDEX_I64 : XSE_INDEX_I32;
+    p.num_ids = batch * seq;
+    p.row_pointers = nullptr;
+    p.num_row_pointers = batch + 1;
     p.batch_size = batch;
+    p.device_csr = true;
+    p.dense_seq = seq;
+    p.pad_value = t->pad_value;
   }
   for (int32_t f = 0; f < nf; ++f) {
     int32_t dim = 0;
