@@ -49,7 +49,7 @@ BATCH = 8192
 BAG = 20
 SEED = 0
 ROTATE = 8  # distinct input/output sets cycled between steps (> L2 in all)
-E2E_THREADS = 4  # concurrent host callers of the operator in the e2e run
+E2E_THREADS = 2  # concurrent host callers of the operator in the e2e run
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one step's
 # pooling kernels, from an ncu capture of this workload on a B200.
 POOL_DRAM_BYTES_PER_STEP = 311.03e6

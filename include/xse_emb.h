@@ -180,6 +180,24 @@ int xse_engine_execute_batch(xse_engine* engine, const xse_bag_request* reqs,
  * with this block (and its message through xse_last_error). */
 int xse_status_wait(xse_status* status, void* stream);
 
+/* Replaces CpuEmbeddingEngine::Execute(Span<const FeatureBatchCsrInput>)
+ * (cpu_embedding_engine.cc:91-166), the per-feature path. For each request,
+ * a feature whose spec has max_sequence_length == 0 is pooled in its table's
+ * type (AssembleCombinedEmbeddings, compute_activations.cc:36-154): fp32 as
+ * xse_engine_execute_batch, bf16 accumulating in bf16 (every operation
+ * rounded to bf16), into output = [num_bags, dim]; a sequence feature
+ * gathers the rows of each sample's first max_sequence_length ids, zero
+ * padded, into output = [num_bags, max_sequence_length, dim] in the table's
+ * type (LookupEmbeddingSequence, compute_activations.cc:187-224, 321-346).
+ * `output` points to that array (bf16 as raw 16-bit values); output_stride
+ * is ignored. Requests follow FeatureBatchCsrInput (feature_batch_csr_
+ * input.cc:33-57): offsets start at 0 and end at num_ids, never decrease;
+ * weights empty or one per id (none for a sequence feature). Tables fp32 or
+ * bf16, whole (no shard window). At most 64 requests; synchronous; checked
+ * before any output is written; messages as the reference's. */
+int xse_engine_execute_legacy(xse_engine* engine, const xse_bag_request* reqs,
+                              int32_t n, void* stream);
+
 /* Allocation-free variant of xse_engine_execute_batch (strict mode,
  * synchronous). No counterpart in the reference, which pools on the host.
  *

@@ -54,6 +54,8 @@ def _load():
   lib.oracle_assemble_bf16_accumulate.argtypes = [P, I64, I64, I32, P, I64, P,
                                                   I64, P, P, ctypes.c_char_p,
                                                   I32]
+  lib.oracle_sequence_gather.argtypes = [P, I32, I64, I64, P, P, I64, I64, P,
+                                         P, I32]
   lib.oracle_dense_to_csr.argtypes = [P, I32, I64, I64, I64, P, P, P,
                                       ctypes.c_char_p, I32]
   lib.oracle_dense_lookup_row_pointers.argtypes = [I64, I64, P,
@@ -157,6 +159,22 @@ def assemble_bf16_accumulate(table_bits, ids, row_pointers, weights=None,
       _p(table_bits), table_bits.shape[0], table_bits.shape[1],
       COMBINE[combine], _p(ids), len(ids), _p(rp), len(rp), _p(w), _p(out),
       err, len(err))
+  if rc != OK:
+    raise OracleError(rc, err.value.decode())
+  return out
+
+
+def sequence_gather(table, ids, row_pointers, max_seq, dtype=F32):
+  """AssembleSequenceEmbeddings restatement: [samples, max_seq, dim] of the
+  table's type (fp32, or bf16 bits as uint16)."""
+  table = np.ascontiguousarray(table)
+  ids = np.ascontiguousarray(ids, dtype=np.int64)
+  rp = np.ascontiguousarray(row_pointers, dtype=np.int32)
+  out = np.zeros((len(rp) - 1, max_seq, table.shape[1]), dtype=table.dtype)
+  err = ctypes.create_string_buffer(1024)
+  rc = lib.oracle_sequence_gather(_p(table), dtype, table.shape[0],
+                                  table.shape[1], _p(ids), _p(rp), len(rp),
+                                  max_seq, _p(out), err, len(err))
   if rc != OK:
     raise OracleError(rc, err.value.decode())
   return out

@@ -584,6 +584,37 @@ int oracle_assemble_bf16_accumulate(const uint16_t* table, int64_t vocab,
   return ORACLE_OK;
 }
 
+int oracle_sequence_gather(const void* table, int32_t dtype, int64_t vocab,
+                           int64_t dim, const int64_t* ids,
+                           const int32_t* row_pointers,
+                           int64_t num_row_pointers, int64_t max_seq,
+                           void* out, char* err, int32_t errlen) {
+  // AssembleSequenceEmbeddings (compute_activations.cc:187-224).
+  const size_t elem = dtype == ORACLE_F32 ? 4 : 2;
+  const int64_t samples = num_row_pointers - 1;
+  for (int64_t s = 0; s < samples; ++s) {
+    const int64_t start = row_pointers[s];
+    const int64_t len = row_pointers[s + 1] - start;
+    const int64_t n = std::min(len, max_seq);
+    for (int64_t k = 0; k < n; ++k) {
+      const int64_t id = ids[start + k];
+      if (id < 0 || id >= vocab) {
+        return Fail(ORACLE_INVALID_ARGUMENT, err, errlen,
+                    "Embedding ID (%" PRId64 ") at index %" PRId64
+                    " is out of bounds [0, %" PRId64 ") for table table.",
+                    id, k, vocab);
+      }
+    }
+    char* dst = static_cast<char*>(out) + s * max_seq * dim * elem;
+    for (int64_t k = 0; k < n; ++k) {
+      std::memcpy(dst + k * dim * elem,
+                  static_cast<const char*>(table) + ids[start + k] * dim * elem,
+                  dim * elem);
+    }
+  }
+  return ORACLE_OK;
+}
+
 int oracle_dense_to_csr(const void* dense, int32_t dense_i64, int64_t batch,
                         int64_t seq, int64_t pad_value, int64_t* ids,
                         int32_t* row_pointers, int64_t* num_ids, char* err,

@@ -77,6 +77,16 @@ int oracle_assemble_bf16_accumulate(const uint16_t* table, int64_t vocab,
                                     const float* weights, uint16_t* out,
                                     char* err, int32_t errlen);
 
+/* AssembleSequenceEmbeddings (compute_activations.cc:187-224): out is
+ * [samples, max_seq, dim] of the table's type (ORACLE_F32 or ORACLE_BF16
+ * bits), zeroed by the caller; each sample's first min(len, max_seq) ids are
+ * bounds-checked (index = position within the sample) and their rows copied. */
+int oracle_sequence_gather(const void* table, int32_t dtype, int64_t vocab,
+                           int64_t dim, const int64_t* ids,
+                           const int32_t* row_pointers,
+                           int64_t num_row_pointers, int64_t max_seq,
+                           void* out, char* err, int32_t errlen);
+
 /* DenseCpuEmbeddingLookupTransform CSR build (dense_cpu_embedding_lookup_
  * transform.cc:186-225). dense is [batch, seq] int32 or int64. Writes ids
  * (capacity >= batch*seq + batch) and batch+1 int32 row pointers; returns the

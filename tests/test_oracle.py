@@ -231,3 +231,19 @@ def test_zipf_rank_distribution():
   for k in range(5):
     expected = p[k] * len(ranks)
     assert abs(counts[k] - expected) < 5 * np.sqrt(expected), k
+
+
+def test_sequence_gather_known_answer(golden):
+  """The oracle's AssembleSequenceEmbeddings against the reference test."""
+  case = golden["sequence"][0]
+  table = (np.arange(40, dtype=np.float32) * np.float32(0.1)).reshape(10, 4)
+  got = oracle.sequence_gather(table, case["ids"], case["offsets"],
+                               case["max_sequence_length"])
+  assert got.shape == (3, 5, 4)
+  np.testing.assert_allclose(got.ravel(), case["expect"], rtol=0,
+                             atol=case["tol"])
+  with pytest.raises(oracle.OracleError, match=r"\(12\) at index 1 "):
+    oracle.sequence_gather(table, [1, 12, 4], [0, 2, 3], 5)
+  # Ids past max_sequence_length are neither read nor checked.
+  got = oracle.sequence_gather(table, [1, 3, 99], [0, 3], 2)
+  np.testing.assert_array_equal(got[0], table[[1, 3]])

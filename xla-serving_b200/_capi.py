@@ -134,6 +134,8 @@ SIGNATURES = {
     "xse_status_wait": (_I, [_P, _P]),
     "xse_engine_execute_batch_noalloc": (_I, [_P, ctypes.POINTER(BagRequest),
                                               _I32, _P]),
+    "xse_engine_execute_legacy": (_I, [_P, ctypes.POINTER(BagRequest), _I32,
+                                       _P]),
     "xse_engine_set_profiling": (_I, [_P, _I32]),
     "xse_engine_profile_read": (_I, [_P, ctypes.POINTER(ctypes.c_double),
                                      ctypes.POINTER(_I64)]),

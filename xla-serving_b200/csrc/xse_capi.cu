@@ -1348,3 +1348,186 @@ extern "C" int xse_engine_execute_batch_noalloc(xse_engine* engine,
   }
   return Ok();
 }
+
+// ---------------------------------------------------------------------------
+// Legacy per-feature path (CpuEmbeddingEngine::Execute).
+
+namespace {
+
+int64_t ReadIndex(const void* base, int is64, int64_t i) {
+  int64_t v = 0;
+  if (is64) {
+    cudaMemcpy(&v, static_cast<const int64_t*>(base) + i, sizeof(v),
+               cudaMemcpyDeviceToHost);
+  } else {
+    int32_t v32 = 0;
+    cudaMemcpy(&v32, static_cast<const int32_t*>(base) + i, sizeof(v32),
+               cudaMemcpyDeviceToHost);
+    v = v32;
+  }
+  return v;
+}
+
+}  // namespace
+
+extern "C" int xse_engine_execute_legacy(xse_engine* engine,
+                                         const xse_bag_request* reqs,
+                                         int32_t n, void* stream) {
+  g_last_launches = 0;
+  if (engine == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null engine");
+  if (n < 0 || (n > 0 && reqs == nullptr)) {
+    return SetError(XSE_INVALID_ARGUMENT, "bad request list");
+  }
+  if (n > xse::kMaxDescsPerLaunch) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "At most %d features per legacy execution, got %d.",
+                    xse::kMaxDescsPerLaunch, n);
+  }
+  // FeatureBatchCsrInput::Create's host-visible check
+  // (feature_batch_csr_input.cc:36-39).
+  for (int32_t i = 0; i < n; ++i) {
+    if (reqs[i].num_offsets < 2) {
+      return SetError(XSE_INVALID_ARGUMENT,
+                      "Row pointers must have at least 2 elements.");
+    }
+  }
+  // Specs, then tables (cpu_embedding_engine.cc:98-124).
+  std::vector<Feature> specs(static_cast<size_t>(n));
+  std::vector<std::shared_ptr<Table>> tables(static_cast<size_t>(n));
+  {
+    std::lock_guard<std::mutex> spec_lock(engine->specs_mu);
+    for (int32_t i = 0; i < n; ++i) {
+      const char* fname = reqs[i].feature_name ? reqs[i].feature_name : "";
+      auto it = engine->features.find(fname);
+      if (it == engine->features.end()) {
+        return SetError(XSE_NOT_FOUND, "Feature spec not found for: %s", fname);
+      }
+      specs[i] = it->second;
+    }
+  }
+  {
+    std::lock_guard<std::mutex> table_lock(engine->tables_mu);
+    for (int32_t i = 0; i < n; ++i) {
+      auto it = engine->tables.find(specs[i].table);
+      if (it == engine->tables.end()) {
+        return SetError(XSE_NOT_FOUND, "Table not found for: %s",
+                        specs[i].table.c_str());
+      }
+      tables[i] = it->second;
+    }
+  }
+  xse::LegacyParams p = {};
+  p.n = n;
+  int64_t tasks = 0;
+  for (int32_t i = 0; i < n; ++i) {
+    const xse_bag_request& r = reqs[i];
+    const Table& t = *tables[i];
+    const bool sequence = specs[i].max_sequence_length > 0;
+    if (t.dtype != XSE_DT_F32 && t.dtype != XSE_DT_BF16) {
+      return SetError(XSE_INVALID_ARGUMENT, "Unsupported data type: %d",
+                      t.dtype);
+    }
+    if (t.row_begin != 0 || t.row_end != t.vocab) {
+      return SetError(XSE_FAILED_PRECONDITION,
+                      "Table %s holds a row-wise shard; the per-feature path "
+                      "needs whole tables.", t.name.c_str());
+    }
+    if (sequence && r.num_weights > 0) {
+      return SetError(XSE_INVALID_ARGUMENT,
+                      "Weights should be empty for sequence assembly.");
+    }
+    if ((r.num_ids > 0 && r.ids == nullptr) || r.offsets == nullptr ||
+        r.output == nullptr || (r.num_weights > 0 && r.weights == nullptr)) {
+      return SetError(XSE_INVALID_ARGUMENT,
+                      "Legacy request %d has a null buffer.", i);
+    }
+    xse::LegacyDesc& d = p.d[i];
+    d.rows = t.rows;
+    d.ids = r.ids;
+    d.offsets = r.offsets;
+    d.weights = r.num_weights > 0 ? r.weights : nullptr;
+    d.out = r.output;
+    d.vocab = t.vocab;
+    d.num_ids = r.num_ids;
+    d.num_weights = r.num_weights;
+    d.num_bags = r.num_offsets - 1;
+    d.task_begin = tasks;
+    d.max_seq = sequence ? specs[i].max_sequence_length : 0;
+    d.dim = t.dim;
+    d.slot = i;
+    d.combine = static_cast<int8_t>(t.combine);
+    d.ids64 = r.ids_type == XSE_INDEX_I64 ? 1 : 0;
+    d.offs64 = r.offsets_type == XSE_INDEX_I64 ? 1 : 0;
+    d.dtype = t.dtype == XSE_DT_F32 ? 0 : 1;
+    d.kind = sequence ? xse::kLegacySequence
+                      : (d.dtype == 0 ? xse::kLegacyPoolF32
+                                      : xse::kLegacyPoolBf16);
+    tasks += d.num_bags;
+  }
+  p.total_tasks = tasks;
+  DeviceGuard guard(engine->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t status_bytes = xse::DevStatusBytes(n > 0 ? n : 1);
+  void* dev_status = nullptr;
+  cudaError_t e = cudaMallocAsync(&dev_status, status_bytes, s);
+  if (e != cudaSuccess) return CudaError(e, "legacy status allocation");
+  e = cudaMemsetAsync(dev_status, 0, status_bytes, s);
+  p.status = static_cast<xse::DevStatus*>(dev_status);
+  if (e == cudaSuccess) e = xse::LaunchLegacy(p, s);
+  std::vector<unsigned char> host(status_bytes);
+  if (e == cudaSuccess) {
+    e = cudaMemcpyAsync(host.data(), dev_status, status_bytes,
+                        cudaMemcpyDeviceToHost, s);
+  }
+  cudaFreeAsync(dev_status, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return CudaError(e, "legacy execution");
+  g_last_launches = tasks > 0 ? 2 : 0;
+  const auto* st = reinterpret_cast<const xse::DevStatus*>(host.data());
+  if (st->group_error == 0) return Ok();
+  // FeatureBatchCsrInput's checks first (they precede Execute in the
+  // reference), in request order (feature_batch_csr_input.cc:36-54).
+  for (int32_t i = 0; i < n; ++i) {
+    const unsigned int f = st->req[i].flags;
+    const xse::LegacyDesc& d = p.d[i];
+    if (f & (xse::kLegacySizeMismatch | xse::kLegacyNotSorted |
+             xse::kLegacyWeights)) {
+      const int64_t last = ReadIndex(d.offsets, d.offs64, d.num_bags);
+      if (f & xse::kLegacySizeMismatch) {
+        return SetError(XSE_INVALID_ARGUMENT,
+                        "Embedding ids size (%" PRId64
+                        ") does not match last element of row pointers "
+                        "(%" PRId64 ")",
+                        d.num_ids, last);
+      }
+      if (f & xse::kLegacyNotSorted) {
+        return SetError(XSE_INVALID_ARGUMENT, "Row pointers are not sorted.");
+      }
+      return SetError(XSE_INVALID_ARGUMENT,
+                      "Weights size (%" PRId64
+                      ") does not match expected size (%" PRId64 ")",
+                      d.num_weights, last);
+    }
+  }
+  // Then the bounds scans (compute_activations.cc:89-98, 205-213).
+  for (int32_t i = 0; i < n; ++i) {
+    if ((st->req[i].flags & xse::kLegacyBadId) == 0) continue;
+    const xse::LegacyDesc& d = p.d[i];
+    const int64_t pos = static_cast<int64_t>(~st->req[i].inv_min_bad_index);
+    const int64_t id = ReadIndex(d.ids, d.ids64, pos);
+    int64_t index = pos;
+    if (d.kind == xse::kLegacySequence) {  // position within its sample
+      std::vector<int64_t> rp(static_cast<size_t>(d.num_bags) + 1);
+      for (int64_t b = 0; b <= d.num_bags; ++b) {
+        rp[b] = ReadIndex(d.offsets, d.offs64, b);
+      }
+      const auto it = std::upper_bound(rp.begin(), rp.end(), pos);
+      index = pos - *(it - 1);
+    }
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Embedding ID (%" PRId64 ") at index %" PRId64
+                    " is out of bounds [0, %" PRId64 ") for table %s.",
+                    id, index, d.vocab, tables[i]->name.c_str());
+  }
+  return SetError(XSE_INTERNAL, "legacy execution failed");
+}

@@ -110,6 +110,47 @@ cudaError_t LaunchDotInteraction(const float* dense, int64_t dense_stride,
                                  float* out, int64_t out_stride,
                                  cudaStream_t stream);
 
+// Legacy per-feature path (csrc/xse_legacy.cu): FeatureBatchCsrInput checks,
+// pooling in the table's type, sequence gather.
+enum : unsigned int {
+  kLegacySizeMismatch = 16u,  // first offset != 0 or last != number of ids
+  kLegacyNotSorted = 32u,     // offsets decrease
+  kLegacyWeights = 64u,       // weights neither empty nor one per id
+  kLegacyBadId = kErrBadId,   // an id read by the feature is out of range
+};
+enum : int8_t { kLegacyPoolF32 = 0, kLegacyPoolBf16 = 1, kLegacySequence = 2 };
+
+struct LegacyDesc {
+  const void* rows;      // [vocab, dim] fp32 or bf16
+  const void* ids;
+  const void* offsets;   // num_bags + 1 entries
+  const float* weights;  // nullptr or num_weights entries
+  void* out;             // [num_bags, dim] or [num_bags, max_seq, dim]
+  int64_t vocab;
+  int64_t num_ids;
+  int64_t num_weights;
+  int64_t num_bags;
+  int64_t task_begin;
+  int64_t max_seq;       // sequence features only
+  int32_t dim;
+  int32_t slot;
+  int8_t combine;
+  int8_t ids64;
+  int8_t offs64;
+  int8_t dtype;          // 0 fp32, 1 bf16
+  int8_t kind;           // kLegacy*
+};
+
+struct LegacyParams {
+  int32_t n;
+  int32_t reserved;
+  int64_t total_tasks;   // samples of all requests
+  DevStatus* status;
+  LegacyDesc d[kMaxDescsPerLaunch];
+};
+
+cudaError_t LaunchLegacy(const LegacyParams& p, cudaStream_t stream);
+
 // Dense ids -> CSR on the device (csrc/xse_dense_csr.cu): scratch bytes for
 // `batch` rows, the conversion (rp: batch + 1 int32, ids: capacity
 // batch * max(seq, 1) int64), and dense_lookup row pointers b * valency.

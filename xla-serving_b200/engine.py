@@ -249,6 +249,32 @@ class EmbeddingEngine:
     del names
     C.check(rc)
 
+  def execute_legacy(self, requests: Sequence[BagRequest], *, stream=None):
+    """CpuEmbeddingEngine::Execute: per request, a [num_bags, dim] pooled
+    array, or [num_bags, max_sequence_length, dim] for a sequence feature,
+    in the table's type (float32 or bfloat16; a bf16 table accumulates in
+    bf16). The requests' `output` fields are ignored; new tensors are
+    returned."""
+    outs = []
+    for r in requests:
+      try:
+        table, seq = self.feature_table(r.feature_name)
+        info = self.table_info(table)
+      except C.XseError:
+        outs.append(None)  # the engine call below reports the reference's error
+        continue
+      dtype = torch.bfloat16 if info.dtype == C.DT_BF16 else torch.float32
+      bags = max(r.offsets.numel() - 1, 0)
+      shape = (bags, seq, info.dim) if seq > 0 else (bags, info.dim)
+      outs.append(torch.empty(shape, dtype=dtype, device=r.offsets.device))
+    arr, names = self._c_requests(
+        [dataclasses.replace(r, output=o) for r, o in zip(requests, outs)])
+    rc = C.lib.xse_engine_execute_legacy(self._handle, arr, len(requests),
+                                         stream_handle(stream))
+    del names
+    C.check(rc)
+    return outs
+
   def set_profiling(self, enable):
     """Records CUDA events around the pooling kernels of every execution."""
     C.check(C.lib.xse_engine_set_profiling(self._handle, 1 if enable else 0))
