@@ -31,6 +31,8 @@
 // if any; per bag: one offset and the fp32 output row.
 
 #include <cuda_runtime.h>
+
+#include <algorithm>
 #include <stdint.h>
 
 #include "xse_internal.h"
@@ -502,23 +504,26 @@ __device__ __forceinline__ void LoadChunk(const BagDesc& d, int64_t pos,
 // (RowsInFlight, sized for MinBlocks resident blocks); a deep setting (a
 // whole id chunk) serves launches too small to fill the GPU, where each
 // group pools one or two bags and every batch is a full memory round trip.
+//
+// One launch serves every weighting mode of a layout group: descriptors are
+// sorted by mode, and each mode's tasks [task_lo, task_hi) are pooled by its
+// own range of blocks with a body compiled for that mode (a block never
+// switches mode, so the bodies do not share registers).
 template <int DT, int G, int V, bool EXACT, int WM, int UR>
-__global__ void __launch_bounds__(kThreads,
-                                  UR == 0 ? MinBlocks<DT, V>::value : 2)
-    PoolVecKernel(const __grid_constant__ PoolParams p) {
+__device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
+                                         int64_t task_hi, int64_t block,
+                                         int64_t blocks) {
   constexpr int PPV = ElemsPerVec<DT>::value / 2;
   constexpr int U = UR == 0 ? RowsInFlight<DT, V>::value : UR;
   constexpr int kGroupsPerBlock = kThreads / G;
-  if (!p.fused_checks && p.status->group_error != 0) return;
 
   const int lane = threadIdx.x & 31;
   const int gl = lane % G;
   const unsigned gmask =
       G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane - gl));
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kGroupsPerBlock;
-  int64_t task = static_cast<int64_t>(blockIdx.x) * kGroupsPerBlock +
-                 threadIdx.x / G;
-  if (task >= p.total_tasks) return;
+  const int64_t stride = blocks * kGroupsPerBlock;
+  int64_t task = task_lo + block * kGroupsPerBlock + threadIdx.x / G;
+  if (task >= task_hi) return;
   int t = AdvanceDesc(p, 0, task);
   int64_t begin, end;
   {
@@ -534,7 +539,7 @@ __global__ void __launch_bounds__(kThreads,
     const int64_t bag = task - d.task_begin;
     // Lookahead: the next task's offsets, consumed one bag later.
     const int64_t ntask = task + stride;
-    const bool has_next = ntask < p.total_tasks;
+    const bool has_next = ntask < task_hi;
     int nt = t;
     int64_t nbegin = 0, nend = 0;
     if (has_next) {
@@ -600,6 +605,26 @@ __global__ void __launch_bounds__(kThreads,
     begin = nbegin;
     end = nend;
     have_chunk = next_chunk;
+  }
+}
+
+template <int DT, int G, int V, bool EXACT, int UR>
+__global__ void __launch_bounds__(kThreads,
+                                  UR == 0 ? MinBlocks<DT, V>::value : 2)
+    PoolVecKernel(const __grid_constant__ PoolParams p) {
+  if (!p.fused_checks && p.status->group_error != 0) return;
+  const int64_t b = blockIdx.x;
+  const int64_t b0 = p.mode_blocks[0], b1 = p.mode_blocks[1];
+  if (b < b0) {
+    PoolBody<DT, G, V, EXACT, kUnweighted, UR>(p, 0, p.mode_tasks[0], b, b0);
+  } else if (b < b1) {
+    PoolBody<DT, G, V, EXACT, kWeightedSum, UR>(p, p.mode_tasks[0],
+                                                p.mode_tasks[1], b - b0,
+                                                b1 - b0);
+  } else {
+    PoolBody<DT, G, V, EXACT, kWeightedNorm, UR>(p, p.mode_tasks[1],
+                                                 p.mode_tasks[2], b - b1,
+                                                 gridDim.x - b1);
   }
 }
 
@@ -785,45 +810,70 @@ constexpr int DeepRows() {
   return (DT == 2 || V != 1) ? 0 : (G < 8 ? G : 8);
 }
 
-template <int DT, int G, int V, bool EXACT, int WM>
+// Splits `grid` blocks over the weighting modes in proportion to their tasks
+// (every mode with tasks gets at least one block) and records the cumulative
+// task and block ends in p.
+void SplitModes(PoolParams* p, int64_t max_grid, int groups_per_block) {
+  int64_t tasks[3] = {0, 0, 0};
+  for (int k = 0; k < p->n; ++k) tasks[WeightModeOf(p->d[k])] += p->d[k].num_bags;
+  int64_t need[3], total_need = 0;
+  for (int m = 0; m < 3; ++m) {
+    need[m] = (tasks[m] + groups_per_block - 1) / groups_per_block;
+    total_need += need[m];
+  }
+  int64_t blocks[3] = {0, 0, 0};
+  if (total_need <= max_grid) {
+    for (int m = 0; m < 3; ++m) blocks[m] = need[m];
+  } else {
+    const int64_t total = p->total_tasks > 0 ? p->total_tasks : 1;
+    for (int m = 0; m < 3; ++m) {
+      if (tasks[m] == 0) continue;
+      const int64_t share = max_grid * tasks[m] / total;
+      blocks[m] = share < 1 ? 1 : share;  // grid-stride covers the rest
+    }
+  }
+  int64_t task_end = 0, block_end = 0;
+  for (int m = 0; m < 3; ++m) {
+    task_end += tasks[m];
+    block_end += blocks[m];
+    p->mode_tasks[m] = task_end;
+    p->mode_blocks[m] = static_cast<int32_t>(block_end);
+  }
+}
+
+template <int DT, int G, int V, bool EXACT>
 cudaError_t LaunchVec(const PoolParams& in, cudaStream_t stream) {
   PoolParams p = in;
+  // Descriptors by weighting mode (stable: request order within a mode).
+  std::stable_sort(p.d, p.d + p.n, [](const BagDesc& a, const BagDesc& b) {
+    return WeightModeOf(a) < WeightModeOf(b);
+  });
   AssignTasks(&p, 1);
-  auto kernel = PoolVecKernel<DT, G, V, EXACT, WM, 0>;
+  auto kernel = PoolVecKernel<DT, G, V, EXACT, 0>;
+  int64_t max_grid = static_cast<int64_t>(SmCount()) * BlocksPerSm(kernel);
   constexpr int kDeep = DeepRows<DT, G, V>();
   if constexpr (kDeep > 0) {
     // Fewer bags than one wave of the throughput kernel's groups: every
     // group pools about one bag, so latency (round trips per bag), not
     // bandwidth, sets the time; gather a whole chunk per round trip.
-    const int64_t wave = static_cast<int64_t>(SmCount()) *
-                         BlocksPerSm(kernel) * (kThreads / G);
-    if (p.total_tasks <= wave) {
-      auto deep = PoolVecKernel<DT, G, V, EXACT, WM, kDeep>;
-      const int grid = GridFor(deep, p.total_tasks, kThreads / G);
-      deep<<<grid, kThreads, 0, stream>>>(p);
+    if (p.total_tasks <= max_grid * (kThreads / G)) {
+      auto deep = PoolVecKernel<DT, G, V, EXACT, kDeep>;
+      SplitModes(&p, static_cast<int64_t>(SmCount()) * BlocksPerSm(deep),
+                 kThreads / G);
+      deep<<<p.mode_blocks[2], kThreads, 0, stream>>>(p);
       return cudaGetLastError();
     }
   }
-  const int grid = GridFor(kernel, p.total_tasks, kThreads / G);
-  kernel<<<grid, kThreads, 0, stream>>>(p);
+  SplitModes(&p, max_grid, kThreads / G);
+  kernel<<<p.mode_blocks[2], kThreads, 0, stream>>>(p);
   return cudaGetLastError();
-}
-
-template <int DT, int G, int V, bool EXACT>
-cudaError_t LaunchVecMode(const Layout& l, const PoolParams& p,
-                          cudaStream_t stream) {
-  switch (l.wmode) {
-    case kUnweighted: return LaunchVec<DT, G, V, EXACT, kUnweighted>(p, stream);
-    case kWeightedSum: return LaunchVec<DT, G, V, EXACT, kWeightedSum>(p, stream);
-    default: return LaunchVec<DT, G, V, EXACT, kWeightedNorm>(p, stream);
-  }
 }
 
 template <int DT, int G, int V>
 cudaError_t LaunchVecExact(const Layout& l, const PoolParams& p,
                            cudaStream_t stream) {
-  return l.exact ? LaunchVecMode<DT, G, V, true>(l, p, stream)
-                 : LaunchVecMode<DT, G, V, false>(l, p, stream);
+  return l.exact ? LaunchVec<DT, G, V, true>(p, stream)
+                 : LaunchVec<DT, G, V, false>(p, stream);
 }
 
 template <int DT>

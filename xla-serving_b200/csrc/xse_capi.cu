@@ -596,8 +596,8 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
         l.v = 0;  // an empty int8 window: the element-wise kernel
         l.exact = false;
       }
-      l.wmode = l.v == 0 ? 0 : xse::WeightModeOf(d);
-      groups[{l.dtype, l.g, l.v, l.exact, l.wmode}].push_back(d);
+      // One launch per layout; its weighting modes share it.
+      groups[{l.dtype, l.g, l.v, l.exact, 0}].push_back(d);
     }
     for (auto& [key, list] : groups) {
       const xse::Layout l{std::get<0>(key), std::get<1>(key), std::get<2>(key),
@@ -1288,8 +1288,8 @@ extern "C" int xse_engine_execute_batch_noalloc(xse_engine* engine,
       }
       lj.wmode = lj.v == 0 ? 0 : xse::WeightModeOf(descs[j]);
       if (lj.dtype != li.dtype || lj.g != li.g || lj.v != li.v ||
-          lj.exact != li.exact || lj.wmode != li.wmode) {
-        continue;
+          lj.exact != li.exact) {
+        continue;  // weighting modes share a launch
       }
       launched[j] = true;
       group.d[group.n] = descs[j];

@@ -69,17 +69,23 @@ struct PoolParams {
   int32_t bags_per_task;  // consecutive bags one lane group pools per task
   int32_t reserved;
   DevStatus* status;
+  // Vector kernels: descriptors sorted by weighting mode; cumulative task
+  // and block ends of modes 0, 1, 2 (set by the launcher).
+  int64_t mode_tasks[3];
+  int32_t mode_blocks[3];
+  int32_t reserved2;
   BagDesc d[kMaxDescsPerLaunch];
 };
 
 // Row layout class of a launch: G lanes per row, V 16-byte vectors per lane.
 // V == 0 selects the element-wise kernel (dims that are not whole vectors).
+// A launch serves every weighting mode of its layout.
 struct Layout {
   int dtype;
   int g;
   int v;
   bool exact;  // rows are exactly g*v vectors: no per-lane bounds checks
-  int wmode;   // 0 unweighted, 1 weighted sum, 2 weighted mean / sqrt-n
+  int wmode;   // unused by the launcher (kept for callers that group by it)
 };
 
 // Weighting mode of a request (kernels are compiled per mode).
