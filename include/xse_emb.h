@@ -229,14 +229,19 @@ int xse_engine_execute_batch_noalloc(xse_engine* engine,
 int32_t xse_last_launch_count(void);
 
 /* Kernel timing (tracing aid; the reference traces with tsl TraceMe spans,
- * data/processor/cc/core/graph/graph_executor.cc:62,111). While enabled, each
- * xse_engine_execute_batch records CUDA events on its stream around its
- * pooling kernels. xse_engine_profile_read waits for those events and
- * returns the summed pooling time and the number of executions since the
- * last read. */
-int xse_engine_set_profiling(xse_engine* engine, int32_t enable);
+ * data/processor/cc/core/graph/graph_executor.cc:62,111). With period n > 0,
+ * every n-th xse_engine_execute_batch from now on (the first, the (n+1)-th,
+ * ...) records CUDA events on its stream around its pooling kernels; 0 turns
+ * timing off. An event pair costs a few microseconds of stream time and
+ * serialises the kernels it separates, so a period above 1 keeps the timed
+ * executions representative of untimed ones. xse_engine_profile_read waits
+ * for the recorded events and returns the summed pooling time, the number of
+ * timed executions and (when `calls` is non-null) the number of executions,
+ * timed or not, since profiling was set or last read; the read restarts the
+ * sampling. */
+int xse_engine_set_profiling(xse_engine* engine, int32_t period);
 int xse_engine_profile_read(xse_engine* engine, double* pool_ms,
-                            int64_t* executions);
+                            int64_t* executions, int64_t* calls);
 
 /* ---------------------------------------------------------------------------
  * DLRM dot interaction. No counterpart in the reference: its DLRM bundle uses

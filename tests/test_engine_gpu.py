@@ -361,3 +361,77 @@ def test_large_launch_parity(xse, dtype, dim):
                      None if weights is None else to_dev(weights))
     assert_bitwise(small.cpu().numpy(), want[:200], f"small {combine}")
   eng.close()
+
+
+@pytest.mark.parametrize("id_dtype", [np.int64, np.int32])
+@pytest.mark.parametrize("skew", [0, 1, 3])
+def test_validation_reports_smallest_bad_position(xse, id_dtype, skew):
+  """The id check reads 16-byte vectors when the ids are aligned and single
+  ids otherwise (`skew` shifts the ids off alignment); either way the
+  reported position is the smallest failing one inside [offsets[0],
+  offsets[-1]), and ids outside that range are not read."""
+  rng = np.random.default_rng(41 + skew)
+  _, dev, _, _ = random_table(rng, oracle.F32, 1000, 32)
+  eng = xse.EmbeddingEngine(0)
+  eng.add_table("t", dev, "SUM")
+  eng.register_feature("f", "t")
+  n = 9000
+  ids = rng.integers(0, 1000, size=n + skew).astype(id_dtype)
+  backing = to_dev(ids)
+  view = backing[skew:]
+  lens = rng.integers(0, 9, size=2000)
+  first = 5
+  offsets = np.concatenate([[first], first + np.cumsum(lens)])
+  offsets = offsets[offsets <= n - 7]
+  out = torch.empty((len(offsets) - 1, 32), device="cuda")
+  last = int(offsets[-1])
+  for bad_positions in ([first], [last - 1], [2049, 2050, 7000],
+                        [4097, 4096 + 2], [first + 1, first + 3]):
+    host = ids.copy()
+    host[skew:][:first] = -1            # before offsets[0]: not read
+    host[skew:][last:] = 1000           # at or past offsets[-1]: not read
+    for pos in bad_positions:
+      if pos < last:
+        host[skew + pos] = 1000 + pos
+    backing.copy_(torch.from_numpy(host))
+    expect = min(p for p in bad_positions if p < last)
+    with pytest.raises(xse.XseError) as e:
+      eng.execute_batch([xse.BagRequest("f", view, to_dev(
+          offsets.astype(np.int64)), out)])
+    assert e.value.message == (
+        f"FP32 embedding-bag request 0: Embedding ID ({1000 + expect}) at "
+        f"index {expect} is out of bounds [0, 1000).")
+  host = ids.copy()
+  host[skew:][:first] = -1
+  host[skew:][last:] = 1000
+  backing.copy_(torch.from_numpy(host))
+  eng.execute_batch([xse.BagRequest("f", view, to_dev(
+      offsets.astype(np.int64)), out)])
+  eng.close()
+
+
+def test_profiling_period(xse):
+  """Kernel timing samples every `period`-th execution and counts all."""
+  rng = np.random.default_rng(5)
+  _, dev, _, _ = random_table(rng, oracle.F32, 100, 32)
+  eng = xse.EmbeddingEngine(0)
+  eng.add_table("t", dev, "SUM")
+  eng.register_feature("f", "t")
+  ids, offsets = random_csr(rng, 100, 64, 6)
+  reqs = [xse.BagRequest("f", to_dev(ids), to_dev(offsets),
+                         torch.empty((64, 32), device="cuda"))]
+  eng.set_profiling(True, 3)
+  for _ in range(7):
+    eng.execute_batch(reqs)
+  ms, timed, calls = eng.profile_read(with_calls=True)
+  assert (timed, calls) == (3, 7) and ms > 0
+  eng.execute_batch(reqs)  # the read restarts the sampling: timed
+  ms, timed = eng.profile_read()
+  assert timed == 1
+  eng.set_profiling(False)
+  eng.execute_batch(reqs)
+  assert eng.profile_read(with_calls=True)[1:] == (0, 0)
+  with pytest.raises(xse.XseError):
+    C = xse._capi
+    C.check(C.lib.xse_engine_set_profiling(eng._handle, -1))
+  eng.close()

@@ -138,6 +138,7 @@ SIGNATURES = {
                                        _P]),
     "xse_engine_set_profiling": (_I, [_P, _I32]),
     "xse_engine_profile_read": (_I, [_P, ctypes.POINTER(ctypes.c_double),
+                                     ctypes.POINTER(_I64),
                                      ctypes.POINTER(_I64)]),
     "xse_dot_interaction": (_I, [_P, _P, _I64, _I32, _I32, _P, _P]),
     "xse_synth_table": (_I, [_P, _P, _P, _I32, _U64, _U64, _I64, _I64, _I32,

@@ -33,6 +33,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <utility>
 #include <stdint.h>
 
 #include "xse_internal.h"
@@ -75,6 +76,11 @@ struct ElemsPerVec<2> {
 
 #ifndef XSE_POOL_I8_ROWS
 #define XSE_POOL_I8_ROWS 2
+#endif
+
+// 1: validation and pooling kernels use programmatic dependent launch.
+#ifndef XSE_PDL
+#define XSE_PDL 1
 #endif
 
 // Rows gathered per batch (in flight per lane, times V vectors each).
@@ -608,10 +614,26 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
   }
 }
 
+// Programmatic dependent launch. The validation and pooling kernels are
+// launched so that the next kernel of the stream may be scheduled before they
+// finish: each of them lets its dependents launch on entry and, before its
+// first global-memory access, waits until the kernel before it has completed
+// and its writes are visible (griddepcontrol.wait returns at once when the
+// launch had no programmatic dependency). The overlap hides the launch and
+// block-scheduling latency between consecutive kernels of a step and
+// between steps; no data is read early.
+__device__ __forceinline__ void EnterDependent() {
+#if XSE_PDL
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+
 template <int DT, int G, int V, bool EXACT, int UR>
 __global__ void __launch_bounds__(kThreads,
                                   UR == 0 ? MinBlocks<DT, V>::value : 2)
     PoolVecKernel(const __grid_constant__ PoolParams p) {
+  EnterDependent();
   if (!p.fused_checks && p.status->group_error != 0) return;
   const int64_t b = blockIdx.x;
   const int64_t b0 = p.mode_blocks[0], b1 = p.mode_blocks[1];
@@ -635,6 +657,7 @@ template <int DT>
 __global__ void __launch_bounds__(kThreads)
     PoolScalarKernel(const __grid_constant__ PoolParams p) {
   constexpr int kCols = 4;
+  EnterDependent();
   if (!p.fused_checks && p.status->group_error != 0) return;
   const int lane = threadIdx.x & 31;
   const int64_t warps_per_block = kThreads / 32;
@@ -715,6 +738,7 @@ constexpr int kValidateChunk = 256;
 
 __global__ void __launch_bounds__(kThreads)
     ValidateKernel(const __grid_constant__ PoolParams p, int64_t total_work) {
+  EnterDependent();
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
   int t = 0;
@@ -782,6 +806,24 @@ int BlocksPerSm(Kernel kernel) {
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0);
   return per_sm > 0 ? per_sm : 1;
+}
+
+// Launches `kernel` on `grid` blocks of kThreads with a programmatic
+// dependency on the previous kernel of the stream (see EnterDependent).
+template <typename... Params, typename... Args>
+cudaError_t LaunchDependent(void (*kernel)(Params...), int grid,
+                            cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = XSE_PDL;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 template <typename Kernel>
@@ -860,13 +902,11 @@ cudaError_t LaunchVec(const PoolParams& in, cudaStream_t stream) {
       auto deep = PoolVecKernel<DT, G, V, EXACT, kDeep>;
       SplitModes(&p, static_cast<int64_t>(SmCount()) * BlocksPerSm(deep),
                  kThreads / G);
-      deep<<<p.mode_blocks[2], kThreads, 0, stream>>>(p);
-      return cudaGetLastError();
+      return LaunchDependent(deep, p.mode_blocks[2], stream, p);
     }
   }
   SplitModes(&p, max_grid, kThreads / G);
-  kernel<<<p.mode_blocks[2], kThreads, 0, stream>>>(p);
-  return cudaGetLastError();
+  return LaunchDependent(kernel, p.mode_blocks[2], stream, p);
 }
 
 template <int DT, int G, int V>
@@ -884,8 +924,7 @@ cudaError_t LaunchForDtype(const Layout& l, const PoolParams& p,
     AssignTasks(&q, 1);
     auto kernel = PoolScalarKernel<DT>;
     const int grid = GridFor(kernel, q.total_tasks, kThreads / 32);
-    kernel<<<grid, kThreads, 0, stream>>>(q);
-    return cudaGetLastError();
+    return LaunchDependent(kernel, grid, stream, q);
   }
   if (l.v == 1) {
     switch (l.g) {
@@ -955,8 +994,7 @@ cudaError_t LaunchValidate(const PoolParams& p, int64_t total_work,
                            cudaStream_t stream) {
   if (total_work <= 0) return cudaSuccess;
   const int grid = GridFor(ValidateKernel, total_work, kThreads / 32);
-  ValidateKernel<<<grid, kThreads, 0, stream>>>(p, total_work);
-  return cudaGetLastError();
+  return LaunchDependent(ValidateKernel, grid, stream, p, total_work);
 }
 
 cudaError_t LaunchInterleaveScaleBias(const float* scale, const float* bias,

@@ -168,9 +168,11 @@ struct xse_engine {
   std::unordered_map<std::string, std::shared_ptr<Table>> tables;
   std::mutex default_status_mu;
   xse_status* default_status = nullptr;
-  // Kernel timing: event pairs recorded around pooling kernels.
+  // Kernel timing: event pairs recorded around the pooling kernels of every
+  // profile_period-th execution (0: off).
   std::mutex profile_mu;
-  bool profiling = false;
+  int32_t profile_period = 0;
+  int64_t profile_calls = 0;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> profile_events;
   size_t profile_used = 0;
 };
@@ -575,7 +577,8 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
   if (!validate_only && !any_soft) {
     {
       std::lock_guard<std::mutex> lock(engine->profile_mu);
-      if (engine->profiling) {
+      if (engine->profile_period > 0 &&
+          engine->profile_calls++ % engine->profile_period == 0) {
         if (engine->profile_used == engine->profile_events.size()) {
           cudaEvent_t a, b;
           cudaEventCreate(&a);
@@ -716,16 +719,20 @@ void xse_engine_destroy(xse_engine* engine) {
   delete engine;
 }
 
-int xse_engine_set_profiling(xse_engine* engine, int32_t enable) {
+int xse_engine_set_profiling(xse_engine* engine, int32_t period) {
   if (engine == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null engine");
+  if (period < 0) {
+    return SetError(XSE_INVALID_ARGUMENT, "profiling period must be >= 0");
+  }
   std::lock_guard<std::mutex> lock(engine->profile_mu);
-  engine->profiling = enable != 0;
+  engine->profile_period = period;
+  engine->profile_calls = 0;
   engine->profile_used = 0;
   return Ok();
 }
 
 int xse_engine_profile_read(xse_engine* engine, double* pool_ms,
-                            int64_t* executions) {
+                            int64_t* executions, int64_t* calls) {
   if (engine == nullptr || pool_ms == nullptr || executions == nullptr) {
     return SetError(XSE_INVALID_ARGUMENT, "arguments must be non-null");
   }
@@ -743,7 +750,9 @@ int xse_engine_profile_read(xse_engine* engine, double* pool_ms,
   }
   *pool_ms = total;
   *executions = static_cast<int64_t>(engine->profile_used);
+  if (calls != nullptr) *calls = engine->profile_calls;
   engine->profile_used = 0;
+  engine->profile_calls = 0;
   return Ok();
 }
 

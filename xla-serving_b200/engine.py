@@ -275,16 +275,23 @@ class EmbeddingEngine:
     C.check(rc)
     return outs
 
-  def set_profiling(self, enable):
-    """Records CUDA events around the pooling kernels of every execution."""
-    C.check(C.lib.xse_engine_set_profiling(self._handle, 1 if enable else 0))
+  def set_profiling(self, enable, period=1):
+    """Records CUDA events around the pooling kernels of every `period`-th
+    execution (the first, the period+1-th, ...) while `enable` is true."""
+    C.check(C.lib.xse_engine_set_profiling(self._handle,
+                                           int(period) if enable else 0))
 
-  def profile_read(self):
-    """(summed pooling-kernel milliseconds, executions) since the last read."""
+  def profile_read(self, with_calls=False):
+    """(summed pooling-kernel milliseconds, timed executions) since the last
+    read; with `with_calls`, also the number of executions, timed or not."""
     ms = ctypes.c_double()
     n = ctypes.c_int64()
+    calls = ctypes.c_int64()
     C.check(C.lib.xse_engine_profile_read(self._handle, ctypes.byref(ms),
-                                          ctypes.byref(n)))
+                                          ctypes.byref(n),
+                                          ctypes.byref(calls)))
+    if with_calls:
+      return ms.value, n.value, calls.value
     return ms.value, n.value
 
   def pool(self, feature_name, ids, offsets, weights=None, *, stream=None,
