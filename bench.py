@@ -350,16 +350,22 @@ class DlrmWorkload:
   def step(self, i):
     dense, reqs, _, _ = self.sets[i % DLRM_ROTATE]
     self.model.forward(dense, requests=reqs, status=self.status)
-    # Own kernels: the pooling launch (fused checks), the interaction, the
-    # sigmoid head and one operand split per split-TF32 layer (the GEMMs are
-    # cuBLASLt's).
-    return 1 + 2 + len(self.model.tower._split)
+    # Own kernels: the fused pooling + interaction launch (fused checks; or
+    # pooling and the interaction kernel), the sigmoid head and one operand
+    # split per split-TF32 layer (the GEMMs are cuBLASLt's).
+    fused = self.model.fused_interaction
+    return (1 if fused else 2) + 1 + len(self.model.tower._split)
 
   def pool_bytes(self, v):
-    """Algorithmic bytes of variant v's pooled lookup."""
-    return (self.nnz[v] * (DLRM_DIM * 4 + 8) +
-            (DLRM_BATCH + 1) * 8 * DLRM_TABLES +
-            DLRM_BATCH * DLRM_TABLES * DLRM_DIM * 4)
+    """Algorithmic bytes of variant v's timed kernel: every id's row and id,
+    the offsets, and either the pooled [B, 26, 128] fp32 output or -- fused
+    with the interaction -- the bottom-MLP rows read and the [B, 480]
+    interaction rows written."""
+    lookup = (self.nnz[v] * (DLRM_DIM * 4 + 8) +
+              (DLRM_BATCH + 1) * 8 * DLRM_TABLES)
+    if self.model.fused_interaction:
+      return lookup + DLRM_BATCH * (DLRM_DIM + self.model.tower.width_stride) * 4
+    return lookup + DLRM_BATCH * DLRM_TABLES * DLRM_DIM * 4
 
   def close(self):
     self.status.close()
@@ -453,9 +459,9 @@ def measure_dlrm(xse, args, world, local):
       "steps": args.dlrm_steps,
       "ms_per_step": ms / args.dlrm_steps,
       "ids_per_s": ids / (ms / 1000.0),
-      "dtype": "fp32 (tables, pooling, interaction); dense layers as 3xTF32 "
-               "tensor-core GEMMs (hi/lo split operands, fp32-level "
-               "accuracy)",
+      "dtype": "fp32 (tables, pooling); interaction Gram and dense layers "
+               "as 3xTF32 tensor-core MMAs (hi/lo split operands, "
+               "fp32-level accuracy)",
       "parallelism": ("single GPU" if world == 1 else
                       f"{world} data-parallel replicas (tables replicated, "
                       "no collective)"),
@@ -464,6 +470,10 @@ def measure_dlrm(xse, args, world, local):
                  "l2": f"{sum(wl.rows) * DLRM_DIM * 4 / 1e9:.1f} GB of tables "
                        f"and {DLRM_ROTATE} rotating input sets per GPU"},
       "pool_roofline": {
+          "kernel": ("PoolInteractKernel<fp32> (pooled lookup + dot "
+                     "interaction, split-TF32 mma.sync Gram)"
+                     if wl.model.fused_interaction else
+                     "PoolVecKernel<fp32, G=32, V=1, exact>"),
           "bound": "hbm", "achieved": pool_bytes / (pool_avg / 1000.0) / 1e9,
           "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
           "frac": pool_bytes / (pool_avg / 1000.0) / 1e9 / peak,

@@ -255,6 +255,31 @@ int xse_dot_interaction(const float* dense, const float* pooled,
                         int64_t batch, int32_t num_tables, int32_t dim,
                         float* out, void* stream);
 
+/* Pooled lookup fused with the dot interaction: request t (t = 0..n-1, each
+ * with `batch` bags over a whole table, all tables of one dimension) pools
+ * feature t of every sample, and out row b (every out_stride floats, at least
+ * dim + (n+1)n/2) receives [dense_b, Z_b[i].Z_b[j] for i < j] with the pooled
+ * rows in Z_b as xse_dot_interaction has them, zeros up to out_stride. The
+ * requests' output fields are not used: where one kernel serves the tables'
+ * layout (fp32 or bf16 rows of 32 16-byte vectors -- dim 128 fp32 or 256
+ * bf16 --, one weighting mode for all requests, n <= 31, 16-byte aligned
+ * dense rows) the pooled rows of a sample are gathered into shared memory
+ * and its interaction computed there, so the pooled [batch, n, dim] tensor
+ * never reaches HBM; otherwise the bags are pooled into scratch and the
+ * interaction kernel runs after. The pooled
+ * values equal xse_engine_execute_batch's bit for bit. Flags, status,
+ * validation and errors as xse_engine_execute_batch (XSE_EXEC_STRICT
+ * validates every request before the kernel runs); when the call reports an
+ * error the contents of out are unspecified. No counterpart in the reference
+ * (its DLRM feeds the pooled rows to a DCN-v2 cross network,
+ * examples/dlrm/model_jce.py:141-164). */
+int xse_engine_execute_interaction(xse_engine* engine,
+                                   const xse_bag_request* reqs, int32_t n,
+                                   const float* dense, int64_t dense_stride,
+                                   int64_t batch, float* out,
+                                   int64_t out_stride, void* stream,
+                                   int32_t flags, xse_status* status);
+
 /* ---------------------------------------------------------------------------
  * Seeded synthetic inputs on the device (counter-based, reproducible on the
  * host). Used by tests and benchmarks; no reference counterpart (the

@@ -163,10 +163,13 @@ def test_linear_forward_tf32x3(xse, dlrm, rows, in_dim, out_dim, act):
                                1e-5 * bound + 1e-6)
 
 
-def test_dlrm_forward_end_to_end(xse, dlrm):
+@pytest.mark.parametrize("fused_interaction", [False, True])
+def test_dlrm_forward_end_to_end(xse, dlrm, fused_interaction):
   """Pooled lookup of 26 fp32 features (ragged Zipf bags, sum pooling) plus
-  the tower: pooled values bit-exact to the oracle, predictions within 1e-4
-  of the float64 tower applied to the oracle's pooled values."""
+  the tower: pooled values bit-exact to the oracle (unfused: read back from
+  the pooled buffer), predictions within 1e-4 of the float64 tower applied to
+  the oracle's pooled values (fused: pooling and interaction in one
+  kernel, the pooled rows never stored)."""
   from xla_serving_b200 import synth  # pylint: disable=import-outside-toplevel
   engine = xse.EmbeddingEngine()
   rows = synth.log_uniform_rows(26, 50, 5000, 7)
@@ -184,14 +187,17 @@ def test_dlrm_forward_end_to_end(xse, dlrm):
     fb = synth.synth_batch(spec, t, batch, 1, 100, 11, 1.05)
     ids.append(fb.ids)
     offsets.append(fb.offsets)
-  model = dlrm.DLRM(engine, names, seed=1)
+  model = dlrm.DLRM(engine, names, seed=1,
+                    fused_interaction=fused_interaction)
   dense = torch.randn(batch, 13, generator=torch.Generator().manual_seed(2))
   pred = model.forward(dense.cuda(), ids, offsets).cpu().numpy()
-  pooled = model.pooled_buffer(batch).cpu().numpy()
-  for t in range(26):
-    want = oracle.embedding_bag(host_tables[t], ids[t].cpu().numpy(),
-                                offsets[t].cpu().numpy(), None, "SUM")
-    np.testing.assert_array_equal(pooled[:, t, :], want)
+  pooled = np.stack([
+      oracle.embedding_bag(host_tables[t], ids[t].cpu().numpy(),
+                           offsets[t].cpu().numpy(), None, "SUM")
+      for t in range(26)], axis=1)
+  if not fused_interaction:
+    np.testing.assert_array_equal(model.pooled_buffer(batch).cpu().numpy(),
+                                  pooled)
   want = model.tower.reference_forward(dense.numpy(), pooled)
   np.testing.assert_allclose(pred, want, rtol=0, atol=1e-4)
   engine.close()

@@ -140,6 +140,8 @@ SIGNATURES = {
     "xse_engine_profile_read": (_I, [_P, ctypes.POINTER(ctypes.c_double),
                                      ctypes.POINTER(_I64),
                                      ctypes.POINTER(_I64)]),
+    "xse_engine_execute_interaction": (_I, [_P, _P, _I32, _P, _I64, _I64, _P,
+                                            _I64, _P, _I32, _P]),
     "xse_dot_interaction": (_I, [_P, _P, _I64, _I32, _I32, _P, _P]),
     "xse_synth_table": (_I, [_P, _P, _P, _I32, _U64, _U64, _I64, _I64, _I32,
                              _P]),

@@ -427,7 +427,7 @@ __device__ __forceinline__ void GatherBatch(
 // accumulator for the next one.
 template <int DT, int G, int V, bool EXACT>
 __device__ __forceinline__ void FinishBag(
-    const BagDesc& d, int64_t bag, int64_t n, bool weighted,
+    const BagDesc& d, float* out, bool vec_out, int64_t n, bool weighted,
     u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, int gl,
     int row_vecs) {
   constexpr int PPV = ElemsPerVec<DT>::value / 2;
@@ -439,13 +439,12 @@ __device__ __forceinline__ void FinishBag(
 #pragma unroll
       for (int k = 0; k < PPV; ++k) acc[v][k] = Mul2(acc[v][k], s2);
   }
-  float* out = d.out + bag * d.out_stride;
 #pragma unroll
   for (int v = 0; v < V; ++v) {
     const int k = gl + v * G;
     if (EXACT || k < row_vecs) {
       float* o = out + k * (2 * PPV);
-      if (d.vec_out) {
+      if (vec_out) {
 #pragma unroll
         for (int e = 0; e < PPV; e += 2) {
           *reinterpret_cast<ulonglong2*>(o + 2 * e) =
@@ -602,8 +601,9 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
                                            prefetch);
         }
       }
-      FinishBag<DT, G, V, EXACT>(d, bag, end - begin, WM != kUnweighted, acc,
-                                 &wsum, gl, row_vecs);
+      FinishBag<DT, G, V, EXACT>(d, d.out + bag * d.out_stride, d.vec_out,
+                                 end - begin, WM != kUnweighted, acc, &wsum,
+                                 gl, row_vecs);
     }
     if (!has_next) break;
     task = ntask;
@@ -647,6 +647,334 @@ __global__ void __launch_bounds__(kThreads,
     PoolBody<DT, G, V, EXACT, kWeightedNorm, UR>(p, p.mode_tasks[1],
                                                  p.mode_tasks[2], b - b1,
                                                  gridDim.x - b1);
+  }
+}
+
+// ---- fused pooling + dot interaction --------------------------------------
+//
+// Blocks take samples one at a time from a counter in the status block (a
+// block's local sample ls is the ls-th it took), so that all blocks finish
+// together; a block's items are (local sample, request) pairs in
+// sample-major order, taken one at a time by its warps from a shared counter
+// (request t's bag b is table t of sample b). The warp that takes a sample's
+// first item fetches the sample. A warp pools its
+// bag with the same per-bag code (CSR order, the same roundings) as
+// PoolVecKernel and stores the row into the sample's slot of shared memory,
+// Z[slot] = [dense; pooled_0; ...; pooled_{T-1}] (row stride RS floats; NS
+// slots in a ring). The warp that stores a sample's last row computes its
+// interaction row -- [dense, Z[i].Z[j] for 0 <= i < j <= T (row-major),
+// zeros to out_stride] -- and frees the slot; the other warps keep pooling
+// meanwhile, so no block-wide barrier stalls the gathers. The pooled
+// [B, T, D] tensor never reaches HBM. The Gram Z Z^T (R = T + 1 <= 32 rows)
+// runs on the tensor cores as split-TF32 mma.sync tiles (three MMAs per tile,
+// fp32 accumulation: fp32-level accuracy). A warp that needs a slot still
+// held by the sample NS before waits for it with a bounded spin.
+
+// x = hi + lo: hi is x with the 13 low mantissa bits cleared (exact in
+// TF32), lo = x - hi (exact in fp32, |lo| < 2^-10 |x|); the MMA reads lo's
+// top TF32 bits, so lo*hi' + hi*lo' + hi*hi' carries x*y to about 2^-20
+// relative, the dropped lo*lo' being below that. A mask and a subtraction:
+// the conversion instructions' throughput would bound the Gram.
+__device__ __forceinline__ void SplitTf32(float x, uint32_t* hi,
+                                          uint32_t* lo) {
+  const uint32_t h = __float_as_uint(x) & 0xffffe000u;
+  *hi = h;
+  *lo = __float_as_uint(x - __uint_as_float(h));
+}
+
+// acc += A (16x8, row-major fragment a) * B (8x8, column-major fragment b).
+__device__ __forceinline__ void MmaTf32(float (&acc)[4], const uint32_t (&a)[4],
+                                        uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Gram of one sample's rows Z[0..R) (R <= 32, row stride RS floats, D
+// columns) on the tensor cores, half `half` of the six 16x8 output tiles
+// that hold the pairs i < j: half 0 (rows 0-15) x (cols 0-7, 8-15, 16-23),
+// half 1 (rows 0-15) x (cols 24-31) and (rows 16-31) x (cols 16-23, 24-31).
+// Each product is split into TF32 hi/lo parts (three MMAs), accumulated in
+// fp32. Rows past R read row R-1; their outputs are not stored. Writes pair
+// (i, j) to o[i (2R - i - 1) / 2 + j - i - 1].
+template <int D, int HALF>
+__device__ __forceinline__ void GramHalfTf32x3(const float* zs, int R, int RS,
+                                               float* o) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const float* rp[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + g;
+    rp[k] = zs + (r < R ? r : R - 1) * RS + tig;
+  }
+  float acc[3][4];
+#pragma unroll
+  for (int t = 0; t < 3; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
+#pragma unroll 1
+  for (int k0 = 0; k0 < D; k0 += 8) {
+    // v[2k] = Z[8k+g][k0+tig], v[2k+1] = Z[8k+g][k0+tig+4].
+    uint32_t hi[8], lo[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      SplitTf32(rp[k][k0], &hi[2 * k], &lo[2 * k]);
+      SplitTf32(rp[k][k0 + 4], &hi[2 * k + 1], &lo[2 * k + 1]);
+    }
+    // A fragments: row block 0 = rows 0-15, row block 1 = rows 16-31.
+    const uint32_t a0h[4] = {hi[0], hi[2], hi[1], hi[3]};
+    const uint32_t a0l[4] = {lo[0], lo[2], lo[1], lo[3]};
+    const uint32_t a1h[4] = {hi[4], hi[6], hi[5], hi[7]};
+    const uint32_t a1l[4] = {lo[4], lo[6], lo[5], lo[7]};
+    // B fragment of column block c: (hi[2c], hi[2c+1]).
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+      const int cb = HALF == 0 ? t : (t == 0 ? 3 : t + 1);
+      const bool rb1 = HALF == 1 && t > 0;
+      const uint32_t(&ah)[4] = rb1 ? a1h : a0h;
+      const uint32_t(&al)[4] = rb1 ? a1l : a0l;
+      MmaTf32(acc[t], al, hi[2 * cb], hi[2 * cb + 1]);
+      MmaTf32(acc[t], ah, lo[2 * cb], lo[2 * cb + 1]);
+      MmaTf32(acc[t], ah, hi[2 * cb], hi[2 * cb + 1]);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 3; ++t) {
+    const int cb = HALF == 0 ? t : (t == 0 ? 3 : t + 1);
+    const int i0 = (HALF == 1 && t > 0) ? 16 + g : g;
+    const int j0 = 8 * cb + 2 * tig;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = i0 + (e >= 2 ? 8 : 0);
+      const int j = j0 + (e & 1);
+      if (i < j && j < R) o[i * (2 * R - i - 1) / 2 + j - i - 1] = acc[t][e];
+    }
+  }
+}
+
+constexpr int kInteractSlots = 4;
+constexpr int kSampleRing = 8;  // > kInteractSlots + 1 local samples in flight
+constexpr int kSlotSpinLimit = 1 << 22;  // polls (~1 s with the back-off)
+
+// Warp-wide: waits until *flag == want (shared memory); false if the wait
+// ran out.
+__device__ __forceinline__ bool WaitShared(const volatile long long* flag,
+                                           long long want) {
+  for (int it = 0; it < kSlotSpinLimit; ++it) {
+    if (*flag == want) return true;
+    __nanosleep(64);
+  }
+  return false;
+}
+
+template <int DT, int WM>
+__global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
+    PoolInteractKernel(const __grid_constant__ PoolParams p,
+                       const InteractArgs a) {
+  constexpr int G = 32, V = 1;
+  constexpr bool EXACT = true;
+  constexpr int PPV = ElemsPerVec<DT>::value / 2;
+  constexpr int U = RowsInFlight<DT, V>::value;
+  constexpr int D = G * ElemsPerVec<DT>::value;
+  constexpr int kNs = kInteractSlots;
+  EnterDependent();
+  if (!p.fused_checks && p.status->group_error != 0) return;
+  extern __shared__ float4 smem_vec[];
+  __shared__ long long owner[kNs];  // local sample allowed in each slot
+  __shared__ int filled[kNs];       // rows stored for that sample
+  __shared__ long long next_item;
+  __shared__ long long sample_of[kSampleRing];   // global sample of ls
+  __shared__ long long sample_tag[kSampleRing];  // the ls stored there
+  const int T = p.n, R = T + 1, RS = a.row_stride;
+  const int P = R * (R - 1) / 2;
+  const int64_t width = D + P;
+  float* z = reinterpret_cast<float*>(smem_vec);
+  const int lane = threadIdx.x & 31;
+  const int gl = lane;
+  const unsigned gmask = 0xffffffffu;
+  if (threadIdx.x < kNs) {
+    owner[threadIdx.x] = threadIdx.x;
+    filled[threadIdx.x] = 0;
+  }
+  if (threadIdx.x < kSampleRing) sample_tag[threadIdx.x] = -1;
+  if (threadIdx.x == 0) next_item = kThreads / 32;
+  __syncthreads();
+
+  // Item u -> (local sample, request, global sample); false once the
+  // samples are used up (or a wait ran out). Fetches are not in local
+  // order, so a sample past the end can precede valid ones: the warp that
+  // fetched it passes its slot on (FreeSlot) once it holds no other item.
+  auto resolve = [&](int64_t item, int64_t* ls, int* t, int64_t* gs,
+                     bool* fetched) {
+    *ls = item / T;
+    *t = static_cast<int>(item % T);
+    *fetched = *t == 0;
+    const int k = static_cast<int>(*ls % kSampleRing);
+    volatile long long* vs = &sample_of[k];
+    long long g = 0;
+    if (*t == 0) {
+      if (lane == 0) {
+        g = atomicAdd(&p.status->work_counter, 1u);
+        *vs = g;
+        __threadfence_block();
+        *reinterpret_cast<volatile long long*>(&sample_tag[k]) = *ls;
+      }
+      g = __shfl_sync(0xffffffffu, g, 0);
+    } else {
+      if (!WaitShared(&sample_tag[k], *ls)) {
+        if (lane == 0) RecordError(p.status, 0, kErrDeviceWait);
+        *fetched = false;
+        return false;
+      }
+      g = *vs;
+    }
+    *gs = g;
+    return g < a.batch;
+  };
+  // Passes the slot of local sample ls (past the end: no rows, no
+  // interaction) on to ls + kNs once ls may hold it.
+  auto free_slot = [&](int64_t lsv) {
+    const int sl = static_cast<int>(lsv % kNs);
+    if (!WaitShared(&owner[sl], lsv)) {
+      if (lane == 0) RecordError(p.status, 0, kErrDeviceWait);
+      return;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      *reinterpret_cast<volatile long long*>(&owner[sl]) = lsv + kNs;
+    }
+  };
+  int64_t u = threadIdx.x / 32;
+  int t;
+  int64_t ls, bag, begin, end;
+  bool fetched;
+  if (!resolve(u, &ls, &t, &bag, &fetched)) {
+    if (fetched) free_slot(ls);
+    return;
+  }
+  {
+    const BagDesc& d = p.d[t];
+    begin = LoadIndex(d.offsets, d.offs64, bag);
+    end = LoadIndex(d.offsets, d.offs64, bag + 1);
+  }
+  bool have_chunk = false;
+  int64_t cid = 0;
+  float cw = 1.0f;
+  for (;;) {
+    const BagDesc& d = p.d[t];
+    // Lookahead: take the next item now and load its offsets.
+    long long nu = 0;
+    if (lane == 0) {
+      nu = atomicAdd(reinterpret_cast<unsigned long long*>(&next_item), 1ull);
+    }
+    nu = __shfl_sync(0xffffffffu, nu, 0);
+    int nt = t;
+    int64_t nls = 0, nbag = 0, nbegin = 0, nend = 0;
+    bool nfetched;
+    const bool has_next = resolve(nu, &nls, &nt, &nbag, &nfetched);
+    if (has_next) {
+      const BagDesc& nd = p.d[nt];
+      nbegin = LoadIndex(nd.offsets, nd.offs64, nbag);
+      nend = LoadIndex(nd.offsets, nd.offs64, nbag + 1);
+    }
+    bool next_chunk = false;
+    const int slot = static_cast<int>(ls % kNs);
+    float* zs = z + static_cast<size_t>(slot) * R * RS;
+    const bool ok = CheckBag(p, d, begin, end);
+    u64 acc[V][PPV];
+#pragma unroll
+    for (int k = 0; k < PPV; ++k) acc[0][k] = 0;
+    float wsum = 0.0f;
+    if (ok) {
+      const int row_vecs = G * V;
+      const uint4* rows = static_cast<const uint4*>(d.rows) + gl;
+      if (!have_chunk) LoadChunk<WM>(d, begin, end, gl, &cid, &cw);
+      for (int64_t base = begin; base < end; base += G) {
+        const int cnt = static_cast<int>(end - base < G ? end - base : G);
+        const int64_t id = cid;
+        const float my_w = cw;
+        const bool last = base + G >= end;
+        bool pending = true;
+        auto prefetch = [&]() {
+          if (!pending) return;
+          pending = false;
+          if (!last) {
+            LoadChunk<WM>(d, base + G, end, gl, &cid, &cw);
+          } else if (has_next) {
+            const BagDesc& nd = p.d[nt];
+            if (SafeBag(nd, nbegin, nend)) {
+              LoadChunk<WM>(nd, nbegin, nend, gl, &cid, &cw);
+              next_chunk = true;
+            }
+          }
+        };
+        const int my_row = StageRow(p, d, id, base + gl, gl < cnt);
+        int j0 = 0;
+        if (__all_sync(gmask, gl >= cnt || my_row >= 0)) {
+          for (; j0 + U <= cnt; j0 += U) {
+            FullBatch<DT, G, V, EXACT, WM, U>(d, rows, row_vecs, gl, gmask,
+                                           my_row, my_w, j0, cnt, acc, &wsum,
+                                           prefetch);
+          }
+        }
+        for (; j0 < cnt; j0 += U) {
+          const int n = cnt - j0 < U ? cnt - j0 : U;
+          GatherBatch<DT, G, V, EXACT, WM, U>(d, rows, row_vecs, gl, gmask,
+                                           my_row, my_w, j0, n, acc, &wsum,
+                                           prefetch);
+        }
+      }
+    }
+    // The slot may still hold local sample ls - kNs until its interaction
+    // row is out.
+    if (!WaitShared(&owner[slot], ls)) {
+      if (lane == 0) RecordError(p.status, 0, kErrDeviceWait);
+      return;
+    }
+    if (ok) {
+      FinishBag<DT, G, V, EXACT>(d, zs + (1 + t) * RS, true, end - begin,
+                                 WM != kUnweighted, acc, &wsum, gl, G * V);
+    }
+    __syncwarp();
+    __threadfence_block();
+    int done = 0;
+    if (lane == 0) done = atomicAdd(&filled[slot], 1) + 1;
+    done = __shfl_sync(0xffffffffu, done, 0);
+    if (done == T) {
+      // Last row of this sample: its interaction row, then free the slot.
+      __threadfence_block();
+      const float* dense = a.dense + bag * a.dense_stride;
+      float* o = a.out + bag * a.out_stride;
+      for (int c = lane * 4; c < D; c += 128) {
+        *reinterpret_cast<float4*>(zs + c) =
+            __ldg(reinterpret_cast<const float4*>(dense + c));
+      }
+      __syncwarp();
+      for (int c = lane; c < D; c += 32) o[c] = zs[c];  // any out alignment
+      for (int64_t c = width + lane; c < a.out_stride; c += 32) o[c] = 0.0f;
+      GramHalfTf32x3<D, 0>(zs, R, RS, o + D);
+      GramHalfTf32x3<D, 1>(zs, R, RS, o + D);
+      __syncwarp();
+      if (lane == 0) {
+        filled[slot] = 0;
+        __threadfence_block();
+        *reinterpret_cast<volatile long long*>(&owner[slot]) = ls + kNs;
+      }
+    }
+    if (!has_next) {
+      if (nfetched) free_slot(nls);
+      break;
+    }
+    u = nu;
+    ls = nls;
+    t = nt;
+    bag = nbag;
+    begin = nbegin;
+    end = nend;
+    have_chunk = next_chunk;
   }
 }
 
@@ -811,12 +1139,13 @@ int BlocksPerSm(Kernel kernel) {
 // Launches `kernel` on `grid` blocks of kThreads with a programmatic
 // dependency on the previous kernel of the stream (see EnterDependent).
 template <typename... Params, typename... Args>
-cudaError_t LaunchDependent(void (*kernel)(Params...), int grid,
-                            cudaStream_t stream, Args&&... args) {
+cudaError_t LaunchDependentSmem(void (*kernel)(Params...), int grid,
+                                size_t smem, cudaStream_t stream,
+                                Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -824,6 +1153,13 @@ cudaError_t LaunchDependent(void (*kernel)(Params...), int grid,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... Params, typename... Args>
+cudaError_t LaunchDependent(void (*kernel)(Params...), int grid,
+                            cudaStream_t stream, Args&&... args) {
+  return LaunchDependentSmem(kernel, grid, 0, stream,
+                             std::forward<Args>(args)...);
 }
 
 template <typename Kernel>
@@ -943,6 +1279,47 @@ cudaError_t LaunchForDtype(const Layout& l, const PoolParams& p,
   }
 }
 
+// Shared memory of the fused kernel: S samples of R rows (RS floats each).
+size_t InteractSmem(int samples, int rows, int row_stride) {
+  return static_cast<size_t>(samples) * rows * row_stride * sizeof(float);
+}
+
+template <int DT, int WM>
+cudaError_t LaunchInteractFor(const PoolParams& p, InteractArgs a,
+                              cudaStream_t stream) {
+  auto kernel = PoolInteractKernel<DT, WM>;
+  constexpr int D = 32 * ElemsPerVec<DT>::value;
+  const int rows = p.n + 1;
+  a.row_stride = D + 4;  // rows 16-byte aligned, 16-byte bank shift per row
+  a.samples_per_tile = kInteractSlots;
+  const size_t smem = InteractSmem(kInteractSlots, rows, a.row_stride);
+  if (smem > 200 * 1024) return cudaErrorNotSupported;
+  // Set on every launch: the attribute belongs to the current device.
+  cudaError_t e = cudaFuncSetAttribute(
+      kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads,
+                                                smem);
+  // Samples are handed out at run time; no more blocks than samples.
+  int64_t grid = static_cast<int64_t>(SmCount()) * (per_sm > 0 ? per_sm : 1);
+  if (grid > a.batch) grid = a.batch;
+  if (grid < 1) grid = 1;
+  return LaunchDependentSmem(kernel, static_cast<int>(grid), smem, stream, p,
+                             a);
+}
+
+template <int DT>
+cudaError_t LaunchInteractMode(int wm, const PoolParams& p,
+                               const InteractArgs& a, cudaStream_t stream) {
+  switch (wm) {
+    case kUnweighted: return LaunchInteractFor<DT, kUnweighted>(p, a, stream);
+    case kWeightedSum: return LaunchInteractFor<DT, kWeightedSum>(p, a, stream);
+    default: return LaunchInteractFor<DT, kWeightedNorm>(p, a, stream);
+  }
+}
+
 }  // namespace
 
 Layout ChooseLayout(int dtype, int dim, const void* rows) {
@@ -988,6 +1365,25 @@ cudaError_t LaunchPool(const Layout& layout, const PoolParams& p,
     case 1: return LaunchForDtype<1>(layout, p, stream);
     default: return LaunchForDtype<2>(layout, p, stream);
   }
+}
+
+cudaError_t LaunchPoolInteract(const Layout& layout, const PoolParams& p,
+                               const InteractArgs& a, cudaStream_t stream) {
+  if (p.n < 1 || p.n + 1 > 32 || layout.v != 1 || !layout.exact ||
+      layout.dtype > 1 || layout.g != 32) {
+    return cudaErrorNotSupported;
+  }
+  const int wm = WeightModeOf(p.d[0]);
+  for (int k = 1; k < p.n; ++k) {
+    if (WeightModeOf(p.d[k]) != wm) return cudaErrorNotSupported;
+  }
+  if (((reinterpret_cast<uintptr_t>(a.dense) & 15u) != 0) ||
+      a.dense_stride % 4 != 0) {
+    return cudaErrorNotSupported;
+  }
+  if (a.batch <= 0) return cudaSuccess;
+  return layout.dtype == 0 ? LaunchInteractMode<0>(wm, p, a, stream)
+                           : LaunchInteractMode<1>(wm, p, a, stream);
 }
 
 cudaError_t LaunchValidate(const PoolParams& p, int64_t total_work,

@@ -185,6 +185,12 @@ int ResolveSlot(xse_status* st, int k) {
   const StatusSlot& slot = st->slots[k];
   const xse::DevStatus* host = st->host_slot(k);
   for (int32_t i = 0; i < slot.n; ++i) {
+    if (host->req[i].flags & xse::kErrDeviceWait) {
+      return SetError(XSE_INTERNAL,
+                      "A device-side wait of the fused interaction ran out.");
+    }
+  }
+  for (int32_t i = 0; i < slot.n; ++i) {
     const RequestMeta& m = slot.meta[i];
     if (m.stage == kStageEarly) return SetError(m.code, "%s", m.message.c_str());
     const unsigned int flags = host->req[i].flags;
@@ -385,8 +391,12 @@ class DeviceGuard {
   int prev_ = 0, device_ = 0;
 };
 
+// `inter` non-null: the pooled rows feed the dot interaction (the requests'
+// outputs are not used) -- the fused kernel where one serves the layout,
+// else pooling into scratch and the interaction kernel.
 int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
-                 cudaStream_t stream, int32_t flags, xse_status* st) {
+                 cudaStream_t stream, int32_t flags, xse_status* st,
+                 const xse::InteractArgs* inter = nullptr) {
   g_last_launches = 0;
   if (n <= 0 || reqs == nullptr) {
     return SetError(XSE_INVALID_ARGUMENT,
@@ -469,7 +479,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
       m.code = code;
       m.message = buf;
     };
-    if (r.output == nullptr) {
+    if (r.output == nullptr && inter == nullptr) {
       early(kStageEarly, XSE_INVALID_ARGUMENT,
             "FP32 embedding-bag request %d requires an output allocator.",
             false);
@@ -529,9 +539,44 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
   if (any_early && slot.meta[0].stage == kStageEarly) {
     return SetError(slot.meta[0].code, "%s", slot.meta[0].message.c_str());
   }
+  if (inter != nullptr && !any_early) {
+    const int dim = tables[0]->dim;
+    const int64_t width =
+        dim + static_cast<int64_t>(n + 1) * n / 2;
+    for (int32_t i = 0; i < n; ++i) {
+      const Table& t = *tables[i];
+      if (t.dim != dim) {
+        return SetError(XSE_INVALID_ARGUMENT,
+                        "Interaction request %d has dimension %d; request 0 "
+                        "has %d.",
+                        i, t.dim, dim);
+      }
+      if (reqs[i].num_offsets - 1 != inter->batch) {
+        return SetError(XSE_INVALID_ARGUMENT,
+                        "Interaction request %d has %lld bags; the batch has "
+                        "%lld samples.",
+                        i, static_cast<long long>(reqs[i].num_offsets - 1),
+                        static_cast<long long>(inter->batch));
+      }
+      if (t.row_begin != 0 || t.row_end != t.vocab) {
+        return SetError(XSE_INVALID_ARGUMENT,
+                        "Interaction request %d reads a row-wise shard "
+                        "window; the interaction needs whole tables.",
+                        i);
+      }
+    }
+    if (inter->dense_stride < dim || inter->out_stride < width) {
+      return SetError(XSE_INVALID_ARGUMENT,
+                      "Interaction strides too small: dense %lld (dimension "
+                      "%d), output %lld (width %lld).",
+                      static_cast<long long>(inter->dense_stride), dim,
+                      static_cast<long long>(inter->out_stride),
+                      static_cast<long long>(width));
+    }
+  }
   std::string iso_message;
   int iso_code = XSE_OK;
-  if (!any_early) {
+  if (!any_early && inter == nullptr) {
     iso_code = CheckIsolation(reqs, tables, n, &iso_message);
   }
 
@@ -589,40 +634,101 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
       }
     }
     if (timing.first != nullptr) cudaEventRecord(timing.first, stream);
-    // Group descriptors by kernel layout, keeping request order within each.
-    std::map<std::tuple<int, int, int, bool, int>, std::vector<xse::BagDesc>>
-        groups;
-    for (const xse::BagDesc& d : descs) {
+    auto layout_of = [&](const xse::BagDesc& d) {
       xse::Layout l = xse::ChooseLayout(tables[d.slot]->dtype, d.dim, d.rows);
       if (tables[d.slot]->dtype == XSE_DT_I8_ROWWISE &&
           d.scale_bias == nullptr) {
         l.v = 0;  // an empty int8 window: the element-wise kernel
         l.exact = false;
       }
-      // One launch per layout; its weighting modes share it.
-      groups[{l.dtype, l.g, l.v, l.exact, 0}].push_back(d);
-    }
-    for (auto& [key, list] : groups) {
-      const xse::Layout l{std::get<0>(key), std::get<1>(key), std::get<2>(key),
-                          std::get<3>(key), std::get<4>(key)};
-      for (size_t base = 0; base < list.size();
-           base += xse::kMaxDescsPerLaunch) {
+      return l;
+    };
+    // Pooling launches: descriptors grouped by kernel layout, request order
+    // kept within each group.
+    auto launch_groups = [&]() -> cudaError_t {
+      std::map<std::tuple<int, int, int, bool, int>,
+               std::vector<xse::BagDesc>>
+          groups;
+      for (const xse::BagDesc& d : descs) {
+        const xse::Layout l = layout_of(d);
+        // One launch per layout; its weighting modes share it.
+        groups[{l.dtype, l.g, l.v, l.exact, 0}].push_back(d);
+      }
+      for (auto& [key, list] : groups) {
+        const xse::Layout l{std::get<0>(key), std::get<1>(key),
+                            std::get<2>(key), std::get<3>(key),
+                            std::get<4>(key)};
+        for (size_t base = 0; base < list.size();
+             base += xse::kMaxDescsPerLaunch) {
+          xse::PoolParams p{};
+          p.status = dev_status;
+          p.fused_checks = fused ? 1 : 0;
+          const size_t cnt =
+              std::min<size_t>(xse::kMaxDescsPerLaunch, list.size() - base);
+          int64_t tasks = 0;
+          for (size_t k = 0; k < cnt; ++k) {
+            p.d[k] = list[base + k];
+            p.d[k].task_begin = tasks;
+            tasks += xse::TasksFor(l, p.d[k].num_bags);
+          }
+          p.n = static_cast<int32_t>(cnt);
+          p.total_tasks = tasks;
+          cudaError_t le = xse::LaunchPool(l, p, stream, &launches);
+          if (le != cudaSuccess) return le;
+        }
+      }
+      return cudaSuccess;
+    };
+    if (inter == nullptr) {
+      e = launch_groups();
+      if (e != cudaSuccess) return CudaError(e, "pooling launch");
+    } else {
+      // Fused when every request has the layout of request 0 and a fused
+      // kernel serves it.
+      const xse::Layout l0 = layout_of(descs[0]);
+      bool same = descs.size() <= static_cast<size_t>(xse::kMaxDescsPerLaunch);
+      for (const xse::BagDesc& d : descs) {
+        const xse::Layout l = layout_of(d);
+        same = same && l.dtype == l0.dtype && l.g == l0.g && l.v == l0.v &&
+               l.exact == l0.exact;
+      }
+      e = cudaErrorNotSupported;
+      if (same) {
         xse::PoolParams p{};
         p.status = dev_status;
         p.fused_checks = fused ? 1 : 0;
-        const size_t cnt =
-            std::min<size_t>(xse::kMaxDescsPerLaunch, list.size() - base);
-        int64_t tasks = 0;
-        for (size_t k = 0; k < cnt; ++k) {
-          p.d[k] = list[base + k];
-          p.d[k].task_begin = tasks;
-          tasks += xse::TasksFor(l, p.d[k].num_bags);
-        }
-        p.n = static_cast<int32_t>(cnt);
-        p.total_tasks = tasks;
-        e = xse::LaunchPool(l, p, stream, &launches);
-        if (e != cudaSuccess) return CudaError(e, "pooling launch");
+        for (size_t k = 0; k < descs.size(); ++k) p.d[k] = descs[k];
+        p.n = static_cast<int32_t>(descs.size());
+        e = xse::LaunchPoolInteract(l0, p, *inter, stream);
+        if (e == cudaSuccess) ++launches;
       }
+      if (e == cudaErrorNotSupported) {
+        (void)cudaGetLastError();
+        // Unfused: pool into scratch, then the interaction kernel.
+        const int dim = descs[0].dim;
+        const int64_t width = static_cast<int64_t>(n) * dim;
+        float* scratch = nullptr;
+        const size_t bytes = static_cast<size_t>(
+            std::max<int64_t>(inter->batch * width, 4) * sizeof(float));
+        e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, stream);
+        if (e != cudaSuccess) return CudaError(e, "interaction scratch");
+        for (size_t k = 0; k < descs.size(); ++k) {
+          descs[k].out = scratch + k * dim;
+          descs[k].out_stride = width;
+          descs[k].vec_out = static_cast<int8_t>(dim % 4 == 0);
+        }
+        e = launch_groups();
+        if (e == cudaSuccess) {
+          e = xse::LaunchDotInteraction(inter->dense, inter->dense_stride,
+                                        scratch, width, inter->batch, n, dim,
+                                        inter->out, inter->out_stride,
+                                        stream);
+          ++launches;
+        }
+        cudaError_t fe = cudaFreeAsync(scratch, stream);
+        if (e == cudaSuccess) e = fe;
+      }
+      if (e != cudaSuccess) return CudaError(e, "interaction launch");
     }
     if (timing.second != nullptr) cudaEventRecord(timing.second, stream);
   }
@@ -946,6 +1052,36 @@ int xse_engine_execute_batch(xse_engine* engine, const xse_bag_request* reqs,
   }
   std::lock_guard<std::mutex> lock(engine->default_status_mu);
   return ExecuteBatch(engine, reqs, n, s, flags, engine->default_status);
+}
+
+int xse_engine_execute_interaction(xse_engine* engine,
+                                   const xse_bag_request* reqs, int32_t n,
+                                   const float* dense, int64_t dense_stride,
+                                   int64_t batch, float* out,
+                                   int64_t out_stride, void* stream,
+                                   int32_t flags, xse_status* status) {
+  if (engine == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null engine");
+  if (dense == nullptr || out == nullptr || batch < 0) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Interaction needs dense rows, an output and a "
+                    "non-negative batch.");
+  }
+  xse::InteractArgs a{};
+  a.dense = dense;
+  a.dense_stride = dense_stride;
+  a.out = out;
+  a.out_stride = out_stride;
+  a.batch = batch;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (status != nullptr) {
+    return ExecuteBatch(engine, reqs, n, s, flags, status, &a);
+  }
+  if ((flags & XSE_EXEC_ASYNC) != 0) {
+    return SetError(XSE_INVALID_ARGUMENT,
+                    "Asynchronous execution needs a caller-owned status.");
+  }
+  std::lock_guard<std::mutex> lock(engine->default_status_mu);
+  return ExecuteBatch(engine, reqs, n, s, flags, engine->default_status, &a);
 }
 
 int xse_status_wait(xse_status* status, void* stream) {

@@ -42,6 +42,7 @@ enum : unsigned int {
   kErrLastExceedsIds = 2u,     // final offset > number of ids
   kErrLastExceedsWeights = 4u, // final offset > number of weights
   kErrBadId = 8u,              // some id outside [0, vocab)
+  kErrDeviceWait = 128u,       // a bounded device-side wait ran out
 };
 
 struct DevRequestStatus {
@@ -54,7 +55,8 @@ struct DevRequestStatus {
 
 struct DevStatus {
   unsigned int group_error;  // nonzero once any request failed validation
-  unsigned int reserved[3];
+  unsigned int work_counter;  // samples handed out by the fused interaction
+  unsigned int reserved[2];
   DevRequestStatus req[1];   // capacity set at allocation
 };
 
@@ -109,6 +111,23 @@ cudaError_t LaunchInterleaveScaleBias(const float* scale, const float* bias,
                                       cudaStream_t stream);
 // Sets the calling thread's message returned by xse_last_error().
 void SetLastErrorMessage(const char* message);
+
+// Fused pooling + dot interaction (PoolInteractKernel, csrc/xse_bag.cu).
+struct InteractArgs {
+  const float* dense;        // [batch] rows of dim floats, 16-byte aligned
+  int64_t dense_stride;      // floats, multiple of 4
+  float* out;                // [batch] rows of out_stride floats
+  int64_t out_stride;        // >= dim + (T+1)T/2
+  int64_t batch;
+  int32_t samples_per_tile;  // shared-memory sample slots (set by the launcher)
+  int32_t row_stride;        // set by the launcher
+};
+
+// Launches the fused kernel over p's descriptors (request order; each is one
+// table with a.batch bags). Returns cudaErrorNotSupported, launching
+// nothing, when no fused kernel serves this layout, weighting or size.
+cudaError_t LaunchPoolInteract(const Layout& layout, const PoolParams& p,
+                               const InteractArgs& a, cudaStream_t stream);
 
 cudaError_t LaunchDotInteraction(const float* dense, int64_t dense_stride,
                                  const float* pooled, int64_t pooled_stride,

@@ -161,16 +161,29 @@ class DenseTower:
   def forward(self, dense, pooled, *, stream=None):
     """dense [B, num_dense] fp32, pooled [B, T, dim] fp32 (a sample's T rows
     contiguous) -> predictions [B] (a view of an internal buffer)."""
-    batch = dense.shape[0]
-    bufs = self._buffers_for(batch)
+    x = self.bottom_forward(dense, stream=stream)
+    inter = self.interaction_buffer(dense.shape[0])
+    C.check(C.lib.xse_dot_interaction_strided(
+        x.data_ptr(), x.stride(0), pooled.data_ptr(), pooled.stride(0),
+        dense.shape[0], self.num_tables, self.dim, inter.data_ptr(),
+        inter.stride(0), stream_handle(stream)))
+    return self.top_forward(inter, stream=stream)
+
+  def bottom_forward(self, dense, *, stream=None):
+    """The bottom MLP: [B, num_dense] -> [B, dim] (an internal buffer)."""
+    bufs = self._buffers_for(dense.shape[0])
     x = dense
     for layer, out in zip(self.bottom, bufs["bottom"]):
       x = self._layer(x, layer, out, bufs, stream)
-    inter = bufs["inter"]
-    C.check(C.lib.xse_dot_interaction_strided(
-        x.data_ptr(), x.stride(0), pooled.data_ptr(), pooled.stride(0), batch,
-        self.num_tables, self.dim, inter.data_ptr(), inter.stride(0),
-        stream_handle(stream)))
+    return x
+
+  def interaction_buffer(self, batch):
+    """The [B, width_stride] interaction rows the top MLP reads."""
+    return self._buffers_for(batch)["inter"]
+
+  def top_forward(self, inter, *, stream=None):
+    """The top MLP over interaction rows -> predictions [B]."""
+    bufs = self._buffers_for(inter.shape[0])
     x = inter
     for layer, out in zip(self.top, bufs["top"]):
       x = self._layer(x, layer, out, bufs, stream)
@@ -213,8 +226,11 @@ class DLRM:
 
   def __init__(self, engine: EmbeddingEngine, feature_names: Sequence[str],
                dim=128, num_dense=13, seed=0, device="cuda",
-               math=C.MATH_FP32):
+               math=C.MATH_FP32, fused_interaction=True):
     self.engine = engine
+    # Pooling and the dot interaction in one engine call
+    # (execute_interaction): the pooled rows stay on chip.
+    self.fused_interaction = fused_interaction
     self.features = list(feature_names)
     self.dim = dim
     self.tower = DenseTower(num_dense, len(self.features), dim, seed,
@@ -255,6 +271,12 @@ class DLRM:
     # Fused checks: the pooled rows are internal to the forward, so a
     # failing group need not leave them untouched (the error is still
     # raised, or reported by status.wait()); no separate validation pass.
+    if self.fused_interaction:
+      x = self.tower.bottom_forward(dense, stream=stream)
+      inter = self.tower.interaction_buffer(dense.shape[0])
+      self.engine.execute_interaction(requests, x, inter, stream=stream,
+                                      status=status, fused=True)
+      return self.tower.top_forward(inter, stream=stream)
     self.engine.execute_batch(requests, stream=stream, status=status,
                               fused=True)
     return self.tower.forward(dense, pooled, stream=stream)

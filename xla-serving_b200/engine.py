@@ -59,7 +59,9 @@ class BagRequest:
   feature_name: str
   ids: torch.Tensor
   offsets: torch.Tensor  # absolute CSR offsets, num_bags + 1 entries
-  output: torch.Tensor   # [num_bags, dim] or a strided view of a wider buffer
+  output: Optional[torch.Tensor]  # [num_bags, dim] or a strided view of a
+                                  # wider buffer (None for
+                                  # execute_interaction)
   weights: Optional[torch.Tensor] = None
   output_stride: int = 0  # floats between bags; 0 = dim
 
@@ -246,6 +248,32 @@ class EmbeddingEngine:
     rc = C.lib.xse_engine_execute_batch(
         self._handle, arr, len(requests), stream_handle(stream), flags,
         status.handle if status is not None else None)
+    del names
+    C.check(rc)
+
+  def execute_interaction(self, requests: Sequence[BagRequest], dense, out,
+                          *, stream=None, fused=False,
+                          status: Optional[Status] = None):
+    """Pools request t (feature t of every sample; `output` unused, may be
+    None) and writes the dot interaction of [dense_b; pooled_b,0..T-1] into
+    out [batch, >= dim + (T+1)T/2] (fp32): one fused kernel where it serves
+    the tables' layout, without writing the pooled rows. Flags and status as
+    execute_batch."""
+    arr, names = self._c_requests(requests)
+    flags = C.EXEC_FUSED if fused else C.EXEC_STRICT
+    if status is not None:
+      flags |= C.EXEC_ASYNC
+    if dense.dtype != torch.float32 or out.dtype != torch.float32:
+      raise C.XseError(C.INVALID_ARGUMENT, "dense and out must be float32")
+    if dense.dim() != 2 or out.dim() != 2 or dense.stride(1) != 1 or \
+        out.stride(1) != 1 or out.shape[0] != dense.shape[0]:
+      raise C.XseError(C.INVALID_ARGUMENT,
+                       "dense [B, dim] and out [B, width] need unit column "
+                       "stride and one batch")
+    rc = C.lib.xse_engine_execute_interaction(
+        self._handle, arr, len(requests), dense.data_ptr(), dense.stride(0),
+        dense.shape[0], out.data_ptr(), out.stride(0), stream_handle(stream),
+        flags, status.handle if status is not None else None)
     del names
     C.check(rc)
 
