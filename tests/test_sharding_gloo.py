@@ -1,6 +1,6 @@
 """CPU tests of the sharded paths' host logic with world-size-2 gloo ranks:
-placement, sample-block request slicing, the pipelined pairwise exchange and
-the chunked reduce-scatter. Each rank pools with the oracle on the CPU (the
+placement, sample-block request slicing, the pipelined pairwise exchange,
+the chunked reduce-scatter and the ids all-to-all of data-parallel input. Each rank pools with the oracle on the CPU (the
 test stands in for the GPU pooling kernels), then the exchanged result is
 compared with one process pooling every table over the whole batch: bit for
 bit table-wise, within 1e-5 of the magnitude sum row-wise (partial sums are
@@ -93,6 +93,61 @@ def _tablewise_rank(rank, world, port, mode, results):
     dist.destroy_process_group()
 
 
+class TorchPacker:
+  """The packing step of sharding.IdsAllToAll on CPU tensors (the GPU runs
+  the kernels of include/xse_shard.h; this stands in for them here)."""
+
+  @staticmethod
+  def extents(jobs):
+    out = []
+    for ids, offsets, _, *_ in jobs:
+      lo, hi = int(offsets[0]), int(offsets[-1])
+      out.append(hi - lo if 0 <= lo <= hi <= ids.numel() else -1)
+    return torch.tensor(out, dtype=torch.int64)
+
+  @staticmethod
+  def pack(jobs):
+    for ids, offsets, weights, d_ids, d_offs, d_w, base in jobs:
+      lo, hi = int(offsets[0]), int(offsets[-1])
+      d_ids.copy_(ids[lo:hi])
+      d_offs.copy_(offsets.to(torch.int64) - lo + base)
+      if weights is not None and d_w is not None:
+        d_w.copy_(weights[lo:hi])
+
+
+def _ids_a2a_rank(rank, world, port, mode, results):
+  """Data-parallel input: this rank holds every table's ids for its own
+  sample block only (absolute offsets into the whole batch's arrays)."""
+  os.environ["MASTER_ADDR"] = "127.0.0.1"
+  os.environ["MASTER_PORT"] = str(port)
+  dist.init_process_group("gloo", rank=rank, world_size=world)
+  try:
+    from conftest import load_package  # pylint: disable=import-outside-toplevel
+    sharding = load_package().sharding
+    plan = sharding.ShardPlan(world, rank)
+    tables = make_tables()
+    b0, b1 = plan.sample_block(BATCH, rank)
+    dp, by_name = [], {}
+    for t in range(NUM_TABLES):
+      ids, offsets, weights = make_batch(t)
+      name = f"f{t}"
+      by_name[name] = (tables[t], COMBINE[t])
+      dp.append((name, torch.from_numpy(ids),
+                 torch.from_numpy(offsets[b0:b1 + 1]),
+                 None if weights is None else torch.from_numpy(weights)))
+    ids_a2a = sharding.IdsAllToAll(plan, BATCH, NUM_TABLES,
+                                   packer=TorchPacker())
+    ex = sharding.TablewiseExchange(plan, BATCH, NUM_TABLES, DIM,
+                                    cpu_pooler(by_name), mode=mode)
+    ex.recv.fill_(float("nan"))
+    for _ in range(2):  # buffers are rebuilt per step
+      blocks = ids_a2a.run(dp)
+      ex.run(ex.schedule(blocks=blocks))
+    results[rank] = ex.sample_major().numpy().copy()
+  finally:
+    dist.destroy_process_group()
+
+
 def _rowwise_rank(rank, world, port, chunks, results):
   os.environ["MASTER_ADDR"] = "127.0.0.1"
   os.environ["MASTER_PORT"] = str(port)
@@ -160,6 +215,20 @@ def test_tablewise_exchange_gloo(mode):
   tables = make_tables()
   want = full_pooled(tables)
   got = _spawn(_tablewise_rank, mode)
+  world = 2
+  block = BATCH // world
+  for r in range(world):
+    np.testing.assert_array_equal(got[r], want[r * block:(r + 1) * block])
+
+
+@pytest.mark.parametrize("mode", ["pipelined", "a2a"])
+def test_ids_all_to_all_then_tablewise_gloo(mode):
+  """Data-parallel ids moved to the table owners (IdsAllToAll), pooled there
+  and returned: the same rows, bit for bit, as pooling every table over the
+  whole batch in one process."""
+  tables = make_tables()
+  want = full_pooled(tables)
+  got = _spawn(_ids_a2a_rank, mode)
   world = 2
   block = BATCH // world
   for r in range(world):

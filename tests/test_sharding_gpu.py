@@ -1,7 +1,8 @@
 """Sharded pooling on two GPUs (one process each, NCCL): table-wise placement
 with the pipelined pairwise exchange, with one all-to-all and with pooled rows
 stored straight into the owner's buffer over NVLink, and row-wise windows
-with the chunked reduce-scatter, through the engine's kernels. The
+with the chunked reduce-scatter, and data-parallel input moved to the table
+owners by the ids all-to-all, through the engine's kernels. The
 result on each rank is compared with the oracle pooling every table over the
 whole batch: bit for bit table-wise, within 1e-5 relative to the magnitude
 sum row-wise (partials are added in another order). Needs two GPUs."""
@@ -77,7 +78,31 @@ def _rank_main(rank, world, port, mode, results):
                        torch.from_numpy(offsets).cuda(),
                        None if weights is None else
                        torch.from_numpy(weights).cuda()))
-    if mode == "rowwise":
+    if mode.startswith("ids_a2a"):
+      # Data-parallel input: every table's ids for this rank's samples only.
+      b0, b1 = plan.sample_block(BATCH, rank)
+      dp = []
+      for t in range(NUM_TABLES):
+        ids, offsets, weights = batch_of(t)
+        dp.append((f"f{t}", torch.from_numpy(ids).cuda(),
+                   torch.from_numpy(offsets[b0:b1 + 1]).cuda(),
+                   None if weights is None else
+                   torch.from_numpy(weights).cuda()))
+      ids_a2a = sharding.IdsAllToAll(plan, BATCH, NUM_TABLES, device="cuda")
+      ex = sharding.TablewiseExchange(plan, BATCH, NUM_TABLES, DIM, pool,
+                                      device="cuda",
+                                      mode=mode.split("_")[2])
+      outs = []
+      for _ in range(3):
+        ex.run(ex.schedule(blocks=ids_a2a.run(dp)))
+        outs.append(ex.sample_major())
+      status.wait()
+      ex.check()
+      for o in outs[:-1]:
+        torch.testing.assert_close(o, outs[-1], rtol=0, atol=0)
+      out = outs[-1]
+      ex.close()
+    elif mode == "rowwise":
       ex = sharding.RowwiseExchange(plan, BATCH, NUM_TABLES, DIM, pool,
                                     chunks=2, device="cuda")
       for _ in range(2):  # twice: buffers are reused across steps
@@ -116,7 +141,8 @@ def full_pooled():
 
 
 @pytest.mark.parametrize("mode", ["tablewise_pipelined", "tablewise_a2a",
-                                  "tablewise_peer", "rowwise"])
+                                  "tablewise_peer", "rowwise",
+                                  "ids_a2a_peer", "ids_a2a_pipelined"])
 def test_sharded_two_gpus(mode):
   if torch.cuda.device_count() < 2:
     pytest.skip("needs two GPUs")

@@ -224,6 +224,29 @@ SIGNATURES.update({
 })
 
 
+class CsrSegment(ctypes.Structure):
+  """xse_csr_segment (include/xse_shard.h)."""
+  _fields_ = [
+      ("ids", ctypes.c_void_p),
+      ("offsets", ctypes.c_void_p),
+      ("weights", ctypes.c_void_p),
+      ("num_ids", ctypes.c_int64),
+      ("num_bags", ctypes.c_int64),
+      ("ids_type", ctypes.c_int32),
+      ("offsets_type", ctypes.c_int32),
+      ("dst_ids", ctypes.c_void_p),
+      ("dst_offsets", ctypes.c_void_p),
+      ("dst_weights", ctypes.c_void_p),
+      ("dst_base", ctypes.c_int64),
+  ]
+
+
+SIGNATURES.update({
+    "xse_csr_extents": (_I, [ctypes.POINTER(CsrSegment), _I32, _P, _P]),
+    "xse_csr_pack": (_I, [ctypes.POINTER(CsrSegment), _I32, _P]),
+})
+
+
 def _load():
   if not os.path.exists(LIB_PATH):
     raise ImportError(

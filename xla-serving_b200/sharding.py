@@ -30,6 +30,12 @@ A bag request over samples [b0, b1) of a CSR batch is the same ids and
 weights with the offsets slice [b0, b1] (absolute offsets, first entry may be
 above zero, as the reference's EmbeddingBagInput allows,
 data/cpu_embedding/cc/embedding_bag.h:66-72), so sample blocks need no copies.
+
+When the input arrives data-parallel instead (each rank holds every table's
+ids for its own sample block), IdsAllToAll moves each table's block to the
+table's owner first: one packing launch (include/xse_shard.h) per rank and
+NCCL all-to-alls of the extents, the rebased offsets, the ids and the
+weights; the owner pools block s straight from source s's chunk.
 """
 
 import ctypes
@@ -171,6 +177,189 @@ class PeerGroup:
       self._handle = ctypes.c_void_p()
 
 
+CsrFeature = Tuple[str, torch.Tensor, torch.Tensor, Optional[torch.Tensor]]
+
+
+def _index_type(t: torch.Tensor) -> int:
+  if t.dtype == torch.int64:
+    return C.INDEX_I64
+  if t.dtype == torch.int32:
+    return C.INDEX_I32
+  raise TypeError(f"ids and offsets must be int32 or int64, got {t.dtype}")
+
+
+class CsrPacker:
+  """The packing kernels of include/xse_shard.h over device tensors. A job
+  is (ids, offsets, weights, dst_ids, dst_offsets, dst_weights, dst_base):
+  bags [0, len(offsets) - 1) of the source, their id range copied to dst_ids
+  (and weights to dst_weights when both are given) and the offsets rebased
+  to start at dst_base written to dst_offsets (int64)."""
+
+  @staticmethod
+  def _segments(jobs, with_dst):
+    segs = (C.CsrSegment * max(len(jobs), 1))()
+    for k, (ids, offsets, weights, d_ids, d_offs, d_w, base) in enumerate(
+        jobs):
+      g = segs[k]
+      g.ids = ids.data_ptr() if ids.numel() else None
+      g.offsets = offsets.data_ptr()
+      g.weights = None if weights is None else weights.data_ptr()
+      g.num_ids = ids.numel()
+      g.num_bags = offsets.numel() - 1
+      g.ids_type = _index_type(ids)
+      g.offsets_type = _index_type(offsets)
+      if with_dst:
+        g.dst_ids = d_ids.data_ptr() if d_ids.numel() else None
+        g.dst_offsets = d_offs.data_ptr()
+        g.dst_weights = (None if d_w is None or weights is None
+                         else d_w.data_ptr())
+        g.dst_base = base
+    return segs
+
+  def extents(self, jobs, stream=None) -> torch.Tensor:
+    """int64 device tensor: each job's id count, -1 for a bad range."""
+    out = torch.empty(len(jobs), dtype=torch.int64, device="cuda")
+    if jobs:
+      C.check(C.lib.xse_csr_extents(self._segments(jobs, False), len(jobs),
+                                    out.data_ptr(), stream_handle(stream)))
+    return out
+
+  def pack(self, jobs, stream=None):
+    if jobs:
+      C.check(C.lib.xse_csr_pack(self._segments(jobs, True), len(jobs),
+                                 stream_handle(stream)))
+
+
+class IdsAllToAll:
+  """Data-parallel input -> the table-wise layout.
+
+  run(features): features[t] = (feature name, ids, offsets, weights) of
+  global table t for this rank's sample block (offsets: B/W + 1 absolute
+  entries; the same weighting per table on every rank). Returns blocks,
+  blocks[s][k] = (name, ids, offsets, weights) of local table k (global
+  table rank + k W) for the samples of rank s: offsets are B/W + 1 int64
+  entries into source s's received chunk `ids` -- what
+  TablewiseExchange.schedule(blocks=...) takes.
+
+  Steps: the extents of the W x T_q slices (one launch), an all-to-all of
+  them and one device->host read (the sizes NCCL needs), one packing launch
+  that writes, per destination, its tables' id ranges back to back with
+  rebased offsets, then all-to-alls of the offsets, the ids and (if any
+  table is weighted) the weights.
+  """
+
+  def __init__(self, plan: ShardPlan, batch: int, num_tables: int,
+               device=None, group=None, packer=None):
+    self.plan = plan
+    self.batch = batch
+    self.num_tables = num_tables
+    self.block = plan.block_size(batch)
+    self.device = device
+    self.group = group
+    self.packer = CsrPacker() if packer is None else packer
+    w = plan.world
+    self.counts = [len(plan.tables_of(q, num_tables)) for q in range(w)]
+    self.local = plan.tables_of(plan.rank, num_tables)
+    # Send order: destination-major, each destination's tables in order.
+    self.order = [t for q in range(w) for t in plan.tables_of(q, num_tables)]
+    self.bytes_last = 0  # bytes this rank sent in the last run()
+
+  def run(self, features: Sequence[CsrFeature]):
+    w, nb = self.plan.world, self.block
+    if len(features) != self.num_tables:
+      raise ValueError(f"expected {self.num_tables} features, got "
+                       f"{len(features)}")
+    for name, _, offsets, _ in features:
+      if offsets.numel() != nb + 1:
+        raise ValueError(f"feature {name}: {offsets.numel()} row pointers, "
+                         f"the sample block needs {nb + 1}")
+    id_dtype = features[0][1].dtype
+    if any(f[1].dtype != id_dtype for f in features):
+      raise TypeError("all features' ids must share one dtype")
+    weighted = [f[3] is not None for f in features]
+    any_w = any(weighted)
+    jobs_src = [(features[t][1], features[t][2], features[t][3])
+                for t in self.order]
+    ext = self.packer.extents([j + (None, None, None, 0) for j in jobs_src])
+    n_local = len(self.local)
+    recv_ext = torch.empty(w * n_local, dtype=torch.int64, device=ext.device)
+    if w > 1:
+      dist.all_to_all_single(recv_ext, ext, output_split_sizes=[n_local] * w,
+                             input_split_sizes=self.counts, group=self.group)
+    else:
+      recv_ext.copy_(ext)
+    host = torch.cat([ext, recv_ext]).cpu().tolist()
+    send_ext, recv_list = host[:len(self.order)], host[len(self.order):]
+    for t, e in zip(self.order, send_ext):
+      if e < 0:
+        raise C.XseError(C.INVALID_ARGUMENT,
+                         f"feature {features[t][0]}: row pointers outside "
+                         "the ids (negative, decreasing or past the end)")
+    # Positions: each destination's chunk holds its tables back to back.
+    bases, send_sizes, j = [], [], 0
+    for q in range(w):
+      at = 0
+      for _ in range(self.counts[q]):
+        bases.append(at)
+        at += send_ext[j]
+        j += 1
+      send_sizes.append(at)
+    recv_sizes = [sum(recv_list[s * n_local:(s + 1) * n_local])
+                  for s in range(w)]
+    dev = ext.device
+    send_ids = torch.empty(sum(send_sizes), dtype=id_dtype, device=dev)
+    send_offs = torch.empty((len(self.order), nb + 1), dtype=torch.int64,
+                            device=dev)
+    send_w = (torch.empty(sum(send_sizes), dtype=torch.float32, device=dev)
+              if any_w else None)
+    jobs, start, j = [], 0, 0
+    for q in range(w):
+      for _ in range(self.counts[q]):
+        t = self.order[j]
+        lo, hi = start + bases[j], start + bases[j] + send_ext[j]
+        jobs.append(jobs_src[j] + (
+            send_ids[lo:hi], send_offs[j],
+            None if send_w is None else send_w[lo:hi], bases[j]))
+        j += 1
+      start += send_sizes[q]
+    self.packer.pack(jobs)
+    recv_ids = torch.empty(sum(recv_sizes), dtype=id_dtype, device=dev)
+    recv_offs = torch.empty((w, n_local, nb + 1), dtype=torch.int64,
+                            device=dev)
+    recv_w = (torch.empty(sum(recv_sizes), dtype=torch.float32, device=dev)
+              if any_w else None)
+    if w > 1:
+      dist.all_to_all_single(
+          recv_offs.view(-1), send_offs.view(-1),
+          output_split_sizes=[n_local * (nb + 1)] * w,
+          input_split_sizes=[c * (nb + 1) for c in self.counts],
+          group=self.group)
+      dist.all_to_all_single(recv_ids, send_ids, output_split_sizes=recv_sizes,
+                             input_split_sizes=send_sizes, group=self.group)
+      if any_w:
+        dist.all_to_all_single(recv_w, send_w, output_split_sizes=recv_sizes,
+                               input_split_sizes=send_sizes, group=self.group)
+    else:
+      recv_offs.view(-1).copy_(send_offs.view(-1))
+      recv_ids.copy_(send_ids)
+      if any_w:
+        recv_w.copy_(send_w)
+    esize = send_ids.element_size()
+    self.bytes_last = (sum(send_sizes) * (esize + (4 if any_w else 0)) +
+                       send_offs.numel() * 8)
+    blocks, start = [], 0
+    for s in range(w):
+      end = start + recv_sizes[s]
+      chunk = recv_ids[start:end]
+      wchunk = None if recv_w is None else recv_w[start:end]
+      blocks.append([
+          (features[t][0], chunk, recv_offs[s, k],
+           wchunk if weighted[t] else None)
+          for k, t in enumerate(self.local)])
+      start = end
+    return blocks
+
+
 MODES = ("a2a", "pipelined", "peer")
 # Receive slots of the peer exchange: a step may overwrite a slot once the
 # barrier of the step after its previous use has passed on every rank, so
@@ -254,10 +443,14 @@ class TablewiseExchange:
       out[:, q::self.plan.world, :] = self.recv_from(q)
     return out
 
-  def block_requests(self, features, dest: int, out):
+  def block_requests(self, features, dest: int, out, blocks=None):
     """Requests pooling the samples of rank `dest` into out, a [B/W, T_local,
-    D] tensor or the DevicePointer of one."""
-    b0, b1 = self.plan.sample_block(self.batch, dest)
+    D] tensor or the DevicePointer of one: slices of the whole-batch
+    `features`, or `blocks[dest]` (IdsAllToAll.run) as they are."""
+    if blocks is not None:
+      b0, b1, features = 0, self.block, blocks[dest]
+    else:
+      b0, b1 = self.plan.sample_block(self.batch, dest)
     row = self.num_local * self.dim
     reqs = []
     for k, (name, ids, offsets, weights) in enumerate(features):
@@ -269,20 +462,30 @@ class TablewiseExchange:
       reqs.append(slice_request(base, b0, b1, dst, row))
     return reqs
 
-  def schedule(self, features):
-    """The request groups of one exchange, built once and reused by run().
+  def schedule(self, features=None, blocks=None):
+    """The request groups of one exchange, built once and reused by run()
+    (with `blocks` from IdsAllToAll.run, built again for every step's
+    blocks).
 
-    a2a: [(None, whole-batch requests writing send)] (send [W][B/W][T_local]
-    [D] is [B][T_local][D] in sample order). pipelined: [(dest, requests)]
-    for rank+1, rank+2, ..., then the own block pooled straight into recv.
+    a2a: [(None, requests writing send)] (send [W][B/W][T_local][D] is
+    [B][T_local][D] in sample order). pipelined: [(dest, requests)] for
+    rank+1, rank+2, ..., then the own block pooled straight into recv.
     peer: one group per receive slot, each writing every rank's slot."""
-    if len(features) != self.num_local:
-      raise ValueError(f"rank {self.plan.rank} holds {self.num_local} tables, "
-                       f"got {len(features)} features")
     w, r = self.plan.world, self.plan.rank
+    local = features if blocks is None else blocks[r]
+    if len(local) != self.num_local or (blocks is not None and
+                                        len(blocks) != w):
+      raise ValueError(f"rank {self.plan.rank} holds {self.num_local} tables, "
+                       f"got {len(local)} features")
     if w == 1:
-      return [(r, self.block_requests(features, r, self.recv_from(r)))]
+      return [(r, self.block_requests(features, r, self.recv_from(r),
+                                      blocks))]
     if self.mode == "a2a":
+      if blocks is not None:
+        reqs = []
+        for dest in range(w):
+          reqs += self.block_requests(None, dest, self.send[dest], blocks)
+        return [(None, reqs)]
       whole = self.send.view(self.batch, self.num_local, self.dim)
       reqs = [BagRequest(name, ids, offsets, whole[:, k, :], weights,
                          self.num_local * self.dim)
@@ -293,8 +496,9 @@ class TablewiseExchange:
       for j in range(1, w):
         dest = (r + j) % w
         steps.append((dest, self.block_requests(features, dest,
-                                                self.send[dest])))
-      steps.append((r, self.block_requests(features, r, self.recv_from(r))))
+                                                self.send[dest], blocks)))
+      steps.append((r, self.block_requests(features, r, self.recv_from(r),
+                                           blocks)))
       return steps
     total = self.block * self.num_tables * self.dim
     groups = []
@@ -304,7 +508,8 @@ class TablewiseExchange:
         # Rank dest's slot holds [q][B/W][T_q][D]; this rank writes block r.
         at = 4 * (slot * total + self.recv_offsets[r])
         reqs += self.block_requests(
-            features, dest, DevicePointer(self.peers.address(dest) + at))
+            features, dest, DevicePointer(self.peers.address(dest) + at),
+            blocks)
       groups.append((slot, reqs))
     return groups
 
