@@ -66,6 +66,37 @@ typedef struct xse_resource xse_resource;
 int xse_resource_load(const char* const* asset_names,
                       const char* const* asset_paths, int32_t num_assets,
                       int32_t device, xse_resource** out);
+/* Placement of a resource's tables over the ranks of a sharded job, and the
+ * host -> HBM upload. The reference loads every table into one host
+ * (cpu_embedding_resource.cc:97-225); here rank `rank` of `world` keeps:
+ *   XSE_SHARD_NONE      every table whole (world and rank ignored);
+ *   XSE_SHARD_TABLEWISE table i of the manifest (in manifest order) when
+ *                       i mod world == rank -- the features of other ranks'
+ *                       tables are not registered, their embedding
+ *                       dimensions still answer GetEmbeddingDim;
+ *   XSE_SHARD_ROWWISE   rows [vocab r / world, vocab (r+1) / world) of every
+ *                       table (the engine's shard window), read from the
+ *                       asset at that offset.
+ * Rows are read from the memory-mapped asset into pinned staging buffers of
+ * chunk_bytes (0: 64 MiB; < 0: one pageable cudaMemcpy per table) by
+ * upload_threads host threads (0: 8), double-buffered so that reading the
+ * file overlaps the DMA of the previous chunk. */
+enum { XSE_SHARD_NONE = 0, XSE_SHARD_TABLEWISE = 1, XSE_SHARD_ROWWISE = 2 };
+typedef struct {
+  int32_t world;
+  int32_t rank;
+  int32_t sharding;       /* XSE_SHARD_* */
+  int32_t upload_threads;
+  int64_t chunk_bytes;
+} xse_load_options;
+
+/* xse_resource_load with a placement and upload options (NULL: as
+ * xse_resource_load). */
+int xse_resource_load_sharded(const char* const* asset_names,
+                              const char* const* asset_paths,
+                              int32_t num_assets, int32_t device,
+                              const xse_load_options* options,
+                              xse_resource** out);
 /* An empty resource whose engine is filled through xse_resource_engine
  * (the reference's tests build resources this way). */
 int xse_resource_create(int32_t device, xse_resource** out);

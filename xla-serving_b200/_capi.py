@@ -156,6 +156,17 @@ HB_INVALID, HB_S32, HB_S64, HB_F32 = 0, 1, 2, 3
 HB_MAX_RANK = 8
 
 
+SHARD_NONE, SHARD_TABLEWISE, SHARD_ROWWISE = 0, 1, 2
+
+
+class LoadOptions(ctypes.Structure):
+  """xse_load_options (include/xse_ops.h)."""
+  _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+              ("sharding", ctypes.c_int32),
+              ("upload_threads", ctypes.c_int32),
+              ("chunk_bytes", ctypes.c_int64)]
+
+
 class HostBufferStruct(ctypes.Structure):
   _fields_ = [
       ("data", ctypes.c_void_p),
@@ -173,6 +184,8 @@ SIGNATURES.update({
     "xse_host_buffer_alloc": (_I, [_I32, _I32, ctypes.POINTER(_I64), _HBP]),
     "xse_host_buffer_free": (None, [_HBP]),
     "xse_resource_load": (_I, [_STRS, _STRS, _I32, _I32, _P]),
+    "xse_resource_load_sharded": (_I, [_STRS, _STRS, _I32, _I32,
+                                       ctypes.POINTER(LoadOptions), _P]),
     "xse_resource_create": (_I, [_I32, _P]),
     "xse_resource_destroy": (None, [_P]),
     "xse_resource_engine": (_P, [_P]),

@@ -20,6 +20,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <unordered_map>
 #include <vector>
@@ -862,7 +863,73 @@ int xse_engine_profile_read(xse_engine* engine, double* pool_ms,
   return Ok();
 }
 
-int xse_engine_add_table(xse_engine* engine, const xse_table_desc* desc) {
+}  // extern "C"
+
+namespace xse {
+
+// Host -> HBM copy of table rows through pinned staging: chunk k is copied
+// from the (pageable, often memory-mapped) source into pinned buffer k % 2
+// by `threads` host threads while chunk k - 1's DMA runs, so reading the
+// file and PCIe overlap and page faults are taken in parallel. chunk <= 0
+// copies straight from the source (one pageable cudaMemcpy).
+cudaError_t UploadFromHost(void* dst, const void* src, size_t bytes,
+                           int64_t chunk, int threads) {
+  if (bytes == 0) return cudaSuccess;
+  if (chunk <= 0) return cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+  cudaPointerAttributes attr{};
+  if (cudaPointerGetAttributes(&attr, src) == cudaSuccess &&
+      attr.type == cudaMemoryTypeHost) {  // already pinned
+    return cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+  }
+  (void)cudaGetLastError();
+  const size_t step = std::min<size_t>(static_cast<size_t>(chunk), bytes);
+  if (threads < 1) threads = 1;
+  void* pinned[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  cudaStream_t stream = nullptr;
+  cudaError_t e = cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking);
+  for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
+    e = cudaHostAlloc(&pinned[b], step, cudaHostAllocDefault);
+    if (e == cudaSuccess) {
+      e = cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming);
+    }
+  }
+  const char* from = static_cast<const char*>(src);
+  char* to = static_cast<char*>(dst);
+  for (size_t off = 0, k = 0; off < bytes && e == cudaSuccess;
+       off += step, ++k) {
+    const size_t len = std::min(step, bytes - off);
+    const int b = static_cast<int>(k & 1);
+    if (k >= 2) e = cudaEventSynchronize(done[b]);  // buffer b is free
+    if (e != cudaSuccess) break;
+    // Parallel fill of the staging buffer (16-byte aligned slices).
+    const size_t per = (len / threads + 15) / 16 * 16;
+    std::vector<std::thread> pool;
+    for (int i = 1; i < threads && per * i < len; ++i) {
+      pool.emplace_back([&, i]() {
+        const size_t lo = per * i, hi = std::min(len, per * (i + 1));
+        std::memcpy(static_cast<char*>(pinned[b]) + lo, from + off + lo,
+                    hi - lo);
+      });
+    }
+    std::memcpy(pinned[b], from + off, std::min(len, per > 0 ? per : len));
+    for (auto& th : pool) th.join();
+    e = cudaMemcpyAsync(to + off, pinned[b], len, cudaMemcpyHostToDevice,
+                        stream);
+    if (e == cudaSuccess) e = cudaEventRecord(done[b], stream);
+  }
+  const cudaError_t se = stream ? cudaStreamSynchronize(stream) : cudaSuccess;
+  if (e == cudaSuccess) e = se;
+  for (int b = 0; b < 2; ++b) {
+    if (done[b]) cudaEventDestroy(done[b]);
+    if (pinned[b]) cudaFreeHost(pinned[b]);
+  }
+  if (stream) cudaStreamDestroy(stream);
+  return e;
+}
+
+int AddTable(xse_engine* engine, const xse_table_desc* desc,
+             int64_t upload_chunk, int upload_threads) {
   if (engine == nullptr || desc == nullptr) {
     return SetError(XSE_INVALID_ARGUMENT, "engine and table must be non-null");
   }
@@ -927,10 +994,11 @@ int xse_engine_add_table(xse_engine* engine, const xse_table_desc* desc) {
     e = cudaMalloc(&t->rows, bytes);
     if (e != cudaSuccess) return CudaError(e, "table allocation");
     t->owns_rows = true;
-    e = cudaMemcpy(t->rows, desc->rows, bytes,
-                   desc->placement == XSE_PLACE_COPY_FROM_HOST
-                       ? cudaMemcpyHostToDevice
-                       : cudaMemcpyDeviceToDevice);
+    e = desc->placement == XSE_PLACE_COPY_FROM_HOST
+            ? UploadFromHost(t->rows, desc->rows, bytes, upload_chunk,
+                             upload_threads)
+            : cudaMemcpy(t->rows, desc->rows, bytes,
+                         cudaMemcpyDeviceToDevice);
     if (e != cudaSuccess) return CudaError(e, "table upload");
   }
   if (desc->dtype == XSE_DT_I8_ROWWISE && rows > 0) {
@@ -957,6 +1025,15 @@ int xse_engine_add_table(xse_engine* engine, const xse_table_desc* desc) {
                     desc->name);
   }
   return Ok();
+}
+
+}  // namespace xse
+
+extern "C" {
+
+int xse_engine_add_table(xse_engine* engine, const xse_table_desc* desc) {
+  return xse::AddTable(engine, desc, xse::kDefaultUploadChunk,
+                       xse::kDefaultUploadThreads);
 }
 
 int xse_engine_register_feature(xse_engine* engine, const char* feature,

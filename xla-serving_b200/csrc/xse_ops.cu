@@ -427,6 +427,12 @@ bool ReadFile(const std::string& path, std::string* out) {
 
 }  // namespace
 
+namespace xse {
+// xse_engine_add_table with upload options (csrc/xse_capi.cu).
+int AddTable(xse_engine* engine, const xse_table_desc* desc,
+             int64_t upload_chunk, int upload_threads);
+}  // namespace xse
+
 // ---------------------------------------------------------------------------
 struct xse_resource {
   int device = 0;
@@ -454,9 +460,11 @@ int CombineFromManifest(const std::string& mode, const std::string& table,
   return XSE_OK;
 }
 
-// LoadCpuEmbeddingEngine (cpu_embedding_resource.cc:97-225).
+// LoadCpuEmbeddingEngine (cpu_embedding_resource.cc:97-225), with the
+// placement and upload options of xse_load_options.
 int LoadResource(xse_resource* res, const std::string& manifest_path,
-                 const std::unordered_map<std::string, std::string>& tables) {
+                 const std::unordered_map<std::string, std::string>& tables,
+                 const xse_load_options& opt) {
   std::string text;
   if (!ReadFile(manifest_path, &text)) {
     return Fail(XSE_NOT_FOUND, "Could not read manifest %s",
@@ -470,7 +478,11 @@ int LoadResource(xse_resource* res, const std::string& manifest_path,
                 manifest_path.c_str(), perr.c_str());
   }
   std::unordered_map<std::string, int64_t> table_to_dim;
+  std::unordered_map<std::string, bool> table_local;
+  const bool sharded = opt.sharding != XSE_SHARD_NONE && opt.world > 1;
+  int64_t table_index = -1;
   for (const ManifestTable& t : m.tables) {
+    ++table_index;
     auto it = tables.find(t.name);
     if (it == tables.end()) {
       return Fail(XSE_NOT_FOUND, "Failed to find table asset: %s",
@@ -483,6 +495,9 @@ int LoadResource(xse_resource* res, const std::string& manifest_path,
                   t.vocab_size, t.embedding_dim);
     }
     table_to_dim[t.name] = t.embedding_dim;
+    const bool local = !sharded || opt.sharding != XSE_SHARD_TABLEWISE ||
+                       table_index % opt.world == opt.rank;
+    table_local[t.name] = local;
     int32_t dtype = XSE_DT_F32;
     size_t elem = 4;
     if (t.data_type == "BFLOAT16") {
@@ -520,6 +535,12 @@ int LoadResource(xse_resource* res, const std::string& manifest_path,
     int32_t combine = 0;
     int code = CombineFromManifest(t.combine_mode, t.name, &combine);
     if (code != XSE_OK) return code;
+    if (!local) continue;  // another rank's table (table-wise)
+    int64_t row_begin = 0, row_end = t.vocab_size;
+    if (sharded && opt.sharding == XSE_SHARD_ROWWISE) {
+      row_begin = t.vocab_size * opt.rank / opt.world;
+      row_end = t.vocab_size * (opt.rank + 1) / opt.world;
+    }
     xse_table_desc desc{};
     desc.name = t.name.c_str();
     desc.dtype = dtype;
@@ -527,20 +548,31 @@ int LoadResource(xse_resource* res, const std::string& manifest_path,
     desc.vocab = t.vocab_size;
     desc.dim = static_cast<int32_t>(t.embedding_dim);
     desc.placement = XSE_PLACE_COPY_FROM_HOST;
-    desc.rows = file.data;
+    desc.row_begin = row_begin;
+    desc.row_end = row_end;
+    const char* base = static_cast<const char*>(file.data);
+    desc.rows = base + static_cast<size_t>(row_begin) * t.embedding_dim * elem;
     if (dtype == XSE_DT_I8_ROWWISE) {
-      const char* base = static_cast<const char*>(file.data);
-      desc.scale = reinterpret_cast<const float*>(base + cells);
-      desc.bias = reinterpret_cast<const float*>(base + cells + 4 * t.vocab_size);
+      desc.scale = reinterpret_cast<const float*>(base + cells) + row_begin;
+      desc.bias = reinterpret_cast<const float*>(base + cells +
+                                                 4 * t.vocab_size) +
+                  row_begin;
     }
-    code = xse_engine_add_table(res->engine, &desc);
+    code = xse::AddTable(res->engine, &desc,
+                         opt.chunk_bytes == 0 ? xse::kDefaultUploadChunk
+                                              : opt.chunk_bytes,
+                         opt.upload_threads > 0 ? opt.upload_threads
+                                                : xse::kDefaultUploadThreads);
     if (code != XSE_OK) return FailFromEngine(code);
   }
   for (const ManifestFeature& f : m.features) {
-    int code = xse_engine_register_feature(
-        res->engine, f.name.c_str(), f.table.c_str(),
-        static_cast<int32_t>(f.max_sequence_length));
-    if (code != XSE_OK) return FailFromEngine(code);
+    auto loc = table_local.find(f.table);
+    if (loc == table_local.end() || loc->second) {
+      int code = xse_engine_register_feature(
+          res->engine, f.name.c_str(), f.table.c_str(),
+          static_cast<int32_t>(f.max_sequence_length));
+      if (code != XSE_OK) return FailFromEngine(code);
+    }
     auto it = table_to_dim.find(f.table);
     if (it == table_to_dim.end()) {
       return Fail(XSE_NOT_FOUND, "Failed to find table %s for feature %s",
@@ -989,6 +1021,24 @@ int xse_resource_create(int32_t device, xse_resource** out) {
 int xse_resource_load(const char* const* asset_names,
                       const char* const* asset_paths, int32_t num_assets,
                       int32_t device, xse_resource** out) {
+  return xse_resource_load_sharded(asset_names, asset_paths, num_assets,
+                                   device, nullptr, out);
+}
+
+int xse_resource_load_sharded(const char* const* asset_names,
+                              const char* const* asset_paths,
+                              int32_t num_assets, int32_t device,
+                              const xse_load_options* options,
+                              xse_resource** out) {
+  xse_load_options opt{1, 0, XSE_SHARD_NONE, 0, 0};
+  if (options != nullptr) opt = *options;
+  if (opt.sharding < XSE_SHARD_NONE || opt.sharding > XSE_SHARD_ROWWISE ||
+      (opt.sharding != XSE_SHARD_NONE &&
+       (opt.world < 1 || opt.rank < 0 || opt.rank >= opt.world))) {
+    return Fail(XSE_INVALID_ARGUMENT,
+                "Bad placement: sharding %d, rank %d of %d.", opt.sharding,
+                opt.rank, opt.world);
+  }
   if (out == nullptr || num_assets < 0 ||
       (num_assets > 0 && (asset_names == nullptr || asset_paths == nullptr))) {
     return Fail(XSE_INVALID_ARGUMENT, "invalid asset list");
@@ -1015,7 +1065,7 @@ int xse_resource_load(const char* const* asset_names,
   xse_resource* res = nullptr;
   int code = xse_resource_create(device, &res);
   if (code != XSE_OK) return code;
-  code = LoadResource(res, manifest, tables);
+  code = LoadResource(res, manifest, tables, opt);
   if (code != XSE_OK) {
     const std::string keep = xse_last_error();
     delete res;

@@ -146,6 +146,18 @@ def _is_invalid_table_name(name):
           "\\" in name or ".." in name or name == MANIFEST_ASSET_NAME)
 
 
+def _load_options(placement, upload_threads, chunk_bytes):
+  opt = C.LoadOptions(1, 0, C.SHARD_NONE, int(upload_threads),
+                      int(chunk_bytes))
+  if placement is not None:
+    kind, world, rank = placement
+    kinds = {"table": C.SHARD_TABLEWISE, "row": C.SHARD_ROWWISE}
+    if kind not in kinds:
+      raise ValueError(f"unknown sharding {kind!r} (table or row)")
+    opt.sharding, opt.world, opt.rank = kinds[kind], int(world), int(rank)
+  return opt
+
+
 class CpuEmbeddingResource:
   """Tables (and feature specs) loaded into HBM through the resource's asset
   format: a CpuEmbeddingManifest text proto plus one `<table>.bin` per table
@@ -156,11 +168,19 @@ class CpuEmbeddingResource:
   combine_modes: table name -> "SUM" | "MEAN" | "SQRT_N" (default MEAN, as the
     reference's manifest builder, cpu_embedding_module.py:87).
   feature_specs: [{"name", "table_name", optional "max_sequence_length"}].
+  placement: None (every table whole) or (sharding, world, rank) with
+    sharding "table" (table i of the manifest on rank i mod world) or "row"
+    (rows [vocab r / world, vocab (r+1) / world) of every table).
+  upload_threads, chunk_bytes: the host -> HBM upload (pinned staging chunks
+    filled by that many threads; 0 = defaults, chunk_bytes < 0 = one
+    pageable copy per table).
   """
 
   def __init__(self, table_data, combine_modes, feature_specs, *, device=0,
-               max_cpu_slots=8, block_size=64):
+               max_cpu_slots=8, block_size=64, placement=None,
+               upload_threads=0, chunk_bytes=0):
     self.device = device
+    self._options = _load_options(placement, upload_threads, chunk_bytes)
     self._handle = ctypes.c_void_p()
     self._dir = tempfile.TemporaryDirectory(prefix="xse_assets_")
     names, paths = [MANIFEST_ASSET_NAME], []
@@ -204,14 +224,17 @@ class CpuEmbeddingResource:
     self._load([MANIFEST_ASSET_NAME] + names[1:], [manifest] + paths)
 
   def _load(self, names, paths):
-    C.check(C.lib.xse_resource_load(_names(names), _names(paths), len(names),
-                                    self.device, ctypes.byref(self._handle)))
+    C.check(C.lib.xse_resource_load_sharded(
+        _names(names), _names(paths), len(names), self.device,
+        ctypes.byref(self._options), ctypes.byref(self._handle)))
 
   @classmethod
-  def from_assets(cls, assets: Dict[str, str], device=0):
+  def from_assets(cls, assets: Dict[str, str], device=0, *, placement=None,
+                  upload_threads=0, chunk_bytes=0):
     """Loads from existing asset files: {asset name: path}."""
     self = cls.__new__(cls)
     self.device = device
+    self._options = _load_options(placement, upload_threads, chunk_bytes)
     self._handle = ctypes.c_void_p()
     self._dir = None
     names = list(assets)
