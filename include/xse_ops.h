@@ -77,10 +77,11 @@ int xse_resource_load(const char* const* asset_names,
  *   XSE_SHARD_ROWWISE   rows [vocab r / world, vocab (r+1) / world) of every
  *                       table (the engine's shard window), read from the
  *                       asset at that offset.
- * Rows are read from the memory-mapped asset into pinned staging buffers of
- * chunk_bytes (0: 64 MiB; < 0: one pageable cudaMemcpy per table) by
- * upload_threads host threads (0: 8), double-buffered so that reading the
- * file overlaps the DMA of the previous chunk. */
+ * Rows are read from the asset file (pread) into pinned staging buffers of
+ * chunk_bytes (0: 32 MiB; < 0: one pageable cudaMemcpy per table from the
+ * memory-mapped asset) by upload_threads host threads (0: 8),
+ * double-buffered so that reading the file overlaps the DMA of the previous
+ * chunk. */
 enum { XSE_SHARD_NONE = 0, XSE_SHARD_TABLEWISE = 1, XSE_SHARD_ROWWISE = 2 };
 typedef struct {
   int32_t world;

@@ -11,7 +11,11 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <unistd.h>
+
 #include <algorithm>
+#include <atomic>
+#include <cerrno>
 #include <cinttypes>
 #include <cstdarg>
 #include <cstdio>
@@ -867,21 +871,42 @@ int xse_engine_profile_read(xse_engine* engine, double* pool_ms,
 
 namespace xse {
 
-// Host -> HBM copy of table rows through pinned staging: chunk k is copied
-// from the (pageable, often memory-mapped) source into pinned buffer k % 2
-// by `threads` host threads while chunk k - 1's DMA runs, so reading the
-// file and PCIe overlap and page faults are taken in parallel. chunk <= 0
-// copies straight from the source (one pageable cudaMemcpy).
+// Host -> HBM copy of table rows through pinned staging: chunk k is filled
+// into pinned buffer k % 2 by `threads` host threads while chunk k - 1's DMA
+// runs, so reading and PCIe overlap. The fill reads the file `fd` at
+// file_offset with pread (no page faults on a mapping) when fd >= 0, else
+// copies from `src` (pageable memory). chunk <= 0 copies straight from
+// `src` (one pageable cudaMemcpy).
 cudaError_t UploadFromHost(void* dst, const void* src, size_t bytes,
-                           int64_t chunk, int threads) {
+                           int64_t chunk, int threads, int fd,
+                           int64_t file_offset) {
   if (bytes == 0) return cudaSuccess;
   if (chunk <= 0) return cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
   cudaPointerAttributes attr{};
-  if (cudaPointerGetAttributes(&attr, src) == cudaSuccess &&
+  if (fd < 0 && cudaPointerGetAttributes(&attr, src) == cudaSuccess &&
       attr.type == cudaMemoryTypeHost) {  // already pinned
     return cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
   }
   (void)cudaGetLastError();
+  std::atomic<bool> read_failed{false};
+  // Fills n bytes at dst from source offset `at`.
+  auto fill = [&](char* to, size_t at, size_t n) {
+    if (fd < 0) {
+      std::memcpy(to, static_cast<const char*>(src) + at, n);
+      return;
+    }
+    while (n > 0) {
+      const ssize_t r = pread(fd, to, n, static_cast<off_t>(file_offset + at));
+      if (r < 0 && errno == EINTR) continue;
+      if (r <= 0) {
+        read_failed = true;
+        return;
+      }
+      to += r;
+      at += static_cast<size_t>(r);
+      n -= static_cast<size_t>(r);
+    }
+  };
   const size_t step = std::min<size_t>(static_cast<size_t>(chunk), bytes);
   if (threads < 1) threads = 1;
   void* pinned[2] = {nullptr, nullptr};
@@ -894,7 +919,6 @@ cudaError_t UploadFromHost(void* dst, const void* src, size_t bytes,
       e = cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming);
     }
   }
-  const char* from = static_cast<const char*>(src);
   char* to = static_cast<char*>(dst);
   for (size_t off = 0, k = 0; off < bytes && e == cudaSuccess;
        off += step, ++k) {
@@ -902,18 +926,23 @@ cudaError_t UploadFromHost(void* dst, const void* src, size_t bytes,
     const int b = static_cast<int>(k & 1);
     if (k >= 2) e = cudaEventSynchronize(done[b]);  // buffer b is free
     if (e != cudaSuccess) break;
-    // Parallel fill of the staging buffer (16-byte aligned slices).
-    const size_t per = (len / threads + 15) / 16 * 16;
+    // Parallel fill of the staging buffer (4 KiB-aligned slices).
+    const size_t per = std::max<size_t>((len / threads + 4095) / 4096 * 4096,
+                                        4096);
+    char* stage = static_cast<char*>(pinned[b]);
     std::vector<std::thread> pool;
     for (int i = 1; i < threads && per * i < len; ++i) {
       pool.emplace_back([&, i]() {
         const size_t lo = per * i, hi = std::min(len, per * (i + 1));
-        std::memcpy(static_cast<char*>(pinned[b]) + lo, from + off + lo,
-                    hi - lo);
+        fill(stage + lo, off + lo, hi - lo);
       });
     }
-    std::memcpy(pinned[b], from + off, std::min(len, per > 0 ? per : len));
+    fill(stage, off, std::min(len, per));
     for (auto& th : pool) th.join();
+    if (read_failed) {
+      e = cudaErrorFileNotFound;
+      break;
+    }
     e = cudaMemcpyAsync(to + off, pinned[b], len, cudaMemcpyHostToDevice,
                         stream);
     if (e == cudaSuccess) e = cudaEventRecord(done[b], stream);
@@ -929,7 +958,8 @@ cudaError_t UploadFromHost(void* dst, const void* src, size_t bytes,
 }
 
 int AddTable(xse_engine* engine, const xse_table_desc* desc,
-             int64_t upload_chunk, int upload_threads) {
+             int64_t upload_chunk, int upload_threads, int fd,
+             int64_t file_offset) {
   if (engine == nullptr || desc == nullptr) {
     return SetError(XSE_INVALID_ARGUMENT, "engine and table must be non-null");
   }
@@ -996,7 +1026,7 @@ int AddTable(xse_engine* engine, const xse_table_desc* desc,
     t->owns_rows = true;
     e = desc->placement == XSE_PLACE_COPY_FROM_HOST
             ? UploadFromHost(t->rows, desc->rows, bytes, upload_chunk,
-                             upload_threads)
+                             upload_threads, fd, file_offset)
             : cudaMemcpy(t->rows, desc->rows, bytes,
                          cudaMemcpyDeviceToDevice);
     if (e != cudaSuccess) return CudaError(e, "table upload");
@@ -1033,7 +1063,7 @@ extern "C" {
 
 int xse_engine_add_table(xse_engine* engine, const xse_table_desc* desc) {
   return xse::AddTable(engine, desc, xse::kDefaultUploadChunk,
-                       xse::kDefaultUploadThreads);
+                       xse::kDefaultUploadThreads, -1, 0);
 }
 
 int xse_engine_register_feature(xse_engine* engine, const char* feature,

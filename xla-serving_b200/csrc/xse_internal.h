@@ -112,12 +112,14 @@ cudaError_t LaunchInterleaveScaleBias(const float* scale, const float* bias,
 // Sets the calling thread's message returned by xse_last_error().
 void SetLastErrorMessage(const char* message);
 
-// Table loading (csrc/xse_capi.cu): xse_engine_add_table with the host
-// upload's staging chunk (<= 0: one pageable copy) and fill threads.
-constexpr int64_t kDefaultUploadChunk = 64ll << 20;
+// Table loading (csrc/xse_capi.cu): the host upload's staging chunk (<= 0:
+// one pageable copy) and fill threads; the fill reads file `fd` at
+// file_offset when fd >= 0, else copies from src.
+constexpr int64_t kDefaultUploadChunk = 32ll << 20;
 constexpr int kDefaultUploadThreads = 8;
 cudaError_t UploadFromHost(void* dst, const void* src, size_t bytes,
-                           int64_t chunk, int threads);
+                           int64_t chunk, int threads, int fd,
+                           int64_t file_offset);
 
 // Fused pooling + dot interaction (PoolInteractKernel, csrc/xse_bag.cu).
 struct InteractArgs {

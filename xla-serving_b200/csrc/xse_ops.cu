@@ -380,15 +380,18 @@ class TextProtoReader {
   size_t pos_ = 0;
 };
 
-// A read-only memory map of an asset file.
+// A read-only memory map of an asset file; the descriptor stays open for
+// pread uploads.
 struct MappedFile {
   void* data = nullptr;
   size_t bytes = 0;
+  int fd = -1;
   ~MappedFile() {
     if (data != nullptr && bytes > 0) munmap(data, bytes);
+    if (fd >= 0) ::close(fd);
   }
   bool Open(const std::string& path, std::string* error) {
-    const int fd = ::open(path.c_str(), O_RDONLY);
+    const int fd = ::open(path.c_str(), O_RDONLY | O_CLOEXEC);
     if (fd < 0) {
       *error = std::string("could not open ") + path + ": " + strerror(errno);
       return false;
@@ -409,7 +412,7 @@ struct MappedFile {
         return false;
       }
     }
-    ::close(fd);
+    this->fd = fd;
     return true;
   }
 };
@@ -428,9 +431,11 @@ bool ReadFile(const std::string& path, std::string* out) {
 }  // namespace
 
 namespace xse {
-// xse_engine_add_table with upload options (csrc/xse_capi.cu).
+// xse_engine_add_table with upload options (csrc/xse_capi.cu); rows read
+// from file `fd` at file_offset when fd >= 0.
 int AddTable(xse_engine* engine, const xse_table_desc* desc,
-             int64_t upload_chunk, int upload_threads);
+             int64_t upload_chunk, int upload_threads, int fd,
+             int64_t file_offset);
 }  // namespace xse
 
 // ---------------------------------------------------------------------------
@@ -558,11 +563,14 @@ int LoadResource(xse_resource* res, const std::string& manifest_path,
                                                  4 * t.vocab_size) +
                   row_begin;
     }
-    code = xse::AddTable(res->engine, &desc,
-                         opt.chunk_bytes == 0 ? xse::kDefaultUploadChunk
-                                              : opt.chunk_bytes,
-                         opt.upload_threads > 0 ? opt.upload_threads
-                                                : xse::kDefaultUploadThreads);
+    code = xse::AddTable(
+        res->engine, &desc,
+        opt.chunk_bytes == 0 ? xse::kDefaultUploadChunk : opt.chunk_bytes,
+        opt.upload_threads > 0 ? opt.upload_threads
+                               : xse::kDefaultUploadThreads,
+        file.fd,
+        static_cast<int64_t>(row_begin) * t.embedding_dim *
+            static_cast<int64_t>(elem));
     if (code != XSE_OK) return FailFromEngine(code);
   }
   for (const ManifestFeature& f : m.features) {

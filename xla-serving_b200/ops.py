@@ -172,8 +172,8 @@ class CpuEmbeddingResource:
     sharding "table" (table i of the manifest on rank i mod world) or "row"
     (rows [vocab r / world, vocab (r+1) / world) of every table).
   upload_threads, chunk_bytes: the host -> HBM upload (pinned staging chunks
-    filled by that many threads; 0 = defaults, chunk_bytes < 0 = one
-    pageable copy per table).
+    filled from the asset file by that many threads; 0 = defaults,
+    chunk_bytes < 0 = one pageable copy per table).
   """
 
   def __init__(self, table_data, combine_modes, feature_specs, *, device=0,
