@@ -765,6 +765,21 @@ class ConfigWorkload:
           self.plan, cfg["batch"], num_tables, dim, self.pooler,
           device="cuda", mode=exchange)
     self.steps = [self.exchange.schedule(f) for f in self.inputs]
+    # Table-wise at N > 1: the same batch arriving data-parallel (every
+    # table's ids for this rank's samples) for the separately timed ids
+    # all-to-all that would feed the owners.
+    self.ids_a2a, self.dp_input = None, None
+    if not rowwise and world > 1:
+      block = self.plan.block_size(cfg["batch"])
+      self.dp_input = []
+      for g in range(num_tables):
+        spec = synth.TableSpec(f"t{g}", vocab, dim, dt, "SUM")
+        fb = synth.synth_batch(spec, 5000 + 97 * rank + g, block,
+                               cfg["lengths"][0], cfg["lengths"][1], SEED,
+                               cfg["alpha"])
+        self.dp_input.append((spec.name, fb.ids, fb.offsets, None))
+      self.ids_a2a = sharding.IdsAllToAll(self.plan, cfg["batch"],
+                                          num_tables, device="cuda")
     torch.cuda.synchronize()
 
   def step(self, i):
@@ -890,6 +905,29 @@ def run_config(args, name):
   base = None
   if world == 1 and not args.no_cpu_baseline:
     base = config_cpu_baseline(wl, args.cpu_seconds)
+  ids_a2a = None
+  if wl.ids_a2a is not None:
+    # Timed on its own: extents, their all-to-all and host read, the pack
+    # launch and the all-to-alls of offsets and ids, every step.
+    for _ in range(3):
+      wl.ids_a2a.run(wl.dp_input)
+    torch.cuda.synchronize()
+    barrier(world, local)
+    a2a_steps = 20
+    start.record(stream)
+    for _ in range(a2a_steps):
+      wl.ids_a2a.run(wl.dp_input)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world, local)
+    a2a_ms = max_over_ranks(start.elapsed_time(end), world) / a2a_steps
+    dp_ids = sum(int(f[1].numel()) for f in wl.dp_input)
+    ids_a2a = {"ms_per_step": a2a_ms, "steps": a2a_steps,
+               "ids_per_rank": dp_ids,
+               "bytes_sent_per_rank": wl.ids_a2a.bytes_last,
+               "note": "data-parallel input (every table's ids for this "
+                       "rank's samples) moved to the table owners; timed "
+                       "apart from the pooling"}
   if rank == 0:
     line = {
         "metric": "embedding-bag ids/sec", "value": ids / (ms / 1000.0),
@@ -927,6 +965,8 @@ def run_config(args, name):
         "cpu_baseline": base,
         "clocks": clock_info,
     }
+    if ids_a2a is not None:
+      line["ids_all_to_all"] = ids_a2a
     print(json.dumps(line), flush=True)
   wl.close()
   if world > 1:
