@@ -1059,6 +1059,9 @@ def main():
   ap.add_argument("--warmup", type=int, default=50)
   ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
   ap.add_argument("--e2e-steps", type=int, default=200)
+  ap.add_argument("--e2e-threads", type=int, default=E2E_THREADS,
+                  help="concurrent host callers of the operator in the e2e "
+                       "run")
   ap.add_argument("--cpu-seconds", type=float, default=10.0)
   ap.add_argument("--no-cpu-baseline", action="store_true")
   ap.add_argument("--exchange", default="peer",
@@ -1132,11 +1135,11 @@ def main():
   pool_ms, pool_n = wl.engine.profile_read()
   wl.engine.set_profiling(False)
 
-  # End to end through the operator with host buffers, E2E_THREADS
+  # End to end through the operator with host buffers, args.e2e_threads
   # concurrent callers.
-  host.run(3 * E2E_THREADS, E2E_THREADS)
+  host.run(3 * args.e2e_threads, args.e2e_threads)
   barrier(world, local)
-  e2e_ms = max_over_ranks(host.run(args.e2e_steps, E2E_THREADS), world)
+  e2e_ms = max_over_ranks(host.run(args.e2e_steps, args.e2e_threads), world)
   barrier(world, local)
   dlrm_result = None
   if args.dlrm_steps > 0:
@@ -1218,7 +1221,7 @@ def main():
             "path": "CpuEmbeddingLookupTransform (xse_lookup_transform_run, "
                     "C ABI) over 8 features with pinned host inputs; H2D, "
                     "validation, pooling and D2H of the outputs inside each "
-                    f"synchronous call; {E2E_THREADS} host threads issue "
+                    f"synchronous call; {args.e2e_threads} host threads issue "
                     "calls concurrently (one stream each)",
         },
         "gpu_launches": launches,
