@@ -253,7 +253,7 @@ class Workload:
       reqs.append(self.xse.BagRequest(spec.name, fb.ids, fb.offsets,
                                       pooled[:, k, :], fb.weights,
                                       output_stride=NUM_TABLES * DIM))
-    return reqs
+    return self.xse.PreparedBatch(reqs)
 
   def step(self, i):
     v = i % ROTATE

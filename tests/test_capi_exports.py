@@ -46,3 +46,25 @@ def test_abi_version_and_error_channel(xse):
   rc = xse._capi.lib.xse_status_create(0, ctypes.byref(handle))
   assert rc == xse._capi.INVALID_ARGUMENT
   assert "max_requests" in xse._capi.last_error()
+
+
+def test_prepared_batch_holds_the_same_request_array(xse):
+  """PreparedBatch converts its requests once; the array it hands the C ABI
+  equals a fresh per-call conversion, and it still reads as the list."""
+  import torch  # pylint: disable=import-outside-toplevel
+  ids = torch.arange(10, dtype=torch.int64)
+  offsets = torch.tensor([0, 4, 10], dtype=torch.int32)
+  weights = torch.ones(10)
+  out = torch.zeros(2, 3, 8)
+  reqs = [xse.BagRequest(f"f{k}", ids, offsets, out[:, k, :],
+                         weights if k == 1 else None, output_stride=24)
+          for k in range(3)]
+  prepared = xse.PreparedBatch(reqs)
+  assert list(prepared) == reqs
+  fresh, _ = xse.EmbeddingEngine._c_requests(reqs)  # pylint: disable=protected-access
+  fields = [f for f, _ in xse._capi.BagRequest._fields_]  # pylint: disable=protected-access
+  for k in range(3):
+    for f in fields:
+      assert getattr(prepared.array[k], f) == getattr(fresh[k], f), (k, f)
+  assert prepared.array[2].output == out[:, 2, :].data_ptr()
+  assert prepared.array[1].num_weights == 10 and prepared.array[0].weights is None

@@ -12,10 +12,10 @@ from . import dlrm
 from . import ops
 from . import sharding
 from ._capi import XseError
-from .engine import (BagRequest, EmbeddingEngine, Status, dot_interaction,
-                     last_launch_count, stream_handle)
+from .engine import (BagRequest, EmbeddingEngine, PreparedBatch, Status,
+                     dot_interaction, last_launch_count, stream_handle)
 
 __all__ = [
-    "BagRequest", "EmbeddingEngine", "Status", "XseError", "dot_interaction",
-    "last_launch_count", "stream_handle",
+    "BagRequest", "EmbeddingEngine", "PreparedBatch", "Status", "XseError",
+    "dot_interaction", "last_launch_count", "stream_handle",
 ]

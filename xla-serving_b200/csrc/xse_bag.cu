@@ -32,7 +32,6 @@
 
 #include <cuda_runtime.h>
 
-#include <algorithm>
 #include <utility>
 #include <stdint.h>
 
@@ -77,6 +76,9 @@ struct ElemsPerVec<2> {
 #ifndef XSE_POOL_I8_ROWS
 #define XSE_POOL_I8_ROWS 2
 #endif
+#ifndef XSE_POOL_I8_MIN_BLOCKS
+#define XSE_POOL_I8_MIN_BLOCKS 3
+#endif
 
 // 1: validation and pooling kernels use programmatic dependent launch.
 #ifndef XSE_PDL
@@ -95,7 +97,7 @@ template <int DT, int V>
 struct MinBlocks {
   static constexpr int value =
       ElemsPerVec<DT>::value * V <= 16 && RowsInFlight<DT, V>::value * V <= 8
-          ? XSE_POOL_MIN_BLOCKS
+          ? (DT == 2 ? XSE_POOL_I8_MIN_BLOCKS : XSE_POOL_MIN_BLOCKS)
           : 2;
 };
 
@@ -136,23 +138,33 @@ __device__ __forceinline__ int64_t LoadIndex(const void* base, int is64,
               : static_cast<int64_t>(__ldg(static_cast<const int*>(base) + i));
 }
 
-// Read-only 16-byte row load. XSE_POOL_L1 selects its L1 policy: 0 does not
-// allocate in L1 (reuse of rows comes from L2 only), 1 caches in L1 (hot
+// Read-only 16-byte row load. L1 selects its L1 policy: false does not
+// allocate in L1 (reuse of rows comes from L2 only), true caches in L1 (hot
 // rows of skewed id streams are then served by the SM that reads them).
+// XSE_POOL_L1 is the policy of the pooling kernel (which uses no shared
+// memory, so L1 has the SM's whole data cache): caching took the Zipf(1.1)
+// table-wise slice from 1.226 to 1.137 ms per step and the uniform
+// multi-table step from 71.6 to 70.7 us. XSE_INTERACT_L1 is the fused
+// interaction kernel's: its shared-memory slots leave L1 small, and caching
+// cost it 1.5 %.
 #ifndef XSE_POOL_L1
-#define XSE_POOL_L1 0
+#define XSE_POOL_L1 1
 #endif
+#ifndef XSE_INTERACT_L1
+#define XSE_INTERACT_L1 0
+#endif
+template <bool L1>
 __device__ __forceinline__ uint4 LoadRowVec(const uint4* p) {
   uint4 r;
-#if XSE_POOL_L1 == 1
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-#else
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-#endif
+  if constexpr (L1) {
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+  } else {
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+  }
   return r;
 }
 
@@ -323,7 +335,8 @@ __device__ __forceinline__ void AddGathered(
 // Full batch of U rows of a chunk whose ids all contribute: no per-row
 // checks. Lanes past the end of a non-exact row add zeros to accumulator
 // lanes that are never stored.
-template <int DT, int G, int V, bool EXACT, int WM, int U, typename Hook>
+template <int DT, int G, int V, bool EXACT, int WM, int U, bool L1,
+          typename Hook>
 __device__ __forceinline__ void FullBatch(
     const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
     int my_row, float my_w, int j0, int cnt,
@@ -339,7 +352,7 @@ __device__ __forceinline__ void FullBatch(
 #pragma unroll
     for (int v = 0; v < V; ++v) {
       if (EXACT || gl + v * G < row_vecs) {
-        raw[u][v] = LoadRowVec(src + v * G);
+        raw[u][v] = LoadRowVec<L1>(src + v * G);
       } else {
         raw[u][v] = make_uint4(0, 0, 0, 0);
       }
@@ -376,7 +389,8 @@ __device__ __forceinline__ void FullBatch(
 
 // General batch: up to U rows (positions j0..j0+n-1 of the chunk), skipping
 // ids that contribute nothing.
-template <int DT, int G, int V, bool EXACT, int WM, int U, typename Hook>
+template <int DT, int G, int V, bool EXACT, int WM, int U, bool L1,
+          typename Hook>
 __device__ __forceinline__ void GatherBatch(
     const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
     int my_row, float my_w, int j0, int n,
@@ -399,7 +413,7 @@ __device__ __forceinline__ void GatherBatch(
     for (int v = 0; v < V; ++v) {
       if (use) {
         if (EXACT || gl + v * G < row_vecs) {
-          raw[u][v] = LoadRowVec(src + v * G);
+          raw[u][v] = LoadRowVec<L1>(src + v * G);
         } else {
           raw[u][v] = make_uint4(0, 0, 0, 0);
         }
@@ -423,9 +437,28 @@ __device__ __forceinline__ void GatherBatch(
   }
 }
 
+// 1: lanes holding 8 or 16 output floats store them with 32-byte stores.
+#ifndef XSE_POOL_WIDE_STORES
+#define XSE_POOL_WIDE_STORES 1
+#endif
+
+// One 32-byte store (sm_100 256-bit st.global): a lane's 8 output floats in
+// one instruction, so a lane group writes its whole output row at once
+// instead of two half-filled passes over the row's 32-byte sectors (which
+// matters most when the row is a peer's memory, reached over NVLink).
+__device__ __forceinline__ void Store32B(float* p, u64 a, u64 b, u64 c,
+                                         u64 d) {
+  asm volatile("st.global.v4.b64 [%0], {%1,%2,%3,%4};" ::"l"(p), "l"(a),
+               "l"(b), "l"(c), "l"(d)
+               : "memory");
+}
+
 // Scales (mean / sqrt-n) and stores one finished bag, then clears the
-// accumulator for the next one.
-template <int DT, int G, int V, bool EXACT>
+// accumulator for the next one. GLOBAL_OUT: `out` is global memory (this
+// device's or a peer's), so 32-byte st.global stores may be used; the fused
+// interaction kernel passes rows in shared memory and sets it false (a
+// st.global to a shared address faults).
+template <int DT, int G, int V, bool EXACT, bool GLOBAL_OUT>
 __device__ __forceinline__ void FinishBag(
     const BagDesc& d, float* out, bool vec_out, int64_t n, bool weighted,
     u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, int gl,
@@ -439,12 +472,22 @@ __device__ __forceinline__ void FinishBag(
 #pragma unroll
       for (int k = 0; k < PPV; ++k) acc[v][k] = Mul2(acc[v][k], s2);
   }
+  // Lanes holding 8 or 16 floats store 32-byte pieces when the row is
+  // 32-byte aligned (each lane's part then is too).
+  const bool wide = XSE_POOL_WIDE_STORES && GLOBAL_OUT && PPV % 4 == 0 &&
+                    vec_out && (reinterpret_cast<uintptr_t>(out) & 31u) == 0;
 #pragma unroll
   for (int v = 0; v < V; ++v) {
     const int k = gl + v * G;
     if (EXACT || k < row_vecs) {
       float* o = out + k * (2 * PPV);
-      if (vec_out) {
+      if (wide) {
+#pragma unroll
+        for (int e = 0; e + 3 < PPV; e += 4) {
+          Store32B(o + 2 * e, acc[v][e], acc[v][e + 1], acc[v][e + 2],
+                   acc[v][e + 3]);
+        }
+      } else if (vec_out) {
 #pragma unroll
         for (int e = 0; e < PPV; e += 2) {
           *reinterpret_cast<ulonglong2*>(o + 2 * e) =
@@ -521,6 +564,7 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
   constexpr int PPV = ElemsPerVec<DT>::value / 2;
   constexpr int U = UR == 0 ? RowsInFlight<DT, V>::value : UR;
   constexpr int kGroupsPerBlock = kThreads / G;
+  constexpr bool kL1 = XSE_POOL_L1 != 0;
 
   const int lane = threadIdx.x & 31;
   const int gl = lane % G;
@@ -589,21 +633,22 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
         int j0 = 0;
         if (__all_sync(gmask, gl >= cnt || my_row >= 0)) {
           for (; j0 + U <= cnt; j0 += U) {
-            FullBatch<DT, G, V, EXACT, WM, U>(d, rows, row_vecs, gl, gmask,
-                                           my_row, my_w, j0, cnt, acc, &wsum,
-                                           prefetch);
+            FullBatch<DT, G, V, EXACT, WM, U, kL1>(
+                d, rows, row_vecs, gl, gmask, my_row, my_w, j0, cnt, acc,
+                &wsum, prefetch);
           }
         }
         for (; j0 < cnt; j0 += U) {
           const int n = cnt - j0 < U ? cnt - j0 : U;
-          GatherBatch<DT, G, V, EXACT, WM, U>(d, rows, row_vecs, gl, gmask,
-                                           my_row, my_w, j0, n, acc, &wsum,
-                                           prefetch);
+          GatherBatch<DT, G, V, EXACT, WM, U, kL1>(
+              d, rows, row_vecs, gl, gmask, my_row, my_w, j0, n, acc, &wsum,
+              prefetch);
         }
       }
-      FinishBag<DT, G, V, EXACT>(d, d.out + bag * d.out_stride, d.vec_out,
-                                 end - begin, WM != kUnweighted, acc, &wsum,
-                                 gl, row_vecs);
+      FinishBag<DT, G, V, EXACT, true>(d, d.out + bag * d.out_stride,
+                                       d.vec_out, end - begin,
+                                       WM != kUnweighted, acc, &wsum, gl,
+                                       row_vecs);
     }
     if (!has_next) break;
     task = ntask;
@@ -780,6 +825,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
   constexpr int U = RowsInFlight<DT, V>::value;
   constexpr int D = G * ElemsPerVec<DT>::value;
   constexpr int kNs = kInteractSlots;
+  constexpr bool kL1 = XSE_INTERACT_L1 != 0;
   EnterDependent();
   if (!p.fused_checks && p.status->group_error != 0) return;
   extern __shared__ float4 smem_vec[];
@@ -915,16 +961,16 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
         int j0 = 0;
         if (__all_sync(gmask, gl >= cnt || my_row >= 0)) {
           for (; j0 + U <= cnt; j0 += U) {
-            FullBatch<DT, G, V, EXACT, WM, U>(d, rows, row_vecs, gl, gmask,
-                                           my_row, my_w, j0, cnt, acc, &wsum,
-                                           prefetch);
+            FullBatch<DT, G, V, EXACT, WM, U, kL1>(
+                d, rows, row_vecs, gl, gmask, my_row, my_w, j0, cnt, acc,
+                &wsum, prefetch);
           }
         }
         for (; j0 < cnt; j0 += U) {
           const int n = cnt - j0 < U ? cnt - j0 : U;
-          GatherBatch<DT, G, V, EXACT, WM, U>(d, rows, row_vecs, gl, gmask,
-                                           my_row, my_w, j0, n, acc, &wsum,
-                                           prefetch);
+          GatherBatch<DT, G, V, EXACT, WM, U, kL1>(
+              d, rows, row_vecs, gl, gmask, my_row, my_w, j0, n, acc, &wsum,
+              prefetch);
         }
       }
     }
@@ -935,8 +981,9 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
       return;
     }
     if (ok) {
-      FinishBag<DT, G, V, EXACT>(d, zs + (1 + t) * RS, true, end - begin,
-                                 WM != kUnweighted, acc, &wsum, gl, G * V);
+      FinishBag<DT, G, V, EXACT, false>(d, zs + (1 + t) * RS, true,
+                                        end - begin, WM != kUnweighted, acc,
+                                        &wsum, gl, G * V);
     }
     __syncwarp();
     __threadfence_block();
@@ -1222,10 +1269,20 @@ void SplitModes(PoolParams* p, int64_t max_grid, int groups_per_block) {
 template <int DT, int G, int V, bool EXACT>
 cudaError_t LaunchVec(const PoolParams& in, cudaStream_t stream) {
   PoolParams p = in;
-  // Descriptors by weighting mode (stable: request order within a mode).
-  std::stable_sort(p.d, p.d + p.n, [](const BagDesc& a, const BagDesc& b) {
-    return WeightModeOf(a) < WeightModeOf(b);
-  });
+  // Descriptors by weighting mode (stable: request order within a mode). An
+  // in-place insertion sort over at most kMaxDescsPerLaunch entries: unlike
+  // std::stable_sort it never takes a heap buffer, so launches stay
+  // allocation-free.
+  for (int k = 1; k < p.n; ++k) {
+    const BagDesc moving = p.d[k];
+    const int mode = WeightModeOf(moving);
+    int j = k;
+    while (j > 0 && WeightModeOf(p.d[j - 1]) > mode) {
+      p.d[j] = p.d[j - 1];
+      --j;
+    }
+    p.d[j] = moving;
+  }
   AssignTasks(&p, 1);
   auto kernel = PoolVecKernel<DT, G, V, EXACT, 0>;
   int64_t max_grid = static_cast<int64_t>(SmCount()) * BlocksPerSm(kernel);

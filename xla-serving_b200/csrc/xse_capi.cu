@@ -366,16 +366,45 @@ int CheckIsolation(const xse_bag_request* reqs,
       }
     }
   }
+  // Inputs sorted by start, with the running maximum of their ends: an
+  // output is tested only against inputs that start before its end, walking
+  // down while some input at or below the position still reaches past the
+  // output's start. Of the inputs an output meets, the first in request
+  // order is reported, as a scan of the inputs in request order would.
+  // (A sharded step holds 8 tables x W destinations of requests; the plain
+  // outputs x inputs scan took about 50 us at W = 8.)
+  std::vector<int32_t> order(inputs.size());
+  for (size_t i = 0; i < order.size(); ++i) order[i] = static_cast<int32_t>(i);
+  std::sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
+    return inputs[a].base < inputs[b].base;
+  });
+  std::vector<int64_t> reach(order.size());
+  int64_t far = INT64_MIN;
+  for (size_t k = 0; k < order.size(); ++k) {
+    far = std::max(far, inputs[order[k]].end());
+    reach[k] = far;
+  }
   for (const Range& o : outputs) {
-    for (const Range& in : inputs) {
-      if (Overlaps(o, in)) {
-        snprintf(buf, sizeof(buf),
-                 "FP32 embedding-bag request %d output overlaps request %d %s "
-                 "storage.",
-                 o.request, in.request, in.kind);
-        *message = buf;
-        return XSE_INVALID_ARGUMENT;
-      }
+    const int64_t o_end = o.end();
+    const size_t hi =
+        std::lower_bound(order.begin(), order.end(), o_end,
+                         [&](int32_t idx, int64_t v) {
+                           return inputs[idx].base < v;
+                         }) -
+        order.begin();
+    int32_t hit = -1;
+    for (size_t k = hi; k-- > 0 && reach[k] > o.base;) {
+      const int32_t idx = order[k];
+      if ((hit < 0 || idx < hit) && Overlaps(o, inputs[idx])) hit = idx;
+    }
+    if (hit >= 0) {
+      const Range& in = inputs[hit];
+      snprintf(buf, sizeof(buf),
+               "FP32 embedding-bag request %d output overlaps request %d %s "
+               "storage.",
+               o.request, in.request, in.kind);
+      *message = buf;
+      return XSE_INVALID_ARGUMENT;
     }
   }
   return XSE_OK;

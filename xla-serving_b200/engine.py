@@ -66,6 +66,23 @@ class BagRequest:
   output_stride: int = 0  # floats between bags; 0 = dim
 
 
+class PreparedBatch(list):
+  """A group of BagRequests converted to the C request array once.
+
+  A list of the requests (it keeps their tensors alive) that also holds
+  their xse_bag_request array, so a group that runs every step -- the
+  per-destination groups of a sharded exchange, a serving loop's fixed
+  inputs -- skips the per-call conversion (about 3 us per request in
+  Python, which at 8 tables x 8 destinations outlasts the kernels it
+  launches). The tensors' storage must not change while it is in use; a
+  changed list must be prepared again.
+  """
+
+  def __init__(self, requests: Sequence[BagRequest]):
+    super().__init__(requests)
+    self.array, self._names = EmbeddingEngine._c_requests(self)
+
+
 class Status:
   """Caller-owned device status block for asynchronous execution."""
 
@@ -241,7 +258,10 @@ class EmbeddingEngine:
     `status` it returns right after the launches and the result is read with
     status.wait().
     """
-    arr, names = self._c_requests(requests)
+    if isinstance(requests, PreparedBatch):
+      arr, names = requests.array, None
+    else:
+      arr, names = self._c_requests(requests)
     flags = C.EXEC_FUSED if fused else C.EXEC_STRICT
     if status is not None:
       flags |= C.EXEC_ASYNC

@@ -46,7 +46,8 @@ import torch
 import torch.distributed as dist
 
 from . import _capi as C
-from .engine import BagRequest, last_launch_count, stream_handle
+from .engine import (BagRequest, PreparedBatch, last_launch_count,
+                     stream_handle)
 
 
 @dataclasses.dataclass(frozen=True)
@@ -470,7 +471,13 @@ class TablewiseExchange:
     a2a: [(None, requests writing send)] (send [W][B/W][T_local][D] is
     [B][T_local][D] in sample order). pipelined: [(dest, requests)] for
     rank+1, rank+2, ..., then the own block pooled straight into recv.
-    peer: one group per receive slot, each writing every rank's slot."""
+    peer: one group per receive slot, each writing every rank's slot.
+    Each group is a PreparedBatch (converted to the C request array once).
+    """
+    return [(key, PreparedBatch(reqs))
+            for key, reqs in self._groups(features, blocks)]
+
+  def _groups(self, features, blocks):
     w, r = self.plan.world, self.plan.rank
     local = features if blocks is None else blocks[r]
     if len(local) != self.num_local or (blocks is not None and
@@ -633,7 +640,9 @@ class RowwiseExchange:
     return reqs
 
   def schedule(self, features) -> List[List[BagRequest]]:
-    return [self.chunk_requests(features, c) for c in range(self.chunks)]
+    """One PreparedBatch of requests per chunk, reused by run()."""
+    return [PreparedBatch(self.chunk_requests(features, c))
+            for c in range(self.chunks)]
 
   def run(self, steps):
     works = []
