@@ -67,10 +67,22 @@ struct ElemsPerVec<2> {
 #ifndef XSE_POOL_MIN_BLOCKS
 #define XSE_POOL_MIN_BLOCKS 3
 #endif
-// Rows of the next batch of a chunk prefetched into L2 while the current
-// batch is in flight.
+// Row prefetch. Chunk prefetch (XSE_POOL_CHUNK_PREFETCH, fp32/bf16 rows in
+// the throughput pooling kernel): when a chunk's ids are staged, each lane
+// prefetches the whole row of its id into L1 (the kernel's row loads
+// allocate in L1), so all of a chunk's rows are requested at once and the
+// batches that gather them find them on chip or already in flight. Batch
+// prefetch (XSE_POOL_PREFETCH, everywhere else): the rows of a chunk's next
+// batch go to L2 while the current batch is in flight. Measured on one B200
+// against batch prefetch: Zipf(1.1) table-wise slice 1.22-1.30 -> 1.04-1.07
+// ms per step, multi-table 70.6 -> 69.7 us; int8 rows (3.06 -> 3.51 ms) and
+// the deep small-launch variant were slower with it, so they keep batch
+// prefetch; both kinds at once was slower than either.
 #ifndef XSE_POOL_PREFETCH
 #define XSE_POOL_PREFETCH 1
+#endif
+#ifndef XSE_POOL_CHUNK_PREFETCH
+#define XSE_POOL_CHUNK_PREFETCH 1
 #endif
 
 #ifndef XSE_POOL_I8_ROWS
@@ -153,6 +165,11 @@ __device__ __forceinline__ int64_t LoadIndex(const void* base, int is64,
 #ifndef XSE_INTERACT_L1
 #define XSE_INTERACT_L1 0
 #endif
+// Chunk prefetch in the fused interaction kernel: 0 off (batch prefetch),
+// 1 into L2, 2 into L1.
+#ifndef XSE_INTERACT_CHUNK_PREFETCH
+#define XSE_INTERACT_CHUNK_PREFETCH 0
+#endif
 template <bool L1>
 __device__ __forceinline__ uint4 LoadRowVec(const uint4* p) {
   uint4 r;
@@ -170,6 +187,22 @@ __device__ __forceinline__ uint4 LoadRowVec(const uint4* p) {
 
 __device__ __forceinline__ void PrefetchRowVec(const uint4* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// Prefetches the 128-byte lines of one row of `bytes` bytes at `row` (every
+// line holds a byte of the row, so every address is mapped).
+template <bool L1>
+__device__ __forceinline__ void PrefetchRow(const void* row, int bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(row);
+  const int lines = static_cast<int>(((a & 127u) + bytes + 127) >> 7);
+  const char* line = reinterpret_cast<const char*>(a & ~uintptr_t{127});
+  for (int k = 0; k < lines; ++k) {
+    if constexpr (L1) {
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(line + 128 * k));
+    } else {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(line + 128 * k));
+    }
+  }
 }
 
 // Products are scalar mul.rn.f32, which PTX never contracts into an FMA; a
@@ -334,8 +367,9 @@ __device__ __forceinline__ void AddGathered(
 
 // Full batch of U rows of a chunk whose ids all contribute: no per-row
 // checks. Lanes past the end of a non-exact row add zeros to accumulator
-// lanes that are never stored.
-template <int DT, int G, int V, bool EXACT, int WM, int U, bool L1,
+// lanes that are never stored. PF: prefetch the chunk's next batch of rows
+// into L2 while this one is in flight.
+template <int DT, int G, int V, bool EXACT, int WM, int U, bool L1, bool PF,
           typename Hook>
 __device__ __forceinline__ void FullBatch(
     const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
@@ -358,22 +392,22 @@ __device__ __forceinline__ void FullBatch(
       }
     }
   }
-#if XSE_POOL_PREFETCH
+  if constexpr (PF) {
 #pragma unroll
-  for (int u = 0; u < U; ++u) {
-    const int j = j0 + U + u;
-    if (j < cnt) {
-      const int r = __shfl_sync(gmask, my_row, j, G);
-      const uint4* src = rows + static_cast<int64_t>(r) * stride;
+    for (int u = 0; u < U; ++u) {
+      const int j = j0 + U + u;
+      if (j < cnt) {
+        const int r = __shfl_sync(gmask, my_row, j, G);
+        const uint4* src = rows + static_cast<int64_t>(r) * stride;
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        if (EXACT || gl + v * G < row_vecs) PrefetchRowVec(src + v * G);
+        for (int v = 0; v < V; ++v) {
+          if (EXACT || gl + v * G < row_vecs) PrefetchRowVec(src + v * G);
+        }
       }
     }
+  } else {
+    (void)cnt;
   }
-#else
-  (void)cnt;
-#endif
   hook();  // runs while this batch's rows are in flight
 #pragma unroll
   for (int u = 0; u < U; ++u) {
@@ -565,6 +599,9 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
   constexpr int U = UR == 0 ? RowsInFlight<DT, V>::value : UR;
   constexpr int kGroupsPerBlock = kThreads / G;
   constexpr bool kL1 = XSE_POOL_L1 != 0;
+  constexpr bool kChunkPrefetch =
+      XSE_POOL_CHUNK_PREFETCH != 0 && DT != 2 && UR == 0;
+  constexpr bool kBatchPrefetch = XSE_POOL_PREFETCH != 0 && !kChunkPrefetch;
 
   const int lane = threadIdx.x & 31;
   const int gl = lane % G;
@@ -630,10 +667,18 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
           }
         };
         const int my_row = StageRow(p, d, id, base + gl, gl < cnt);
+        if constexpr (kChunkPrefetch) {
+          if (my_row >= 0) {
+            const int row_bytes = row_vecs * 16;
+            PrefetchRow<kL1>(static_cast<const char*>(d.rows) +
+                                 static_cast<int64_t>(my_row) * row_bytes,
+                             row_bytes);
+          }
+        }
         int j0 = 0;
         if (__all_sync(gmask, gl >= cnt || my_row >= 0)) {
           for (; j0 + U <= cnt; j0 += U) {
-            FullBatch<DT, G, V, EXACT, WM, U, kL1>(
+            FullBatch<DT, G, V, EXACT, WM, U, kL1, kBatchPrefetch>(
                 d, rows, row_vecs, gl, gmask, my_row, my_w, j0, cnt, acc,
                 &wsum, prefetch);
           }
@@ -826,6 +871,8 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
   constexpr int D = G * ElemsPerVec<DT>::value;
   constexpr int kNs = kInteractSlots;
   constexpr bool kL1 = XSE_INTERACT_L1 != 0;
+  constexpr bool kChunkPrefetch = XSE_INTERACT_CHUNK_PREFETCH != 0;
+  constexpr bool kBatchPrefetch = XSE_POOL_PREFETCH != 0 && !kChunkPrefetch;
   EnterDependent();
   if (!p.fused_checks && p.status->group_error != 0) return;
   extern __shared__ float4 smem_vec[];
@@ -958,10 +1005,18 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
           }
         };
         const int my_row = StageRow(p, d, id, base + gl, gl < cnt);
+        if constexpr (kChunkPrefetch) {
+          if (my_row >= 0) {
+            PrefetchRow<XSE_INTERACT_CHUNK_PREFETCH == 2>(
+                static_cast<const char*>(d.rows) +
+                    static_cast<int64_t>(my_row) * (row_vecs * 16),
+                row_vecs * 16);
+          }
+        }
         int j0 = 0;
         if (__all_sync(gmask, gl >= cnt || my_row >= 0)) {
           for (; j0 + U <= cnt; j0 += U) {
-            FullBatch<DT, G, V, EXACT, WM, U, kL1>(
+            FullBatch<DT, G, V, EXACT, WM, U, kL1, kBatchPrefetch>(
                 d, rows, row_vecs, gl, gmask, my_row, my_w, j0, cnt, acc,
                 &wsum, prefetch);
           }
