@@ -84,6 +84,11 @@ struct ElemsPerVec<2> {
 #ifndef XSE_POOL_CHUNK_PREFETCH
 #define XSE_POOL_CHUNK_PREFETCH 1
 #endif
+// Chunk prefetch of int8 rows: 0 off (next-batch L2 prefetch), 1 into L2,
+// 2 into L1.
+#ifndef XSE_POOL_I8_CHUNK_PREFETCH
+#define XSE_POOL_I8_CHUNK_PREFETCH 0
+#endif
 
 #ifndef XSE_POOL_I8_ROWS
 #define XSE_POOL_I8_ROWS 2
@@ -599,8 +604,11 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
   constexpr int U = UR == 0 ? RowsInFlight<DT, V>::value : UR;
   constexpr int kGroupsPerBlock = kThreads / G;
   constexpr bool kL1 = XSE_POOL_L1 != 0;
-  constexpr bool kChunkPrefetch =
-      XSE_POOL_CHUNK_PREFETCH != 0 && DT != 2 && UR == 0;
+  constexpr int kChunkPrefetchTo =  // 0 none, 1 L2, 2 L1
+      UR != 0 ? 0
+      : DT == 2 ? XSE_POOL_I8_CHUNK_PREFETCH
+                : (XSE_POOL_CHUNK_PREFETCH != 0 ? (kL1 ? 2 : 1) : 0);
+  constexpr bool kChunkPrefetch = kChunkPrefetchTo != 0;
   constexpr bool kBatchPrefetch = XSE_POOL_PREFETCH != 0 && !kChunkPrefetch;
 
   const int lane = threadIdx.x & 31;
@@ -670,9 +678,10 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
         if constexpr (kChunkPrefetch) {
           if (my_row >= 0) {
             const int row_bytes = row_vecs * 16;
-            PrefetchRow<kL1>(static_cast<const char*>(d.rows) +
-                                 static_cast<int64_t>(my_row) * row_bytes,
-                             row_bytes);
+            PrefetchRow<kChunkPrefetchTo == 2>(
+                static_cast<const char*>(d.rows) +
+                    static_cast<int64_t>(my_row) * row_bytes,
+                row_bytes);
           }
         }
         int j0 = 0;
