@@ -57,7 +57,7 @@ E2E_THREADS = 2  # concurrent host callers of the operator in the e2e run
 PROFILE_PERIOD = 8
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one step's
 # pooling kernels, from an ncu capture of this workload on a B200.
-POOL_DRAM_BYTES_PER_STEP = 311.03e6
+POOL_DRAM_BYTES_PER_STEP = 330.32e6
 ROW_BYTES = DIM * 2
 WORKLOAD = ("multi_table_bf16: 8 bf16 tables x 500,000 x 128 per GPU, batch "
             "8192, 20 ids per bag, uniform ids, tables 0-3 per-id weighted "

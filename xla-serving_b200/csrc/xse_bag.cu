@@ -1292,11 +1292,15 @@ void AssignTasks(PoolParams* p, int runs) {
   p->total_tasks = tasks;
 }
 
-// Rows in flight of the latency-bound variant (twice the throughput
-// setting; register-limited to 2 resident blocks per SM).
+// Rows in flight of the latency-bound variant (register-limited to 2
+// resident blocks per SM): up to XSE_POOL_DEEP_ROWS, at most one id chunk.
+#ifndef XSE_POOL_DEEP_ROWS
+#define XSE_POOL_DEEP_ROWS 8
+#endif
 template <int DT, int G, int V>
 constexpr int DeepRows() {
-  return (DT == 2 || V != 1) ? 0 : (G < 8 ? G : 8);
+  return (DT == 2 || V != 1) ? 0
+                             : (G < XSE_POOL_DEEP_ROWS ? G : XSE_POOL_DEEP_ROWS);
 }
 
 // Splits `grid` blocks over the weighting modes in proportion to their tasks
