@@ -435,3 +435,33 @@ def test_profiling_period(xse):
     C = xse._capi
     C.check(C.lib.xse_engine_set_profiling(eng._handle, -1))
   eng.close()
+
+
+@pytest.mark.parametrize("dtype,dim", [(oracle.BF16, 128), (oracle.I8_ROWWISE,
+                                                            256),
+                                       (oracle.BF16, 64)])
+@pytest.mark.parametrize("shift", [0, 4, 1])
+def test_output_alignment_variants(xse, dtype, dim, shift):
+  """Lanes store 32-byte pieces only where the output row is 32-byte
+  aligned: rows shifted by 4 floats (16-byte aligned) take 16-byte stores,
+  rows shifted by 1 float scalar stores. All three match the oracle bit for
+  bit and leave the floats around every row untouched."""
+  rng = np.random.default_rng(100 + dim + shift)
+  eng = xse.EmbeddingEngine(0)
+  vocab, batch = 900, 131
+  host, dev, s, b = random_table(rng, dtype, vocab, dim)
+  eng.add_table("t", dev, "MEAN", scale=s, bias=b)
+  eng.register_feature("f", "t")
+  ids, offsets = random_csr(rng, vocab, batch, 37)
+  w = rng.uniform(0, 1, len(ids)).astype(np.float32)
+  stride = dim + 8 + (shift % 4)  # keeps every row at the same alignment
+  buf = torch.full((batch * stride + 16,), -3.0, device="cuda")
+  out = buf[shift:shift + batch * stride].view(batch, stride)[:, :dim]
+  eng.execute_batch([xse.BagRequest("f", to_dev(ids), to_dev(offsets), out,
+                                    to_dev(w), output_stride=stride)])
+  want = oracle_pool(host, dtype, ids, offsets, w, "MEAN", s, b)
+  assert_bitwise(out.cpu().numpy(), want, f"shift {shift}")
+  rest = buf.clone()
+  rest[shift:shift + batch * stride].view(batch, stride)[:, :dim] = -3.0
+  assert torch.all(rest == -3.0)
+  eng.close()
