@@ -97,6 +97,11 @@ struct ElemsPerVec<2> {
 #define XSE_POOL_I8_MIN_BLOCKS 3
 #endif
 
+// 1: launches small enough for one wave of PoolStagedKernel use it.
+#ifndef XSE_POOL_STAGED
+#define XSE_POOL_STAGED 1
+#endif
+
 // 1: validation and pooling kernels use programmatic dependent launch.
 #ifndef XSE_PDL
 #define XSE_PDL 1
@@ -749,6 +754,153 @@ __global__ void __launch_bounds__(kThreads,
   }
 }
 
+// ---- staged small-launch kernel -------------------------------------------
+//
+// A launch with fewer bags than one wave of lane groups is latency-bound:
+// every group pools about one bag, a dependent offsets -> ids -> rows chain,
+// and with U rows in registers per batch a bag of n ids takes n/U row round
+// trips. Here each lane copies its 16-byte column of up to kStageRows rows
+// of the bag straight into its own shared-memory slots with cp.async
+// (LDGSTS, no registers held while in flight), so a whole round of rows is
+// requested at once, and then adds them from shared memory in CSR order with
+// the same arithmetic as PoolVecKernel. A lane reads back only the slots it
+// filled itself, so lanes never wait for one another's copies.
+// fp32/bf16 rows of exactly G 16-byte vectors (G = 4..32), one lane per
+// vector.
+constexpr int kStageRows = 32;       // rows per round of a lane group
+constexpr int kStageThreads = 448;   // 14 warps: 448 * 32 * 16 B = 224 KB
+constexpr size_t kStageSmem =
+    static_cast<size_t>(kStageThreads) * kStageRows * sizeof(uint4);
+
+__device__ __forceinline__ void CopyAsync16(void* smem_dst,
+                                            const void* global_src) {
+  const uint32_t dst =
+      static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(dst),
+               "l"(global_src)
+               : "memory");
+}
+
+__device__ __forceinline__ void CopyAsyncWaitAll() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+template <int DT, int G, int WM>
+__device__ __forceinline__ void StagedBody(const PoolParams& p,
+                                           int64_t task_lo, int64_t task_hi,
+                                           int64_t block, int64_t blocks,
+                                           uint4* smem) {
+  constexpr int PPV = ElemsPerVec<DT>::value / 2;
+  constexpr int kGroups = kStageThreads / G;
+  constexpr int K = kStageRows / G;  // ids per lane per round
+  const int lane = threadIdx.x & 31;
+  const int gl = lane % G;
+  const unsigned gmask =
+      G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane - gl));
+  const int group = threadIdx.x / G;
+  // Slot of row u for this lane: mine[u * G].
+  uint4* const mine = smem + group * (kStageRows * G) + gl;
+  const int64_t stride = blocks * kGroups;
+  int t = 0;
+  for (int64_t task = task_lo + block * kGroups + group; task < task_hi;
+       task += stride) {
+    t = AdvanceDesc(p, t, task);
+    const BagDesc& d = p.d[t];
+    const int64_t bag = task - d.task_begin;
+    const int64_t begin = LoadIndex(d.offsets, d.offs64, bag);
+    const int64_t end = LoadIndex(d.offsets, d.offs64, bag + 1);
+    if (!CheckBag(p, d, begin, end)) continue;
+    const uint4* rows = static_cast<const uint4*>(d.rows) + gl;
+    u64 acc[1][PPV];
+#pragma unroll
+    for (int k = 0; k < PPV; ++k) acc[0][k] = 0;
+    float wsum = 0.0f;
+    for (int64_t base = begin; base < end; base += kStageRows) {
+      const int cnt =
+          static_cast<int>(end - base < kStageRows ? end - base : kStageRows);
+      // Ids (and weights) of this round: position k*G + gl on this lane.
+      int my_row[K];
+      float my_w[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int j = k * G + gl;
+        const bool live = j < cnt;
+        int64_t id = 0;
+        float w = 1.0f;
+        if (live) {
+          id = LoadIndex(d.ids, d.ids64, base + j);
+          if constexpr (WM != kUnweighted) w = __ldg(d.weights + base + j);
+        }
+        my_row[k] = StageRow(p, d, id, base + j, live);
+        my_w[k] = w;
+      }
+      // Every contributing row of the round in flight at once.
+      unsigned int present = 0;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        if (k * G < cnt) {
+#pragma unroll
+          for (int jj = 0; jj < G; ++jj) {
+            const int u = k * G + jj;
+            const int r = __shfl_sync(gmask, my_row[k], jj, G);
+            if (u < cnt && r >= 0) {
+              CopyAsync16(mine + u * G, rows + static_cast<int64_t>(r) * G);
+              present |= 1u << u;
+            }
+          }
+        }
+      }
+      CopyAsyncWaitAll();
+      // Adds in CSR order.
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        if (k * G < cnt) {
+#pragma unroll
+          for (int jj = 0; jj < G; ++jj) {
+            const int u = k * G + jj;
+            float w = 1.0f;
+            if constexpr (WM != kUnweighted) {
+              w = __shfl_sync(gmask, my_w[k], jj, G);
+            }
+            if (u < cnt) {
+              if constexpr (WM != kUnweighted) {
+                AddWeight<WM>(&wsum, w, d.combine);
+              }
+              if ((present >> u) & 1u) {
+                const uint4 raw[1] = {mine[u * G]};
+                AddGathered<DT, 1, WM>(acc, raw, make_float2(0.0f, 0.0f), w);
+              }
+            }
+          }
+        }
+      }
+    }
+    FinishBag<DT, G, 1, true, true>(d, d.out + bag * d.out_stride, d.vec_out,
+                                    end - begin, WM != kUnweighted, acc,
+                                    &wsum, gl, G);
+  }
+}
+
+template <int DT, int G>
+__global__ void __launch_bounds__(kStageThreads, 1)
+    PoolStagedKernel(const __grid_constant__ PoolParams p) {
+  EnterDependent();
+  if (!p.fused_checks && p.status->group_error != 0) return;
+  extern __shared__ uint4 stage_smem[];
+  const int64_t b = blockIdx.x;
+  const int64_t b0 = p.mode_blocks[0], b1 = p.mode_blocks[1];
+  if (b < b0) {
+    StagedBody<DT, G, kUnweighted>(p, 0, p.mode_tasks[0], b, b0, stage_smem);
+  } else if (b < b1) {
+    StagedBody<DT, G, kWeightedSum>(p, p.mode_tasks[0], p.mode_tasks[1],
+                                    b - b0, b1 - b0, stage_smem);
+  } else {
+    StagedBody<DT, G, kWeightedNorm>(p, p.mode_tasks[1], p.mode_tasks[2],
+                                     b - b1, gridDim.x - b1, stage_smem);
+  }
+}
+
 // ---- fused pooling + dot interaction --------------------------------------
 //
 // Blocks take samples one at a time from a counter in the status block (a
@@ -1247,15 +1399,15 @@ int BlocksPerSm(Kernel kernel) {
   return per_sm > 0 ? per_sm : 1;
 }
 
-// Launches `kernel` on `grid` blocks of kThreads with a programmatic
+// Launches `kernel` on `grid` blocks of `threads` with a programmatic
 // dependency on the previous kernel of the stream (see EnterDependent).
 template <typename... Params, typename... Args>
-cudaError_t LaunchDependentSmem(void (*kernel)(Params...), int grid,
-                                size_t smem, cudaStream_t stream,
-                                Args&&... args) {
+cudaError_t LaunchDependentBlock(void (*kernel)(Params...), int grid,
+                                 int threads, size_t smem,
+                                 cudaStream_t stream, Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1264,6 +1416,15 @@ cudaError_t LaunchDependentSmem(void (*kernel)(Params...), int grid,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Same with blocks of kThreads.
+template <typename... Params, typename... Args>
+cudaError_t LaunchDependentSmem(void (*kernel)(Params...), int grid,
+                                size_t smem, cudaStream_t stream,
+                                Args&&... args) {
+  return LaunchDependentBlock(kernel, grid, kThreads, smem, stream,
+                              std::forward<Args>(args)...);
 }
 
 template <typename... Params, typename... Args>
@@ -1354,6 +1515,24 @@ cudaError_t LaunchVec(const PoolParams& in, cudaStream_t stream) {
   AssignTasks(&p, 1);
   auto kernel = PoolVecKernel<DT, G, V, EXACT, 0>;
   int64_t max_grid = static_cast<int64_t>(SmCount()) * BlocksPerSm(kernel);
+#if XSE_POOL_STAGED
+  if constexpr (DT != 2 && V == 1 && EXACT) {
+    // At most one wave of the staged kernel's groups (one block per SM):
+    // whole rounds of rows in flight per bag (see PoolStagedKernel).
+    constexpr int kGroups = kStageThreads / G;
+    if (p.total_tasks <= static_cast<int64_t>(SmCount()) * kGroups) {
+      auto staged = PoolStagedKernel<DT, G>;
+      // Set on every launch: the attribute belongs to the current device.
+      cudaError_t e = cudaFuncSetAttribute(
+          staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
+          static_cast<int>(kStageSmem));
+      if (e != cudaSuccess) return e;
+      SplitModes(&p, SmCount(), kGroups);
+      return LaunchDependentBlock(staged, p.mode_blocks[2], kStageThreads,
+                                  kStageSmem, stream, p);
+    }
+  }
+#endif
   constexpr int kDeep = DeepRows<DT, G, V>();
   if constexpr (kDeep > 0) {
     // Fewer bags than one wave of the throughput kernel's groups: every
