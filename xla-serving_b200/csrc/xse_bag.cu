@@ -97,7 +97,8 @@ struct ElemsPerVec<2> {
 #define XSE_POOL_I8_MIN_BLOCKS 3
 #endif
 
-// 1: launches small enough for one wave of PoolStagedKernel use it.
+// PoolStagedKernel: 0 never, 1 for launches small enough for one wave of
+// it, 2 for every fp32/bf16 launch whose rows it serves.
 #ifndef XSE_POOL_STAGED
 #define XSE_POOL_STAGED 1
 #endif
@@ -786,6 +787,29 @@ __device__ __forceinline__ void CopyAsyncWaitAll() {
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
+// Ids (and weights) of one round of a bag: position k*G + gl of the round
+// starting at `base` on this lane, for k < K (zero past the bag's end).
+template <int WM, int G, int K>
+__device__ __forceinline__ void LoadRound(const BagDesc& d, int64_t base,
+                                          int64_t end, int gl,
+                                          int64_t (&id)[K], float (&w)[K]) {
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int64_t pos = base + k * G + gl;
+    id[k] = 0;
+    w[k] = 1.0f;
+    if (pos < end) {
+      id[k] = LoadIndex(d.ids, d.ids64, pos);
+      if constexpr (WM != kUnweighted) w[k] = __ldg(d.weights + pos);
+    }
+  }
+}
+
+// A group pools its bags (grid-stride tasks) as a software pipeline: while a
+// bag's first round of rows is in flight it loads the next bag's first-round
+// ids (whose offsets it loaded one bag earlier) and the offsets of the bag
+// after that, so consecutive bags cost about one row round trip each.
+// Further rounds of a long bag load their ids when they start.
 template <int DT, int G, int WM>
 __device__ __forceinline__ void StagedBody(const PoolParams& p,
                                            int64_t task_lo, int64_t task_hi,
@@ -802,83 +826,142 @@ __device__ __forceinline__ void StagedBody(const PoolParams& p,
   // Slot of row u for this lane: mine[u * G].
   uint4* const mine = smem + group * (kStageRows * G) + gl;
   const int64_t stride = blocks * kGroups;
-  int t = 0;
-  for (int64_t task = task_lo + block * kGroups + group; task < task_hi;
-       task += stride) {
-    t = AdvanceDesc(p, t, task);
+  int64_t task = task_lo + block * kGroups + group;
+  if (task >= task_hi) return;
+  int t = AdvanceDesc(p, 0, task);
+  int64_t begin, end;
+  {
+    const BagDesc& d = p.d[t];
+    begin = LoadIndex(d.offsets, d.offs64, task - d.task_begin);
+    end = LoadIndex(d.offsets, d.offs64, task - d.task_begin + 1);
+  }
+  int64_t cid[K];
+  float cw[K];
+  if (SafeBag(p.d[t], begin, end)) {
+    LoadRound<WM, G, K>(p.d[t], begin, end, gl, cid, cw);
+  } else {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      cid[k] = 0;
+      cw[k] = 1.0f;
+    }
+  }
+  int64_t ntask = task + stride;
+  int nt = t;
+  int64_t nbegin = 0, nend = 0;
+  if (ntask < task_hi) {
+    nt = AdvanceDesc(p, t, ntask);
+    const BagDesc& nd = p.d[nt];
+    nbegin = LoadIndex(nd.offsets, nd.offs64, ntask - nd.task_begin);
+    nend = LoadIndex(nd.offsets, nd.offs64, ntask - nd.task_begin + 1);
+  }
+  for (;;) {
     const BagDesc& d = p.d[t];
     const int64_t bag = task - d.task_begin;
-    const int64_t begin = LoadIndex(d.offsets, d.offs64, bag);
-    const int64_t end = LoadIndex(d.offsets, d.offs64, bag + 1);
-    if (!CheckBag(p, d, begin, end)) continue;
-    const uint4* rows = static_cast<const uint4*>(d.rows) + gl;
-    u64 acc[1][PPV];
+    const bool has_next = ntask < task_hi;
+    const int64_t n2task = ntask + stride;
+    int n2t = nt;
+    int64_t n2begin = 0, n2end = 0;
+    int64_t xid[K];
+    float xw[K];
 #pragma unroll
-    for (int k = 0; k < PPV; ++k) acc[0][k] = 0;
-    float wsum = 0.0f;
-    for (int64_t base = begin; base < end; base += kStageRows) {
-      const int cnt =
-          static_cast<int>(end - base < kStageRows ? end - base : kStageRows);
-      // Ids (and weights) of this round: position k*G + gl on this lane.
-      int my_row[K];
-      float my_w[K];
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const int j = k * G + gl;
-        const bool live = j < cnt;
-        int64_t id = 0;
-        float w = 1.0f;
-        if (live) {
-          id = LoadIndex(d.ids, d.ids64, base + j);
-          if constexpr (WM != kUnweighted) w = __ldg(d.weights + base + j);
-        }
-        my_row[k] = StageRow(p, d, id, base + j, live);
-        my_w[k] = w;
-      }
-      // Every contributing row of the round in flight at once.
-      unsigned int present = 0;
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        if (k * G < cnt) {
-#pragma unroll
-          for (int jj = 0; jj < G; ++jj) {
-            const int u = k * G + jj;
-            const int r = __shfl_sync(gmask, my_row[k], jj, G);
-            if (u < cnt && r >= 0) {
-              CopyAsync16(mine + u * G, rows + static_cast<int64_t>(r) * G);
-              present |= 1u << u;
-            }
-          }
-        }
-      }
-      CopyAsyncWaitAll();
-      // Adds in CSR order.
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        if (k * G < cnt) {
-#pragma unroll
-          for (int jj = 0; jj < G; ++jj) {
-            const int u = k * G + jj;
-            float w = 1.0f;
-            if constexpr (WM != kUnweighted) {
-              w = __shfl_sync(gmask, my_w[k], jj, G);
-            }
-            if (u < cnt) {
-              if constexpr (WM != kUnweighted) {
-                AddWeight<WM>(&wsum, w, d.combine);
-              }
-              if ((present >> u) & 1u) {
-                const uint4 raw[1] = {mine[u * G]};
-                AddGathered<DT, 1, WM>(acc, raw, make_float2(0.0f, 0.0f), w);
-              }
-            }
-          }
-        }
-      }
+    for (int k = 0; k < K; ++k) {
+      xid[k] = 0;
+      xw[k] = 1.0f;
     }
-    FinishBag<DT, G, 1, true, true>(d, d.out + bag * d.out_stride, d.vec_out,
-                                    end - begin, WM != kUnweighted, acc,
-                                    &wsum, gl, G);
+    bool prefetched = false;
+    // The next bag's first-round ids and the offsets after it.
+    auto prefetch = [&]() {
+      prefetched = true;
+      if (has_next && SafeBag(p.d[nt], nbegin, nend)) {
+        LoadRound<WM, G, K>(p.d[nt], nbegin, nend, gl, xid, xw);
+      }
+      if (n2task < task_hi) {
+        n2t = AdvanceDesc(p, nt, n2task);
+        const BagDesc& n2d = p.d[n2t];
+        n2begin = LoadIndex(n2d.offsets, n2d.offs64, n2task - n2d.task_begin);
+        n2end =
+            LoadIndex(n2d.offsets, n2d.offs64, n2task - n2d.task_begin + 1);
+      }
+    };
+    if (CheckBag(p, d, begin, end)) {
+      const uint4* rows = static_cast<const uint4*>(d.rows) + gl;
+      u64 acc[1][PPV];
+#pragma unroll
+      for (int k = 0; k < PPV; ++k) acc[0][k] = 0;
+      float wsum = 0.0f;
+      for (int64_t base = begin; base < end; base += kStageRows) {
+        const int cnt = static_cast<int>(
+            end - base < kStageRows ? end - base : kStageRows);
+        if (base != begin) LoadRound<WM, G, K>(d, base, end, gl, cid, cw);
+        int my_row[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          const int j = k * G + gl;
+          my_row[k] = StageRow(p, d, cid[k], base + j, j < cnt);
+        }
+        // Every contributing row of the round in flight at once.
+        unsigned int present = 0;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          if (k * G < cnt) {
+#pragma unroll
+            for (int jj = 0; jj < G; ++jj) {
+              const int u = k * G + jj;
+              const int r = __shfl_sync(gmask, my_row[k], jj, G);
+              if (u < cnt && r >= 0) {
+                CopyAsync16(mine + u * G, rows + static_cast<int64_t>(r) * G);
+                present |= 1u << u;
+              }
+            }
+          }
+        }
+        if (!prefetched) prefetch();
+        CopyAsyncWaitAll();
+        // Adds in CSR order.
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          if (k * G < cnt) {
+#pragma unroll
+            for (int jj = 0; jj < G; ++jj) {
+              const int u = k * G + jj;
+              float w = 1.0f;
+              if constexpr (WM != kUnweighted) {
+                w = __shfl_sync(gmask, cw[k], jj, G);
+              }
+              if (u < cnt) {
+                if constexpr (WM != kUnweighted) {
+                  AddWeight<WM>(&wsum, w, d.combine);
+                }
+                if ((present >> u) & 1u) {
+                  const uint4 raw[1] = {mine[u * G]};
+                  AddGathered<DT, 1, WM>(acc, raw, make_float2(0.0f, 0.0f),
+                                         w);
+                }
+              }
+            }
+          }
+        }
+      }
+      FinishBag<DT, G, 1, true, true>(d, d.out + bag * d.out_stride,
+                                      d.vec_out, end - begin,
+                                      WM != kUnweighted, acc, &wsum, gl, G);
+    }
+    if (!prefetched) prefetch();
+    if (!has_next) break;
+    task = ntask;
+    t = nt;
+    begin = nbegin;
+    end = nend;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      cid[k] = xid[k];
+      cw[k] = xw[k];
+    }
+    ntask = n2task;
+    nt = n2t;
+    nbegin = n2begin;
+    nend = n2end;
   }
 }
 
@@ -1518,9 +1601,14 @@ cudaError_t LaunchVec(const PoolParams& in, cudaStream_t stream) {
 #if XSE_POOL_STAGED
   if constexpr (DT != 2 && V == 1 && EXACT) {
     // At most one wave of the staged kernel's groups (one block per SM):
-    // whole rounds of rows in flight per bag (see PoolStagedKernel).
+    // whole rounds of rows in flight per bag (see PoolStagedKernel). Larger
+    // launches take it when the caller chose it (kPoolStaged).
     constexpr int kGroups = kStageThreads / G;
-    if (p.total_tasks <= static_cast<int64_t>(SmCount()) * kGroups) {
+    const bool small =
+        p.total_tasks <= static_cast<int64_t>(SmCount()) * kGroups;
+    if (p.kernel_choice == kPoolStaged ||
+        (p.kernel_choice == kPoolAuto &&
+         (XSE_POOL_STAGED == 2 || small))) {
       auto staged = PoolStagedKernel<DT, G>;
       // Set on every launch: the attribute belongs to the current device.
       cudaError_t e = cudaFuncSetAttribute(
@@ -1625,6 +1713,18 @@ cudaError_t LaunchInteractMode(int wm, const PoolParams& p,
 }
 
 }  // namespace
+
+bool PoolKernelTunable(const Layout& layout, int64_t total_tasks) {
+#if XSE_POOL_STAGED
+  if (layout.dtype == 2 || layout.v != 1 || !layout.exact) return false;
+  const int64_t groups = kStageThreads / layout.g;
+  return total_tasks > static_cast<int64_t>(SmCount()) * groups;
+#else
+  (void)layout;
+  (void)total_tasks;
+  return false;
+#endif
+}
 
 Layout ChooseLayout(int dtype, int dim, const void* rows) {
   const int elem = dtype == 0 ? 4 : dtype == 1 ? 2 : 1;

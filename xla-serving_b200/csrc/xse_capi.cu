@@ -165,6 +165,21 @@ struct xse_status {
   }
 };
 
+// One timed trial launch of the pooling-kernel tuner.
+struct PoolTrial {
+  int32_t choice;  // xse::kPoolStreaming or xse::kPoolStaged
+  cudaEvent_t start, end;
+};
+
+// Pooling-kernel choice for one launch signature (see ChoosePoolKernel).
+struct PoolTuner {
+  int32_t decided = xse::kPoolAuto;
+  int64_t launched = 0;       // trial launches issued
+  int32_t done[2] = {0, 0};   // completed timings: streaming, staged
+  float ms[2] = {0.0f, 0.0f};
+  std::vector<PoolTrial> pending;
+};
+
 struct xse_engine {
   int device = 0;
   std::mutex specs_mu;
@@ -180,6 +195,9 @@ struct xse_engine {
   int64_t profile_calls = 0;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> profile_events;
   size_t profile_used = 0;
+  // Pooling-kernel tuner, keyed by launch signature.
+  std::mutex tune_mu;
+  std::unordered_map<uint64_t, PoolTuner> tuners;
 };
 
 namespace {
@@ -408,6 +426,111 @@ int CheckIsolation(const xse_bag_request* reqs,
     }
   }
   return XSE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Pooling-kernel tuner. fp32/bf16 launches larger than one wave of
+// PoolStagedKernel can run either it or PoolVecKernel, with bit-identical
+// results; which is faster depends on the id stream (the staged kernel wins
+// when skewed ids make most rows cache hits -- the Zipf(1.1) table-wise
+// slice 1.08 -> 0.90 ms -- and loses badly on uniform ids over tables
+// larger than L2: 70 -> 123 us on the multi-table workload), which the
+// engine cannot see. So per launch signature (layout, tables and their
+// weighting modes, request count, log2 of the bag count) the first executions alternate the two
+// kernels with CUDA events around each launch, and once each kernel has
+// kTuneTrials completed timings the faster is used from then on. Events are
+// read without waiting (cudaEventQuery) on later executions of the same
+// signature.
+constexpr int kTuneTrials = 2;
+constexpr size_t kTuneMaxPending = 4 * kTuneTrials;
+
+uint64_t TuneKey(const xse::Layout& l, const xse::PoolParams& p) {
+  uint64_t h = 1469598103934665603ull;  // FNV-1a
+  auto mix = [&h](uint64_t v) {
+    h ^= v;
+    h *= 1099511628211ull;
+  };
+  mix(static_cast<uint64_t>(l.dtype));
+  mix(static_cast<uint64_t>(l.g));
+  mix(static_cast<uint64_t>(l.v));
+  mix(static_cast<uint64_t>(l.exact));
+  mix(static_cast<uint64_t>(p.n));
+  for (int32_t k = 0; k < p.n; ++k) {
+    mix(static_cast<uint64_t>(reinterpret_cast<uintptr_t>(p.d[k].rows)));
+    mix(static_cast<uint64_t>(xse::WeightModeOf(p.d[k])));
+  }
+  int bucket = 0;
+  for (int64_t t = p.total_tasks; t > 1; t >>= 1) ++bucket;
+  mix(static_cast<uint64_t>(bucket));
+  return h;
+}
+
+// Folds the trial timings that have completed into `t` (tune_mu held).
+void PollTrials(PoolTuner* t) {
+  size_t keep = 0;
+  for (size_t i = 0; i < t->pending.size(); ++i) {
+    PoolTrial& trial = t->pending[i];
+    const cudaError_t q = cudaEventQuery(trial.end);
+    if (q == cudaErrorNotReady) {
+      // Not an error: clear it from the runtime's last-error slot.
+      if (cudaPeekAtLastError() == cudaErrorNotReady) (void)cudaGetLastError();
+      t->pending[keep++] = trial;
+      continue;
+    }
+    float ms = 0.0f;
+    if (q == cudaSuccess &&
+        cudaEventElapsedTime(&ms, trial.start, trial.end) == cudaSuccess) {
+      const int k = trial.choice == xse::kPoolStaged ? 1 : 0;
+      t->ms[k] += ms;
+      ++t->done[k];
+    }
+    cudaEventDestroy(trial.start);
+    cudaEventDestroy(trial.end);
+  }
+  t->pending.resize(keep);
+  if (t->decided == xse::kPoolAuto && t->done[0] >= kTuneTrials &&
+      t->done[1] >= kTuneTrials) {
+    t->decided = t->ms[1] / t->done[1] < t->ms[0] / t->done[0]
+                     ? xse::kPoolStaged
+                     : xse::kPoolStreaming;
+  }
+}
+
+// Sets p->kernel_choice for a launch of `engine`; returns the trial to time
+// (events created, choice set) or a trial with null events.
+PoolTrial ChoosePoolKernel(xse_engine* engine, const xse::Layout& l,
+                           xse::PoolParams* p, uint64_t* key) {
+  PoolTrial trial{xse::kPoolAuto, nullptr, nullptr};
+  if (!xse::PoolKernelTunable(l, p->total_tasks)) return trial;
+  *key = TuneKey(l, *p);
+  std::lock_guard<std::mutex> lock(engine->tune_mu);
+  PoolTuner& t = engine->tuners[*key];
+  if (!t.pending.empty()) PollTrials(&t);
+  if (t.decided != xse::kPoolAuto) {
+    p->kernel_choice = t.decided;
+    return trial;
+  }
+  if (t.pending.size() >= kTuneMaxPending) return trial;  // static rule
+  const int32_t choice =
+      t.launched % 2 == 0 ? xse::kPoolStaged : xse::kPoolStreaming;
+  if (cudaEventCreate(&trial.start) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return PoolTrial{xse::kPoolAuto, nullptr, nullptr};
+  }
+  if (cudaEventCreate(&trial.end) != cudaSuccess) {
+    (void)cudaGetLastError();
+    cudaEventDestroy(trial.start);
+    return PoolTrial{xse::kPoolAuto, nullptr, nullptr};
+  }
+  ++t.launched;
+  trial.choice = choice;
+  p->kernel_choice = choice;
+  return trial;
+}
+
+void AddTrial(xse_engine* engine, uint64_t key, const PoolTrial& trial) {
+  std::lock_guard<std::mutex> lock(engine->tune_mu);
+  engine->tuners[key].pending.push_back(trial);
 }
 
 class DeviceGuard {
@@ -707,7 +830,14 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
           }
           p.n = static_cast<int32_t>(cnt);
           p.total_tasks = tasks;
+          uint64_t key = 0;
+          const PoolTrial trial = ChoosePoolKernel(engine, l, &p, &key);
+          if (trial.start != nullptr) cudaEventRecord(trial.start, stream);
           cudaError_t le = xse::LaunchPool(l, p, stream, &launches);
+          if (trial.start != nullptr) {
+            cudaEventRecord(trial.end, stream);
+            AddTrial(engine, key, trial);
+          }
           if (le != cudaSuccess) return le;
         }
       }
@@ -855,6 +985,13 @@ void xse_engine_destroy(xse_engine* engine) {
   for (auto& ev : engine->profile_events) {
     cudaEventDestroy(ev.first);
     cudaEventDestroy(ev.second);
+  }
+  for (auto& [key, tuner] : engine->tuners) {
+    (void)key;
+    for (const PoolTrial& trial : tuner.pending) {
+      cudaEventDestroy(trial.start);
+      cudaEventDestroy(trial.end);
+    }
   }
   delete engine;
 }

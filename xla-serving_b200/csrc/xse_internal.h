@@ -75,9 +75,14 @@ struct PoolParams {
   // and block ends of modes 0, 1, 2 (set by the launcher).
   int64_t mode_tasks[3];
   int32_t mode_blocks[3];
-  int32_t reserved2;
+  // Host-side kernel choice for fp32/bf16 rows (the kernels ignore it):
+  // kPoolAuto, kPoolStreaming (PoolVecKernel) or kPoolStaged
+  // (PoolStagedKernel).
+  int32_t kernel_choice;
   BagDesc d[kMaxDescsPerLaunch];
 };
+
+enum : int32_t { kPoolAuto = 0, kPoolStreaming = 1, kPoolStaged = 2 };
 
 // Row layout class of a launch: G lanes per row, V 16-byte vectors per lane.
 // V == 0 selects the element-wise kernel (dims that are not whole vectors).
@@ -104,6 +109,11 @@ int64_t ValidationWork(int64_t num_bags, int64_t num_ids);
 
 cudaError_t LaunchValidate(const PoolParams& p, int64_t total_work,
                            cudaStream_t stream);
+// True when both PoolVecKernel and PoolStagedKernel serve a launch of this
+// layout and size and neither is the fixed choice: the launch is larger than
+// one wave of the staged kernel (small launches always take it).
+bool PoolKernelTunable(const Layout& layout, int64_t total_tasks);
+
 cudaError_t LaunchPool(const Layout& layout, const PoolParams& p,
                        cudaStream_t stream, int* launches);
 cudaError_t LaunchInterleaveScaleBias(const float* scale, const float* bias,
