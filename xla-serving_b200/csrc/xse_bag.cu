@@ -98,7 +98,7 @@ struct ElemsPerVec<2> {
 #endif
 
 // PoolStagedKernel: 0 never, 1 for launches small enough for one wave of
-// it, 2 for every fp32/bf16 launch whose rows it serves.
+// it, 2 for every launch whose rows it serves.
 #ifndef XSE_POOL_STAGED
 #define XSE_POOL_STAGED 1
 #endif
@@ -766,8 +766,8 @@ __global__ void __launch_bounds__(kThreads,
 // requested at once, and then adds them from shared memory in CSR order with
 // the same arithmetic as PoolVecKernel. A lane reads back only the slots it
 // filled itself, so lanes never wait for one another's copies.
-// fp32/bf16 rows of exactly G 16-byte vectors (G = 4..32), one lane per
-// vector.
+// Rows of exactly G 16-byte vectors (G = 4..32), one lane per vector; int8
+// rows take their (scale, bias) from the lane that holds the row's id.
 constexpr int kStageRows = 32;       // rows per round of a lane group
 constexpr int kStageThreads = 448;   // 14 warps: 448 * 32 * 16 B = 224 KB
 constexpr size_t kStageSmem =
@@ -895,10 +895,15 @@ __device__ __forceinline__ void StagedBody(const PoolParams& p,
             end - base < kStageRows ? end - base : kStageRows);
         if (base != begin) LoadRound<WM, G, K>(d, base, end, gl, cid, cw);
         int my_row[K];
+        float2 my_sb[K];  // int8 rows: (scale, bias) of this lane's id
 #pragma unroll
         for (int k = 0; k < K; ++k) {
           const int j = k * G + gl;
           my_row[k] = StageRow(p, d, cid[k], base + j, j < cnt);
+          if constexpr (DT == 2) {
+            my_sb[k] = my_row[k] >= 0 ? __ldg(d.scale_bias + my_row[k])
+                                      : make_float2(0.0f, 0.0f);
+          }
         }
         // Every contributing row of the round in flight at once.
         unsigned int present = 0;
@@ -933,10 +938,14 @@ __device__ __forceinline__ void StagedBody(const PoolParams& p,
                 if constexpr (WM != kUnweighted) {
                   AddWeight<WM>(&wsum, w, d.combine);
                 }
+                float2 sb = make_float2(0.0f, 0.0f);
+                if constexpr (DT == 2) {
+                  sb.x = __shfl_sync(gmask, my_sb[k].x, jj, G);
+                  sb.y = __shfl_sync(gmask, my_sb[k].y, jj, G);
+                }
                 if ((present >> u) & 1u) {
                   const uint4 raw[1] = {mine[u * G]};
-                  AddGathered<DT, 1, WM>(acc, raw, make_float2(0.0f, 0.0f),
-                                         w);
+                  AddGathered<DT, 1, WM>(acc, raw, sb, w);
                 }
               }
             }
@@ -1599,7 +1608,7 @@ cudaError_t LaunchVec(const PoolParams& in, cudaStream_t stream) {
   auto kernel = PoolVecKernel<DT, G, V, EXACT, 0>;
   int64_t max_grid = static_cast<int64_t>(SmCount()) * BlocksPerSm(kernel);
 #if XSE_POOL_STAGED
-  if constexpr (DT != 2 && V == 1 && EXACT) {
+  if constexpr (V == 1 && EXACT) {
     // At most one wave of the staged kernel's groups (one block per SM):
     // whole rounds of rows in flight per bag (see PoolStagedKernel). Larger
     // launches take it when the caller chose it (kPoolStaged).
@@ -1716,7 +1725,7 @@ cudaError_t LaunchInteractMode(int wm, const PoolParams& p,
 
 bool PoolKernelTunable(const Layout& layout, int64_t total_tasks) {
 #if XSE_POOL_STAGED
-  if (layout.dtype == 2 || layout.v != 1 || !layout.exact) return false;
+  if (layout.v != 1 || !layout.exact) return false;
   const int64_t groups = kStageThreads / layout.g;
   return total_tasks > static_cast<int64_t>(SmCount()) * groups;
 #else

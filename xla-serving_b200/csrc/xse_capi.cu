@@ -429,8 +429,8 @@ int CheckIsolation(const xse_bag_request* reqs,
 }
 
 // ---------------------------------------------------------------------------
-// Pooling-kernel tuner. fp32/bf16 launches larger than one wave of
-// PoolStagedKernel can run either it or PoolVecKernel, with bit-identical
+// Pooling-kernel tuner. Launches of 16-byte-vector rows larger than one wave
+// of PoolStagedKernel can run either it or PoolVecKernel, with bit-identical
 // results; which is faster depends on the id stream (the staged kernel wins
 // when skewed ids make most rows cache hits -- the Zipf(1.1) table-wise
 // slice 1.08 -> 0.90 ms -- and loses badly on uniform ids over tables

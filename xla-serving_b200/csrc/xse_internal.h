@@ -75,7 +75,7 @@ struct PoolParams {
   // and block ends of modes 0, 1, 2 (set by the launcher).
   int64_t mode_tasks[3];
   int32_t mode_blocks[3];
-  // Host-side kernel choice for fp32/bf16 rows (the kernels ignore it):
+  // Host-side kernel choice for 16-byte-vector rows (kernels ignore it):
   // kPoolAuto, kPoolStreaming (PoolVecKernel) or kPoolStaged
   // (PoolStagedKernel).
   int32_t kernel_choice;
