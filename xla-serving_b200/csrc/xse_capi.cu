@@ -443,6 +443,9 @@ int CheckIsolation(const xse_bag_request* reqs,
 // signature.
 constexpr int kTuneTrials = 2;
 constexpr size_t kTuneMaxPending = 4 * kTuneTrials;
+// Signatures beyond this many take the fixed rule (bounds the map when
+// batch shapes or table sets keep changing).
+constexpr size_t kTuneMaxSignatures = 4096;
 
 uint64_t TuneKey(const xse::Layout& l, const xse::PoolParams& p) {
   uint64_t h = 1469598103934665603ull;  // FNV-1a
@@ -504,6 +507,10 @@ PoolTrial ChoosePoolKernel(xse_engine* engine, const xse::Layout& l,
   if (!xse::PoolKernelTunable(l, p->total_tasks)) return trial;
   *key = TuneKey(l, *p);
   std::lock_guard<std::mutex> lock(engine->tune_mu);
+  if (engine->tuners.size() >= kTuneMaxSignatures &&
+      engine->tuners.find(*key) == engine->tuners.end()) {
+    return trial;
+  }
   PoolTuner& t = engine->tuners[*key];
   if (!t.pending.empty()) PollTrials(&t);
   if (t.decided != xse::kPoolAuto) {
