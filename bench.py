@@ -1201,7 +1201,9 @@ def main():
         "roofline": {
             "bound": "hbm",
             "kernel": "PoolVecKernel<bf16, G=16, V=1, exact> (one launch "
-                      "per weighting mode)",
+                      "serving both weighting modes; the engine's kernel "
+                      "tuner keeps it over PoolStagedKernel here: 70 vs "
+                      "123 us)",
             "achieved": achieved,
             "peak": peak,
             "peak_kind": peak_kind,
