@@ -755,19 +755,21 @@ __global__ void __launch_bounds__(kThreads,
   }
 }
 
-// ---- staged small-launch kernel -------------------------------------------
+// ---- staged kernel ---------------------------------------------------------
 //
-// A launch with fewer bags than one wave of lane groups is latency-bound:
-// every group pools about one bag, a dependent offsets -> ids -> rows chain,
-// and with U rows in registers per batch a bag of n ids takes n/U row round
-// trips. Here each lane copies its 16-byte column of up to kStageRows rows
-// of the bag straight into its own shared-memory slots with cp.async
-// (LDGSTS, no registers held while in flight), so a whole round of rows is
-// requested at once, and then adds them from shared memory in CSR order with
-// the same arithmetic as PoolVecKernel. A lane reads back only the slots it
-// filled itself, so lanes never wait for one another's copies.
-// Rows of exactly G 16-byte vectors (G = 4..32), one lane per vector; int8
-// rows take their (scale, bias) from the lane that holds the row's id.
+// PoolVecKernel holds the rows of a batch in registers, U per lane, so a bag
+// of n ids takes about n/U row round trips; with few bags per group (small
+// launches) or with rows that mostly hit the caches (skewed ids) those round
+// trips, not bandwidth, set the time. Here each lane copies its 16-byte
+// column of up to kStageRows rows of the bag straight into its own
+// shared-memory slots with cp.async (LDGSTS, no registers held while in
+// flight), so a whole round of rows is requested at once, and then adds them
+// from shared memory in CSR order with the same arithmetic as PoolVecKernel.
+// A lane reads back only the slots it filled itself, so lanes never wait for
+// one another's copies. Rows of exactly G 16-byte vectors (G = 4..32), one
+// lane per vector; int8 rows take their (scale, bias) from the lane that
+// holds the row's id. Small launches always use it; for larger ones the
+// engine's tuner times both kernels and keeps the faster.
 constexpr int kStageRows = 32;       // rows per round of a lane group
 constexpr int kStageThreads = 448;   // 14 warps: 448 * 32 * 16 B = 224 KB
 constexpr size_t kStageSmem =
