@@ -55,6 +55,7 @@ E2E_THREADS = 2  # concurrent host callers of the operator in the e2e run
 # microseconds of stream time and serialises the kernels on either side of
 # it, so timing every step would slow the very steps being timed.
 PROFILE_PERIOD = 8
+MIN_WARMUP = 8
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one step's
 # pooling kernels, from an ncu capture of this workload on a B200.
 POOL_DRAM_BYTES_PER_STEP = 330.32e6
@@ -1086,8 +1087,11 @@ def main():
                        "forward), dlrm (the DLRM forward alone) or one of "
                        "the other reference configs")
   args = ap.parse_args()
-  if args.warmup < 3:
-    args.warmup = 3
+  # At least 3 warm-up steps, and enough for the engine's pooling-kernel
+  # tuner (the first four executions of a launch alternate its two kernels)
+  # to settle before the timed region.
+  if args.warmup < MIN_WARMUP:
+    args.warmup = MIN_WARMUP
   if args.impl == "reference":
     run_reference(args)
     return

@@ -176,7 +176,7 @@ struct PoolTuner {
   int32_t decided = xse::kPoolAuto;
   int64_t launched = 0;       // trial launches issued
   int32_t done[2] = {0, 0};   // completed timings: streaming, staged
-  float ms[2] = {0.0f, 0.0f};
+  float ms[2] = {0.0f, 0.0f};  // fastest of each kernel's timings
   std::vector<PoolTrial> pending;
 };
 
@@ -436,11 +436,11 @@ int CheckIsolation(const xse_bag_request* reqs,
 // slice 1.08 -> 0.90 ms -- and loses badly on uniform ids over tables
 // larger than L2: 70 -> 123 us on the multi-table workload), which the
 // engine cannot see. So per launch signature (layout, tables and their
-// weighting modes, request count, log2 of the bag count) the first executions alternate the two
-// kernels with CUDA events around each launch, and once each kernel has
-// kTuneTrials completed timings the faster is used from then on. Events are
-// read without waiting (cudaEventQuery) on later executions of the same
-// signature.
+// weighting modes, request count, log2 of the bag count) the first
+// executions alternate the two kernels with CUDA events around each launch,
+// and once each kernel has kTuneTrials completed timings the one with the
+// faster best time is used from then on. Events are read without waiting
+// (cudaEventQuery) on later executions of the same signature.
 constexpr int kTuneTrials = 2;
 constexpr size_t kTuneMaxPending = 4 * kTuneTrials;
 // Signatures beyond this many take the fixed rule (bounds the map when
@@ -483,8 +483,10 @@ void PollTrials(PoolTuner* t) {
     float ms = 0.0f;
     if (q == cudaSuccess &&
         cudaEventElapsedTime(&ms, trial.start, trial.end) == cudaSuccess) {
+      // The fastest timing of each kernel: a first launch can carry one-off
+      // costs (module loading, cold caches) that later ones do not.
       const int k = trial.choice == xse::kPoolStaged ? 1 : 0;
-      t->ms[k] += ms;
+      t->ms[k] = t->done[k] == 0 ? ms : std::min(t->ms[k], ms);
       ++t->done[k];
     }
     cudaEventDestroy(trial.start);
@@ -493,9 +495,8 @@ void PollTrials(PoolTuner* t) {
   t->pending.resize(keep);
   if (t->decided == xse::kPoolAuto && t->done[0] >= kTuneTrials &&
       t->done[1] >= kTuneTrials) {
-    t->decided = t->ms[1] / t->done[1] < t->ms[0] / t->done[0]
-                     ? xse::kPoolStaged
-                     : xse::kPoolStreaming;
+    t->decided =
+        t->ms[1] < t->ms[0] ? xse::kPoolStaged : xse::kPoolStreaming;
   }
 }
 
