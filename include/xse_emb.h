@@ -171,7 +171,12 @@ void xse_status_destroy(xse_status* status);
 /* Runs one group of requests. status may be NULL unless XSE_EXEC_ASYNC is
  * set; a NULL status uses an engine-owned block and serializes such calls.
  * Errors use the reference's messages and request prefix
- * ("FP32 embedding-bag request %d: ...", embedding_bag.cc:229-233). */
+ * ("FP32 embedding-bag request %d: ...", embedding_bag.cc:229-233).
+ * The engine chooses its pooling kernel per launch signature (tables,
+ * layout, request count, batch size class): for large launches the first
+ * four executions of a signature alternate two kernels with CUDA events
+ * around each launch, and the faster is kept. Results are bit-identical
+ * whichever kernel runs. */
 int xse_engine_execute_batch(xse_engine* engine, const xse_bag_request* reqs,
                              int32_t n, void* stream, int32_t flags,
                              xse_status* status);
