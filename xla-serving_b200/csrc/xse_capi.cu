@@ -481,8 +481,13 @@ void PollTrials(PoolTuner* t) {
       continue;
     }
     float ms = 0.0f;
-    if (q == cudaSuccess &&
-        cudaEventElapsedTime(&ms, trial.start, trial.end) == cudaSuccess) {
+    const cudaError_t te =
+        q == cudaSuccess ? cudaEventElapsedTime(&ms, trial.start, trial.end)
+                         : q;
+    // A trial whose events failed is dropped; its error must not surface as
+    // the last error of an unrelated later call.
+    if (te != cudaSuccess) (void)cudaGetLastError();
+    if (te == cudaSuccess) {
       // The fastest timing of each kernel: a first launch can carry one-off
       // costs (module loading, cold caches) that later ones do not.
       const int k = trial.choice == xse::kPoolStaged ? 1 : 0;
@@ -840,10 +845,16 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
           p.total_tasks = tasks;
           uint64_t key = 0;
           const PoolTrial trial = ChoosePoolKernel(engine, l, &p, &key);
-          if (trial.start != nullptr) cudaEventRecord(trial.start, stream);
+          // A failed record only spoils the trial (PollTrials drops it).
+          if (trial.start != nullptr &&
+              cudaEventRecord(trial.start, stream) != cudaSuccess) {
+            (void)cudaGetLastError();
+          }
           cudaError_t le = xse::LaunchPool(l, p, stream, &launches);
           if (trial.start != nullptr) {
-            cudaEventRecord(trial.end, stream);
+            if (cudaEventRecord(trial.end, stream) != cudaSuccess) {
+              (void)cudaGetLastError();
+            }
             AddTrial(engine, key, trial);
           }
           if (le != cudaSuccess) return le;
