@@ -19,7 +19,11 @@
 // per SM, layouts whose rows are exactly G*V vectors drop per-lane bounds
 // checks at compile time, and the fp32 arithmetic runs on packed pairs
 // (sm_100 add/mul.rn.f32x2: two independently rounded IEEE operations in one
-// instruction).
+// instruction). That is PoolVecKernel. PoolStagedKernel instead copies a
+// whole round of up to 32 rows of a bag into shared memory with cp.async,
+// for launches too small to fill the GPU and for id streams whose rows
+// mostly hit the caches; the engine times both on large launches and keeps
+// the faster (the results are bit-identical).
 //
 // Every element is accumulated in fp32 in exactly the reference's order
 // (out = 0; out += row or out += w*row, one separately rounded multiply and
