@@ -222,8 +222,10 @@ int xse_engine_execute_legacy(xse_engine* engine, const xse_bag_request* reqs,
  * (cudaGetSymbolAddress); make that first call outside any CUDA stream
  * capture. All calls share the one array and clear it at their start, so
  * calls that overlap on the GPU (from several host threads or streams at
- * once) race on it: serialize them. Host-side argument errors are reported
- * before any device-side validation error. */
+ * once) race on it: serialize them. Errors are resolved in the order of
+ * xse_engine_execute_batch (request by request: early argument errors,
+ * offsets, null ids or weights, out-of-range ids; output isolation last),
+ * with the same codes and messages. */
 #define XSE_NOALLOC_MAX_REQUESTS 64
 int xse_engine_execute_batch_noalloc(xse_engine* engine,
                                      const xse_bag_request* reqs, int32_t n,

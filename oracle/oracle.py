@@ -70,6 +70,15 @@ def _load():
   lib.oracle_synth_rows_bf16.restype = None
   lib.oracle_synth_rows_i8.argtypes = [U64, U64, I64, I64, I64, P, P, P]
   lib.oracle_synth_rows_i8.restype = None
+  lib.oracle_synth_rows_at.argtypes = [I32, U64, U64, P, I64, I64, P, P, P]
+  lib.oracle_synth_rows_at.restype = None
+  lib.oracle_synth_lengths.argtypes = [I64, I32, I32, U64, U64, P]
+  lib.oracle_synth_lengths.restype = None
+  lib.oracle_synth_weights.argtypes = [I64, U64, U64, I64, P]
+  lib.oracle_synth_weights.restype = None
+  lib.oracle_synth_ids.argtypes = [I64, I64, ctypes.c_double, U64, U64, U64,
+                                   U64, I64, P]
+  lib.oracle_synth_ids.restype = None
   lib.oracle_zipf_rank.argtypes = [U64, U64, U64, I64, ctypes.c_double]
   lib.oracle_zipf_rank.restype = I64
   lib.oracle_host_cores.argtypes = []
@@ -240,3 +249,112 @@ def zipf_rank(seed, stream, index, n, alpha):
 def bf16_bits_to_f32(bits):
   return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(
       np.float32)
+
+
+def synth_rows_at(dtype, seed, table, rows, dim):
+  """Rows `rows` (any order) of a synthetic table: (values, scale, bias) as
+  synth_rows returns them."""
+  rows = np.ascontiguousarray(rows, dtype=np.int64)
+  n = len(rows)
+  vdt = {F32: np.float32, BF16: np.uint16, I8_ROWWISE: np.int8}[dtype]
+  out = np.zeros((n, dim), dtype=vdt)
+  scale = bias = None
+  if dtype == I8_ROWWISE:
+    scale = np.zeros(n, dtype=np.float32)
+    bias = np.zeros(n, dtype=np.float32)
+  lib.oracle_synth_rows_at(dtype, seed, table, _p(rows), n, dim, _p(out),
+                           _p(scale), _p(bias))
+  return out, scale, bias
+
+
+def synth_lengths(n, lo, hi, seed, table):
+  out = np.zeros(n, dtype=np.int64)
+  lib.oracle_synth_lengths(n, lo, hi, seed, table, _p(out))
+  return out
+
+
+def synth_weights(n, seed, table, index0=0):
+  out = np.zeros(n, dtype=np.float32)
+  lib.oracle_synth_weights(n, seed, table, index0, _p(out))
+  return out
+
+
+def synth_ids(n, vocab, seed, table, alpha=0.0, perm_mul=1, perm_add=0,
+              index0=0):
+  out = np.zeros(n, dtype=np.int64)
+  lib.oracle_synth_ids(n, vocab, float(alpha), perm_mul, perm_add, seed,
+                       table, index0, _p(out))
+  return out
+
+
+def compare_pooled(got, want, bound=None, rtol=1e-5):
+  """Pooled rows against the oracle's: bit for bit when `bound` is None,
+  else |got - want| <= rtol * bound per element (the condition-aware bound
+  of int8 row-wise tables). Returns a summary dict."""
+  got = np.asarray(got, dtype=np.float32)
+  want = np.asarray(want, dtype=np.float32)
+  same = (got.view(np.uint32) == want.view(np.uint32)) | (
+      np.isnan(got) & np.isnan(want))
+  err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+  scale = np.maximum(np.abs(want.astype(np.float64)), 1e-30)
+  out = {"elements": int(got.size), "bit_exact": bool(same.all()),
+         "mismatched": int((~same).sum()),
+         "max_abs_err": float(err.max()) if err.size else 0.0,
+         "max_rel_err": float((err / scale).max()) if err.size else 0.0}
+  if bound is None:
+    out["ok"] = out["bit_exact"]
+    out["rule"] = "bit-exact"
+  else:
+    lim = rtol * np.asarray(bound, dtype=np.float64)
+    out["ok"] = bool((err <= lim).all())
+    out["rule"] = f"|err| <= {rtol:g} x sum|w|(|q|s + |b|)"
+  return out
+
+
+def sampled_bags(num_bags, count, seed, lengths=None):
+  """Bag indices to check: the first and last bags, the longest (when
+  `lengths` is given) and a seeded random sample, sorted, without
+  repeats."""
+  rng = np.random.default_rng(seed)
+  pick = set(rng.choice(num_bags, size=min(count, num_bags), replace=False)
+             .tolist())
+  pick.update({0, num_bags - 1})
+  if lengths is not None and len(lengths):
+    pick.add(int(np.argmax(lengths)))
+  return np.array(sorted(pick), dtype=np.int64)
+
+
+def pool_sampled(dtype, seed, table, dim, combine, ids, offsets, weights,
+                 bags, window=None, num_threads=4):
+  """The oracle's pooled rows for bags `bags` of one request (ids, offsets
+  and weights as numpy arrays over the whole batch, offsets absolute),
+  with the touched rows regenerated from the counter RNG instead of
+  materialising the table. `window` (row_begin, row_end): a row-wise shard;
+  ids outside it contribute nothing, while bag lengths and weight sums count
+  every id. Returns (rows [len(bags), dim], bound or None)."""
+  offsets = np.asarray(offsets, dtype=np.int64)
+  starts, ends = offsets[bags], offsets[bags + 1]
+  pos = np.concatenate([np.arange(a, b, dtype=np.int64)
+                        for a, b in zip(starts, ends)] or
+                       [np.zeros(0, np.int64)])
+  sub_ids = np.asarray(ids, dtype=np.int64)[pos]
+  sub_w = None if weights is None else np.asarray(weights, np.float32)[pos]
+  sub_off = np.concatenate([[0], np.cumsum(ends - starts)]).astype(np.int64)
+  uniq, local = np.unique(sub_ids, return_inverse=True)
+  vals, scale, bias = synth_rows_at(dtype, seed, table, uniq, dim)
+  if window is not None:
+    outside = (uniq < window[0]) | (uniq >= window[1])
+    vals[outside] = 0
+    if scale is not None:
+      scale[outside] = 0.0
+      bias[outside] = 0.0
+  want = embedding_bag(vals, local, sub_off, sub_w, combine, dtype, scale,
+                       bias, num_threads=num_threads)
+  bound = None
+  if dtype == I8_ROWWISE:
+    bound = embedding_bag(np.abs(vals.astype(np.int16)).astype(np.int8),
+                          local, sub_off,
+                          None if sub_w is None else np.abs(sub_w), combine,
+                          dtype, np.abs(scale), np.abs(bias),
+                          num_threads=num_threads)
+  return want, bound

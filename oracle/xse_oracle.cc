@@ -83,9 +83,13 @@ float RowValue(const oracle_request& r, int64_t id, int64_t c) {
     case ORACLE_BF16:
       return Bf16ToFloat(static_cast<const uint16_t*>(r.table)[at]);
     default: {
-      // Row-wise dequantisation q * scale + bias with one rounding.
+      // Row-wise dequantisation to an fp32 row, then the fp32 bag: the
+      // product float(q) * scale and the sum with bias are rounded
+      // separately (the file is compiled with -ffp-contract=off, so neither
+      // expression becomes an fma).
       const float q = static_cast<float>(static_cast<const int8_t*>(r.table)[at]);
-      return std::fmaf(q, r.scale[id], r.bias[id]);
+      const float scaled = q * r.scale[id];
+      return scaled + r.bias[id];
     }
   }
 }
@@ -751,6 +755,65 @@ void oracle_synth_rows_i8(uint64_t seed, uint64_t table, int64_t row0,
     const float b_scaled = 0.2f * ub;
     scale[r] = 1e-3f + s_scaled;
     bias[r] = -0.1f + b_scaled;
+  }
+}
+
+void oracle_synth_rows_at(int32_t dtype, uint64_t seed, uint64_t table,
+                          const int64_t* rows, int64_t n, int64_t dim,
+                          void* out, float* scale, float* bias) {
+  // Row by row through the contiguous generators: the value of (row, c)
+  // depends only on the row index, so any subset of rows can be rebuilt.
+  for (int64_t i = 0; i < n; ++i) {
+    if (dtype == ORACLE_F32) {
+      oracle_synth_rows_f32(seed, table, rows[i], 1, dim,
+                            static_cast<float*>(out) + i * dim);
+    } else if (dtype == ORACLE_BF16) {
+      oracle_synth_rows_bf16(seed, table, rows[i], 1, dim,
+                             static_cast<uint16_t*>(out) + i * dim);
+    } else {
+      oracle_synth_rows_i8(seed, table, rows[i], 1, dim,
+                           static_cast<int8_t*>(out) + i * dim, scale + i,
+                           bias + i);
+    }
+  }
+}
+
+void oracle_synth_lengths(int64_t n, int32_t lo, int32_t hi, uint64_t seed,
+                          uint64_t table, int64_t* out) {
+  // u24 scaled to the span by a 24-bit fixed-point multiply.
+  const uint64_t span = static_cast<uint64_t>(hi - lo + 1);
+  for (int64_t i = 0; i < n; ++i) {
+    const uint64_t u24 =
+        Bits64(seed, StreamOf(table, kLengths), static_cast<uint64_t>(i)) >> 40;
+    out[i] = lo + static_cast<int64_t>((u24 * span) >> 24);
+  }
+}
+
+void oracle_synth_weights(int64_t n, uint64_t seed, uint64_t table,
+                          int64_t index0, float* out) {
+  for (int64_t i = 0; i < n; ++i) {
+    out[i] = Uniform24(seed, StreamOf(table, kWeights),
+                       static_cast<uint64_t>(index0 + i));
+  }
+}
+
+void oracle_synth_ids(int64_t n, int64_t vocab, double alpha,
+                      uint64_t perm_mul, uint64_t perm_add, uint64_t seed,
+                      uint64_t table, int64_t index0, int64_t* out) {
+  const uint64_t uv = static_cast<uint64_t>(vocab);
+  const uint64_t stream = StreamOf(table, kIds);
+  for (int64_t i = 0; i < n; ++i) {
+    const uint64_t index = static_cast<uint64_t>(index0 + i);
+    if (alpha <= 0.0) {
+      // Uniform: the high 64 bits of bits * vocab.
+      const unsigned __int128 wide =
+          static_cast<unsigned __int128>(Bits64(seed, stream, index)) * uv;
+      out[i] = static_cast<int64_t>(wide >> 64);
+    } else {
+      const int64_t k = oracle_zipf_rank(seed, stream, index, vocab, alpha);
+      out[i] = static_cast<int64_t>(
+          (static_cast<uint64_t>(k - 1) * perm_mul + perm_add) % uv);
+    }
   }
 }
 

@@ -119,6 +119,23 @@ void oracle_synth_rows_bf16(uint64_t seed, uint64_t table, int64_t row0,
 void oracle_synth_rows_i8(uint64_t seed, uint64_t table, int64_t row0,
                           int64_t nrows, int64_t dim, int8_t* q, float* scale,
                           float* bias);
+/* Rows rows[0..n) of a synthetic table (any order, repeats allowed): out is
+ * [n, dim] in the table's storage type; int8 tables also fill scale[n] and
+ * bias[n]. */
+void oracle_synth_rows_at(int32_t dtype, uint64_t seed, uint64_t table,
+                          const int64_t* rows, int64_t n, int64_t dim,
+                          void* out, float* scale, float* bias);
+/* Bag lengths uniform in [lo, hi], per-id weights U(0,1) and ids (uniform
+ * when alpha <= 0, else bounded Zipf(alpha) ranks mapped to rows by
+ * ((rank - 1) * perm_mul + perm_add) mod vocab), as the device generates
+ * them for the same (seed, table) stream. */
+void oracle_synth_lengths(int64_t n, int32_t lo, int32_t hi, uint64_t seed,
+                          uint64_t table, int64_t* out);
+void oracle_synth_weights(int64_t n, uint64_t seed, uint64_t table,
+                          int64_t index0, float* out);
+void oracle_synth_ids(int64_t n, int64_t vocab, double alpha,
+                      uint64_t perm_mul, uint64_t perm_add, uint64_t seed,
+                      uint64_t table, int64_t index0, int64_t* out);
 /* Bounded Zipf(alpha) rank in [1, n] by rejection-inversion. */
 int64_t oracle_zipf_rank(uint64_t seed, uint64_t stream, uint64_t index,
                          int64_t n, double alpha);

@@ -50,6 +50,60 @@ def oracle_pool(host_table, dtype, ids, offsets, weights, combine, scale=None,
                               dtype, scale, bias, num_threads=4)
 
 
+# Int8 row-wise tables: the oracle states the dequantization as an fp32 row
+# (float(q) * scale rounded, then + bias rounded) pooled in fp32; the kernel
+# dequantizes each element with one fma (one rounding). Results are compared
+# within INT8_RTOL of the condition-aware bound sum_i |w_i| (|q_i| s_i +
+# |b_i|) per output element (the same bag pooled over absolute values), so a
+# sum that cancels to near zero is not held to a relative bound it cannot
+# meet. Both roundings are within 2^-24 of that bound per term.
+INT8_RTOL = 1e-5
+
+
+def int8_bound(host_table, ids, offsets, weights, combine, scale, bias):
+  """sum |w| (|q| scale + |bias|) per output element, with the bag's mean or
+  sqrt-n factor (computed by the oracle over absolute values)."""
+  return oracle.embedding_bag(
+      np.abs(host_table.astype(np.int16)).astype(np.int8), ids, offsets,
+      None if weights is None else np.abs(weights), combine,
+      oracle.I8_ROWWISE, np.abs(scale), np.abs(bias), num_threads=4)
+
+
+def expect_pool(host_table, dtype, ids, offsets, weights, combine, scale=None,
+                bias=None):
+  """The oracle's pooled output, and for int8 tables the bound that the
+  comparison scales its tolerance by (None: bit-exact)."""
+  want = oracle_pool(host_table, dtype, ids, offsets, weights, combine, scale,
+                     bias)
+  bound = None
+  if dtype == oracle.I8_ROWWISE:
+    bound = int8_bound(host_table, ids, offsets, weights, combine, scale,
+                       bias)
+  return want, bound
+
+
+def assert_pooled(got, expected, what=""):
+  """Compares with expect_pool's result: bit for bit, or for int8 tables
+  |got - want| <= INT8_RTOL * bound."""
+  want, bound = expected
+  if bound is None:
+    assert_bitwise(got, want, what)
+    return
+  got = np.asarray(got, dtype=np.float64)
+  want = np.asarray(want, dtype=np.float64)
+  assert got.shape == want.shape, (what, got.shape, want.shape)
+  err = np.abs(got - want)
+  lim = INT8_RTOL * np.asarray(bound, dtype=np.float64)
+  bad = err > lim
+  if bad.any():
+    idx = np.argwhere(bad)[:5]
+    k = tuple(idx[0])
+    raise AssertionError(
+        f"{what}: {int(bad.sum())} of {got.size} beyond {INT8_RTOL} x bound, "
+        f"first at {idx.tolist()}: got {got[k]} want {want[k]} bound "
+        f"{bound[k]}; max abs err {err.max():.3g}")
+
+
 def assert_bitwise(got, want, what=""):
   got = np.asarray(got, dtype=np.float32)
   want = np.asarray(want, dtype=np.float32)

@@ -8,7 +8,8 @@ import pytest
 import torch
 
 from oracle import oracle
-from parity_helpers import (TORCH_DT, assert_bitwise, oracle_pool,
+from parity_helpers import (TORCH_DT, assert_bitwise, assert_pooled,
+                            expect_pool, oracle_pool,
                             random_csr, random_table, to_dev)
 
 pytestmark = pytest.mark.gpu
@@ -129,14 +130,14 @@ def test_random_parity(xse, dtype, dim, combine):
         for id_dt in (torch.int32, torch.int64):
           got = eng.pool("f", to_dev(ids, id_dt), to_dev(offsets.astype(off_dt)),
                          None if w is None else to_dev(w))
-          want = oracle_pool(host, dtype, ids, offsets.astype(off_dt), w,
+          want = expect_pool(host, dtype, ids, offsets.astype(off_dt), w,
                              combine, scale, bias)
-          assert_bitwise(got.cpu().numpy(), want,
+          assert_pooled(got.cpu().numpy(), want,
                          f"dtype={dtype} dim={dim} {combine} w={weighted} "
                          f"first={first}")
       got_fused = eng.pool("f", to_dev(ids), to_dev(offsets),
                            None if w is None else to_dev(w), fused=True)
-      assert_bitwise(got_fused.cpu().numpy(), want, "fused")
+      assert_pooled(got_fused.cpu().numpy(), want, "fused")
   eng.close()
 
 
@@ -162,11 +163,11 @@ def test_strided_output_and_mixed_group(xse):
                                pooled[:, k, :], None if w is None else to_dev(w),
                                output_stride=len(specs) * 128))
     host, s, b = hosts[k]
-    want.append(oracle_pool(host, dt, ids, offsets, w, comb, s, b))
+    want.append(expect_pool(host, dt, ids, offsets, w, comb, s, b))
   eng.execute_batch(reqs)
   got = pooled.cpu().numpy()
   for k in range(len(specs)):
-    assert_bitwise(got[:, k, :], want[k], f"table {k}")
+    assert_pooled(got[:, k, :], want[k], f"table {k}")
   # Interleaved column blocks are disjoint; overlapping ones are rejected
   # before anything is written.
   before = pooled.clone()
@@ -463,8 +464,8 @@ def test_output_alignment_variants(xse, dtype, dim, shift):
   out = buf[shift:shift + batch * stride].view(batch, stride)[:, :dim]
   eng.execute_batch([xse.BagRequest("f", to_dev(ids), to_dev(offsets), out,
                                     to_dev(w), output_stride=stride)])
-  want = oracle_pool(host, dtype, ids, offsets, w, "MEAN", s, b)
-  assert_bitwise(out.cpu().numpy(), want, f"shift {shift}")
+  want = expect_pool(host, dtype, ids, offsets, w, "MEAN", s, b)
+  assert_pooled(out.cpu().numpy(), want, f"shift {shift}")
   rest = buf.clone()
   rest[shift:shift + batch * stride].view(batch, stride)[:, :dim] = -3.0
   assert torch.all(rest == -3.0)

@@ -11,6 +11,7 @@ import numpy as np
 import pytest
 
 from oracle import oracle
+from parity_helpers import assert_pooled, expect_pool
 
 pytestmark = pytest.mark.gpu
 
@@ -283,13 +284,12 @@ def test_resource_assets_and_errors(ops, xse, tmp_path):
   w = rng.uniform(0, 1, 37).astype(np.float32)
   outs = t(ids, [rp] * 3, [w, np.zeros(0, np.float32), w])
   want = [
-      oracle.embedding_bag(f32, ids[0], rp, w, "SQRT_N"),
-      oracle.embedding_bag(bits, ids[1], rp, None, "SUM", oracle.BF16),
-      oracle.embedding_bag(q, ids[2], rp, w, "MEAN", oracle.I8_ROWWISE, sc,
-                           bi),
+      expect_pool(f32, oracle.F32, ids[0], rp, w, "SQRT_N"),
+      expect_pool(bits, oracle.BF16, ids[1], rp, None, "SUM"),
+      expect_pool(q, oracle.I8_ROWWISE, ids[2], rp, w, "MEAN", sc, bi),
   ]
-  for got, exp in zip(outs, want):
-    np.testing.assert_array_equal(got.view(np.uint32), exp.view(np.uint32))
+  for k, (got, exp) in enumerate(zip(outs, want)):
+    assert_pooled(got, exp, f"feature {k}")
 
   # Asset errors.
   manifest = tmp_path / "manifest.textproto"

@@ -166,10 +166,11 @@ def test_int8_and_bf16_widening():
   offsets = np.array([0, 10, 10, 25, 40], dtype=np.int64)
   got = oracle.embedding_bag(q, ids, offsets, dtype=oracle.I8_ROWWISE,
                              scale=scale, bias=bias)
-  # fma(q, scale, bias): the float64 value q*scale + bias is exact here
-  # (8 + 24 significant bits, exponents close), so one rounding to fp32.
-  deq = (q.astype(np.float64) * scale[:, None].astype(np.float64) +
-         bias[:, None].astype(np.float64)).astype(np.float32)
+  # Dequantized to an fp32 row first: float(q) * scale rounded to fp32,
+  # then + bias rounded to fp32 (numpy float32 arithmetic rounds each
+  # operation), then the fp32 bag.
+  deq = (q.astype(np.float32) * scale[:, None]) + bias[:, None]
+  assert deq.dtype == np.float32
   want = np.zeros_like(got)
   for b in range(4):
     for p in range(offsets[b], offsets[b + 1]):

@@ -1578,44 +1578,56 @@ extern "C" int xse_engine_execute_batch_noalloc(xse_engine* engine,
   int code = NoAllocScratch(engine->device, &scratch);
   if (code != XSE_OK) return code;
 
-  // Host checks (PrepareRequest, embedding_bag.cc:235-251) and descriptors.
+  // Host checks (PrepareRequest, embedding_bag.cc:235-251), kept per request
+  // in stack arrays: a request's host-detectable error is reported only when
+  // every earlier request has passed its device checks, as
+  // xse_engine_execute_batch (and the reference's per-request loop,
+  // embedding_bag.cc:493-497) order them.
   xse::PoolParams params{};  // kernel parameter block (~9 KB, on the stack)
   xse::BagDesc* descs = params.d;
+  int32_t nd = 0;
+  int8_t stage[kNoAllocMaxRequests] = {};
+  const char* problem[kNoAllocMaxRequests] = {};
+  bool any_early = false, any_soft = false;
   for (int32_t i = 0; i < n; ++i) {
     const xse_bag_request& r = reqs[i];
     const Table& t = *tables[i];
     if (r.output == nullptr) {
-      return SetError(XSE_INVALID_ARGUMENT,
-                      "FP32 embedding-bag request %d requires an output "
-                      "allocator.",
-                      i);
-    }
-    const char* problem = nullptr;
-    if ((r.ids_type != XSE_INDEX_I32 && r.ids_type != XSE_INDEX_I64) ||
-        (r.offsets_type != XSE_INDEX_I32 && r.offsets_type != XSE_INDEX_I64)) {
-      problem = "Embedding IDs and row pointers must be int32 or int64.";
+      stage[i] = kStageEarly;  // unprefixed message, formatted below
+    } else if ((r.ids_type != XSE_INDEX_I32 && r.ids_type != XSE_INDEX_I64) ||
+               (r.offsets_type != XSE_INDEX_I32 &&
+                r.offsets_type != XSE_INDEX_I64)) {
+      stage[i] = kStageEarly;
+      problem[i] = "Embedding IDs and row pointers must be int32 or int64.";
     } else if (r.num_offsets < 2 || r.offsets == nullptr) {
-      problem = "Row pointers must contain at least two elements.";
+      stage[i] = kStageEarly;
+      problem[i] = "Row pointers must contain at least two elements.";
     } else if (r.num_ids < 0 || r.num_weights < 0 ||
                (r.output_stride != 0 && r.output_stride < t.dim)) {
-      problem =
+      stage[i] = kStageEarly;
+      problem[i] =
           "Request sizes must be non-negative and the output stride at least "
           "the embedding dimension.";
     } else if (r.ids == nullptr && r.num_ids > 0) {
-      problem = "Embedding-ID storage must be non-null.";
+      stage[i] = kStageIdsNull;
+      problem[i] = "Embedding-ID storage must be non-null.";
     } else if (r.weights == nullptr && r.num_weights > 0) {
-      problem = "Weight storage must be non-null.";
+      stage[i] = kStageWeightsNull;
+      problem[i] = "Weight storage must be non-null.";
     }
-    if (problem != nullptr) {
-      return SetError(XSE_INVALID_ARGUMENT, "FP32 embedding-bag request %d: %s",
-                      i, problem);
+    if (stage[i] != kStageNone) any_soft = true;
+    if (stage[i] == kStageEarly) {
+      any_early = true;
+      continue;
     }
     xse::BagDesc d{};
     d.rows = t.rows;
     d.scale_bias = t.scale_bias;
-    d.ids = r.ids;
+    d.ids = stage[i] == kStageIdsNull ? nullptr : r.ids;
     d.offsets = r.offsets;
-    d.weights = r.num_weights > 0 ? r.weights : nullptr;
+    d.weights = (r.num_weights > 0 && stage[i] != kStageWeightsNull)
+                    ? r.weights
+                    : nullptr;
     d.out = r.output;
     d.out_stride = r.output_stride > 0 ? r.output_stride : t.dim;
     d.vocab = t.vocab;
@@ -1632,50 +1644,88 @@ extern "C" int xse_engine_execute_batch_noalloc(xse_engine* engine,
     d.vec_out = static_cast<int8_t>(
         (reinterpret_cast<uintptr_t>(r.output) & 15u) == 0 &&
         d.out_stride % 4 == 0);
-    descs[i] = d;
+    descs[nd++] = d;
   }
+  auto early_error = [&](int32_t i) {
+    if (problem[i] == nullptr) {
+      return SetError(XSE_INVALID_ARGUMENT,
+                      "FP32 embedding-bag request %d requires an output "
+                      "allocator.",
+                      i);
+    }
+    return SetError(XSE_INVALID_ARGUMENT, "FP32 embedding-bag request %d: %s",
+                    i, problem[i]);
+  };
+  // Request 0's early error wins outright: no earlier request can fail.
+  if (stage[0] == kStageEarly) return early_error(0);
 
-  // Output isolation (embedding_bag.cc:304-351) on fixed arrays.
-  Range outputs[kNoAllocMaxRequests];
-  Range inputs[kNoAllocMaxRequests * 4];
-  int32_t n_out = 0, n_in = 0;
-  for (int32_t i = 0; i < n; ++i) {
-    const xse::BagDesc& d = descs[i];
-    const Table& t = *tables[i];
-    if (d.num_bags > 0) {
-      outputs[n_out++] = {static_cast<int64_t>(reinterpret_cast<uintptr_t>(d.out)),
-                          d.out_stride * 4, static_cast<int64_t>(t.dim) * 4,
-                          d.num_bags, i, "output"};
-    }
-    auto add = [&](const void* p, int64_t bytes, const char* kind) {
-      if (p != nullptr && bytes > 0) {
-        inputs[n_in++] = {static_cast<int64_t>(reinterpret_cast<uintptr_t>(p)),
-                          bytes, bytes, 1, i, kind};
+  // Output isolation (embedding_bag.cc:304-351) on fixed arrays, with the
+  // outputs visited in address order as CheckIsolation visits them. Checked
+  // only when no request failed its early checks (as the regular call); an
+  // isolation error is reported after every request's own errors.
+  char iso_message[256];
+  bool iso_failed = false;
+  if (!any_early) {
+    Range outputs[kNoAllocMaxRequests];
+    Range inputs[kNoAllocMaxRequests * 4];
+    int32_t n_out = 0, n_in = 0;
+    for (int32_t i = 0; i < n; ++i) {
+      const xse_bag_request& r = reqs[i];
+      const Table& t = *tables[i];
+      const int64_t bags = r.num_offsets - 1;
+      const int64_t stride = r.output_stride > 0 ? r.output_stride : t.dim;
+      if (bags > 0 && r.output != nullptr) {
+        Range o{static_cast<int64_t>(reinterpret_cast<uintptr_t>(r.output)),
+                stride * 4, static_cast<int64_t>(t.dim) * 4, bags, i,
+                "output"};
+        int32_t k = n_out++;  // insertion by base address
+        while (k > 0 && outputs[k - 1].base > o.base) {
+          outputs[k] = outputs[k - 1];
+          --k;
+        }
+        outputs[k] = o;
       }
-    };
-    add(d.ids, d.num_ids * (d.ids64 ? 8 : 4), "embedding-ID");
-    add(d.offsets, (d.num_bags + 1) * (d.offs64 ? 8 : 4), "row-pointer");
-    add(d.weights, d.num_weights * 4, "weight");
-    add(t.rows,
-        (t.row_end - t.row_begin) * t.dim *
-            static_cast<int64_t>(ElemBytes(t.dtype)),
-        "embedding-table");
-  }
-  for (int32_t a = 0; a < n_out; ++a) {
-    for (int32_t b = a + 1; b < n_out; ++b) {
-      if (Overlaps(outputs[a], outputs[b])) {
-        return SetError(XSE_INVALID_ARGUMENT,
-                        "FP32 embedding-bag request outputs %d and %d "
-                        "overlap.",
-                        outputs[a].request, outputs[b].request);
+      auto add = [&](const void* p, int64_t bytes, const char* kind) {
+        if (p != nullptr && bytes > 0) {
+          inputs[n_in++] = {
+              static_cast<int64_t>(reinterpret_cast<uintptr_t>(p)), bytes,
+              bytes, 1, i, kind};
+        }
+      };
+      add(r.ids, r.num_ids * (r.ids_type == XSE_INDEX_I64 ? 8 : 4),
+          "embedding-ID");
+      add(r.offsets, r.num_offsets * (r.offsets_type == XSE_INDEX_I64 ? 8 : 4),
+          "row-pointer");
+      add(r.weights, r.num_weights * 4, "weight");
+      add(t.rows,
+          (t.row_end - t.row_begin) * t.dim *
+              static_cast<int64_t>(ElemBytes(t.dtype)),
+          "embedding-table");
+    }
+    for (int32_t a = 0; a < n_out && !iso_failed; ++a) {
+      for (int32_t b = a + 1; b < n_out && outputs[b].base < outputs[a].end();
+           ++b) {
+        if (Overlaps(outputs[a], outputs[b])) {
+          snprintf(iso_message, sizeof(iso_message),
+                   "FP32 embedding-bag request outputs %d and %d overlap.",
+                   std::min(outputs[a].request, outputs[b].request),
+                   std::max(outputs[a].request, outputs[b].request));
+          iso_failed = true;
+          break;
+        }
       }
     }
-    for (int32_t b = 0; b < n_in; ++b) {
-      if (Overlaps(outputs[a], inputs[b])) {
-        return SetError(XSE_INVALID_ARGUMENT,
-                        "FP32 embedding-bag request %d output overlaps "
-                        "request %d %s storage.",
-                        outputs[a].request, inputs[b].request, inputs[b].kind);
+    // Of the inputs an output meets, the first in request order is named.
+    for (int32_t a = 0; a < n_out && !iso_failed; ++a) {
+      for (int32_t b = 0; b < n_in; ++b) {
+        if (Overlaps(outputs[a], inputs[b])) {
+          snprintf(iso_message, sizeof(iso_message),
+                   "FP32 embedding-bag request %d output overlaps request %d "
+                   "%s storage.",
+                   outputs[a].request, inputs[b].request, inputs[b].kind);
+          iso_failed = true;
+          break;
+        }
       }
     }
   }
@@ -1685,63 +1735,67 @@ extern "C" int xse_engine_execute_batch_noalloc(xse_engine* engine,
   if (e != cudaSuccess) return CudaError(e, "scratch reset");
   int launches = 0;
   {
+    // The validation pass runs even when the group is known to fail, so
+    // that an earlier request's device-detected error is the one reported.
     int64_t work = 0;
-    for (int32_t i = 0; i < n; ++i) {
-      descs[i].work_begin = work;
-      work += xse::ValidationWork(descs[i].num_bags, descs[i].num_ids);
+    for (int32_t k = 0; k < nd; ++k) {
+      descs[k].work_begin = work;
+      work += xse::ValidationWork(descs[k].num_bags, descs[k].num_ids);
     }
-    params.n = n;
+    params.n = nd;
     params.fused_checks = 0;
     params.status = scratch;
     e = xse::LaunchValidate(params, work, s);
     if (e != cudaSuccess) return CudaError(e, "validation launch");
     ++launches;
   }
-  // One pooling launch per kernel layout, requests kept in order.
-  xse::PoolParams group{};
-  bool launched[kNoAllocMaxRequests] = {};
-  for (int32_t i = 0; i < n; ++i) {
-    if (launched[i]) continue;
-    xse::Layout li = xse::ChooseLayout(tables[i]->dtype, descs[i].dim,
-                                       descs[i].rows);
-    if (tables[i]->dtype == XSE_DT_I8_ROWWISE &&
-        descs[i].scale_bias == nullptr) {
-      li.v = 0;
-      li.exact = false;
-    }
-    li.wmode = li.v == 0 ? 0 : xse::WeightModeOf(descs[i]);
-    group.n = 0;
-    group.fused_checks = 0;
-    group.status = scratch;
-    int64_t tasks = 0;
-    for (int32_t j = i; j < n; ++j) {
-      if (launched[j]) continue;
-      xse::Layout lj = xse::ChooseLayout(tables[j]->dtype, descs[j].dim,
-                                         descs[j].rows);
-      if (tables[j]->dtype == XSE_DT_I8_ROWWISE &&
-          descs[j].scale_bias == nullptr) {
-        lj.v = 0;
-        lj.exact = false;
+  if (!any_soft && !iso_failed) {
+    // One pooling launch per kernel layout, requests kept in order.
+    xse::PoolParams group{};
+    bool launched[kNoAllocMaxRequests] = {};
+    for (int32_t i = 0; i < nd; ++i) {
+      if (launched[i]) continue;
+      const Table& ti = *tables[descs[i].slot];
+      xse::Layout li = xse::ChooseLayout(ti.dtype, descs[i].dim, descs[i].rows);
+      if (ti.dtype == XSE_DT_I8_ROWWISE && descs[i].scale_bias == nullptr) {
+        li.v = 0;
+        li.exact = false;
       }
-      lj.wmode = lj.v == 0 ? 0 : xse::WeightModeOf(descs[j]);
-      if (lj.dtype != li.dtype || lj.g != li.g || lj.v != li.v ||
-          lj.exact != li.exact) {
-        continue;  // weighting modes share a launch
+      li.wmode = li.v == 0 ? 0 : xse::WeightModeOf(descs[i]);
+      group.n = 0;
+      group.fused_checks = 0;
+      group.status = scratch;
+      int64_t tasks = 0;
+      for (int32_t j = i; j < nd; ++j) {
+        if (launched[j]) continue;
+        const Table& tj = *tables[descs[j].slot];
+        xse::Layout lj =
+            xse::ChooseLayout(tj.dtype, descs[j].dim, descs[j].rows);
+        if (tj.dtype == XSE_DT_I8_ROWWISE && descs[j].scale_bias == nullptr) {
+          lj.v = 0;
+          lj.exact = false;
+        }
+        lj.wmode = lj.v == 0 ? 0 : xse::WeightModeOf(descs[j]);
+        if (lj.dtype != li.dtype || lj.g != li.g || lj.v != li.v ||
+            lj.exact != li.exact) {
+          continue;  // weighting modes share a launch
+        }
+        launched[j] = true;
+        group.d[group.n] = descs[j];
+        group.d[group.n].task_begin = tasks;
+        tasks += descs[j].num_bags;
+        ++group.n;
       }
-      launched[j] = true;
-      group.d[group.n] = descs[j];
-      group.d[group.n].task_begin = tasks;
-      tasks += descs[j].num_bags;
-      ++group.n;
+      group.total_tasks = tasks;
+      e = xse::LaunchPool(li, group, s, &launches);
+      if (e != cudaSuccess) return CudaError(e, "pooling launch");
     }
-    group.total_tasks = tasks;
-    e = xse::LaunchPool(li, group, s, &launches);
-    if (e != cudaSuccess) return CudaError(e, "pooling launch");
   }
   g_last_launches = launches;
 
   // Read back this call's status into stack memory and resolve it in the
-  // reference's order of checks.
+  // reference's order of checks: per request, its early error, its offset
+  // errors, its null ids or weights, its out-of-range ids; then isolation.
   alignas(16) unsigned char host_buf[kNoAllocStatusBytes];
   e = cudaMemcpyAsync(host_buf, scratch, xse::DevStatusBytes(n),
                       cudaMemcpyDeviceToHost, s);
@@ -1749,6 +1803,7 @@ extern "C" int xse_engine_execute_batch_noalloc(xse_engine* engine,
   if (e != cudaSuccess) return CudaError(e, "scratch read-back");
   const xse::DevStatus* st = reinterpret_cast<const xse::DevStatus*>(host_buf);
   for (int32_t i = 0; i < n; ++i) {
+    if (stage[i] == kStageEarly) return early_error(i);
     const unsigned int flags = st->req[i].flags;
     const char* msg = nullptr;
     if (flags & xse::kErrBadOffsets) {
@@ -1762,16 +1817,21 @@ extern "C" int xse_engine_execute_batch_noalloc(xse_engine* engine,
       return SetError(XSE_INVALID_ARGUMENT, "FP32 embedding-bag request %d: %s",
                       i, msg);
     }
+    if (stage[i] == kStageIdsNull || stage[i] == kStageWeightsNull) {
+      return SetError(XSE_INVALID_ARGUMENT, "FP32 embedding-bag request %d: %s",
+                      i, problem[i]);
+    }
     if (flags & xse::kErrBadId) {
       const int64_t index = static_cast<int64_t>(~st->req[i].inv_min_bad_index);
+      const bool ids64 = reqs[i].ids_type == XSE_INDEX_I64;
       int64_t id = 0;
-      if (descs[i].ids64) {
-        e = cudaMemcpy(&id, static_cast<const int64_t*>(descs[i].ids) + index,
+      if (ids64) {
+        e = cudaMemcpy(&id, static_cast<const int64_t*>(reqs[i].ids) + index,
                        sizeof(id), cudaMemcpyDeviceToHost);
       } else {
         int32_t id32 = 0;
         e = cudaMemcpy(&id32,
-                       static_cast<const int32_t*>(descs[i].ids) + index,
+                       static_cast<const int32_t*>(reqs[i].ids) + index,
                        sizeof(id32), cudaMemcpyDeviceToHost);
         id = id32;
       }
@@ -1783,6 +1843,7 @@ extern "C" int xse_engine_execute_batch_noalloc(xse_engine* engine,
                       i, id, index, tables[i]->vocab);
     }
   }
+  if (iso_failed) return SetError(XSE_INVALID_ARGUMENT, "%s", iso_message);
   return Ok();
 }
 
