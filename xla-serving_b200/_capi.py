@@ -259,6 +259,39 @@ SIGNATURES.update({
     "xse_csr_pack": (_I, [ctypes.POINTER(CsrSegment), _I32, _P]),
 })
 
+# Sharded execution (include/xse_shard.h).
+SHARD_ID_BYTES = 128
+SHARD_TABLE_PEER, SHARD_TABLE_A2A, SHARD_TABLE_PIPELINED, SHARD_ROW = 0, 1, 2, 3
+SHARD_DEFER_WAIT = 1
+
+
+class ShardPlanStruct(ctypes.Structure):
+  """xse_shard_plan (include/xse_shard.h)."""
+  _fields_ = [
+      ("mode", ctypes.c_int32),
+      ("num_tables", ctypes.c_int32),
+      ("dim", ctypes.c_int32),
+      ("chunks", ctypes.c_int32),
+      ("batch", ctypes.c_int64),
+      ("spin_limit", ctypes.c_int64),
+  ]
+
+
+SIGNATURES.update({
+    "xse_shard_unique_id": (_I, [ctypes.c_char_p]),
+    "xse_shard_comm_create": (_I, [_I32, _I32, _I32, ctypes.c_char_p, _P]),
+    "xse_shard_comm_adopt": (_I, [_P, _I32, _I32, _I32, _P]),
+    "xse_shard_comm_abort": (_I, [_P]),
+    "xse_shard_comm_destroy": (None, [_P]),
+    "xse_shard_exchange_create": (_I, [_P, _P, ctypes.POINTER(ShardPlanStruct),
+                                       _P]),
+    "xse_shard_exchange_run": (_I, [_P, ctypes.POINTER(BagRequest), _I32,
+                                    _I32, _P, _P]),
+    "xse_shard_exchange_ready": (_I, [_P, _P]),
+    "xse_shard_exchange_check": (_I, [_P, _P]),
+    "xse_shard_exchange_destroy": (None, [_P]),
+})
+
 
 def _load():
   if not os.path.exists(LIB_PATH):

@@ -181,6 +181,23 @@ class DenseTower:
     """The [B, width_stride] interaction rows the top MLP reads."""
     return self._buffers_for(batch)["inter"]
 
+  def bottom_output(self, batch):
+    """The bottom MLP's [B, dim] output buffer of the last forward."""
+    return self._buffers_for(batch)["bottom"][-1]
+
+  def interaction_rows(self, batch):
+    """The [B, width_stride] interaction rows of the last forward."""
+    return self.interaction_buffer(batch)
+
+  def interaction_bytes_per_row(self):
+    """Bytes of interaction output written per sample."""
+    return self.width_stride * 4
+
+  def split_launches(self, fused):
+    """Operand-split kernels one forward launches (one per split layer)."""
+    del fused
+    return len(self._split)
+
   def top_forward(self, inter, *, stream=None):
     """The top MLP over interaction rows -> predictions [B]."""
     bufs = self._buffers_for(inter.shape[0])

@@ -657,3 +657,112 @@ class RowwiseExchange:
     for work in works:
       work.wait()
     return self.recv
+
+
+# ---------------------------------------------------------------------------
+# The C ABI's sharded execution (include/xse_shard.h): the schedules above,
+# run by the engine's C++ host code over its own NCCL communicator.
+
+SHARD_MODES = {"peer": C.SHARD_TABLE_PEER, "a2a": C.SHARD_TABLE_A2A,
+               "pipelined": C.SHARD_TABLE_PIPELINED, "row": C.SHARD_ROW}
+
+
+class ShardComm:
+  """The engine's NCCL communicator over the ranks of `group` (the default
+  torch.distributed group): rank 0 draws the NCCL unique id through the C
+  ABI and the id reaches every rank over torch.distributed."""
+
+  def __init__(self, device: int, plan: ShardPlan, group=None):
+    self.plan = plan
+    self._handle = ctypes.c_void_p()
+    uid = ctypes.create_string_buffer(C.SHARD_ID_BYTES)
+    if plan.rank == 0:
+      C.check(C.lib.xse_shard_unique_id(uid))
+    if plan.world > 1:
+      box = [bytes(uid.raw)]
+      dist.broadcast_object_list(box, src=0, group=group)
+      uid = ctypes.create_string_buffer(box[0], C.SHARD_ID_BYTES)
+    C.check(C.lib.xse_shard_comm_create(device, plan.world, plan.rank, uid,
+                                        ctypes.byref(self._handle)))
+
+  @property
+  def handle(self):
+    return self._handle
+
+  def abort(self):
+    if self._handle:
+      C.check(C.lib.xse_shard_comm_abort(self._handle))
+
+  def close(self):
+    if self._handle:
+      C.lib.xse_shard_comm_destroy(self._handle)
+      self._handle = ctypes.c_void_p()
+
+
+class ShardedExchange:
+  """One sharded step per run() through xse_shard_exchange_run.
+
+  mode: "peer", "a2a", "pipelined" (table-wise: global table t on rank
+  t mod W; features are this rank's tables in local order) or "row"
+  (every table's rows split over the ranks; features are all tables).
+  features: (feature name, ids, offsets, weights) over the whole batch.
+  run() returns this rank's pooled rows [B/W, T, D] (sample-major, global
+  table order) as a view of the exchange's output slot, valid until the
+  next run().
+  """
+
+  def __init__(self, engine, comm: ShardComm, mode: str, num_tables: int,
+               dim: int, batch: int, chunks: int = 1, spin_limit: int = 0):
+    self.comm = comm
+    self.mode = mode
+    self.plan = comm.plan
+    self.num_tables = num_tables
+    self.dim = dim
+    self.batch = batch
+    self.block = self.plan.block_size(batch)
+    p = C.ShardPlanStruct(mode=SHARD_MODES[mode], num_tables=num_tables,
+                          dim=dim, chunks=chunks, batch=batch,
+                          spin_limit=spin_limit)
+    self._handle = ctypes.c_void_p()
+    C.check(C.lib.xse_shard_exchange_create(engine.handle, comm.handle,
+                                            ctypes.byref(p),
+                                            ctypes.byref(self._handle)))
+    self.recv = None
+    self._views = {}  # output slot address -> tensor view
+
+  def prepare(self, features: Sequence[CsrFeature]) -> PreparedBatch:
+    """The C request array of one step's features, built once."""
+    return PreparedBatch([BagRequest(name, ids, offsets, None, weights)
+                          for name, ids, offsets, weights in features])
+
+  def run(self, prepared, stream=None, defer=False) -> torch.Tensor:
+    if not isinstance(prepared, PreparedBatch):
+      prepared = self.prepare(prepared)
+    out = ctypes.c_void_p()
+    C.check(C.lib.xse_shard_exchange_run(
+        self._handle, prepared.array, len(prepared),
+        C.SHARD_DEFER_WAIT if defer else 0, stream_handle(stream),
+        ctypes.byref(out)))
+    view = self._views.get(out.value)
+    if view is None:
+      shape = (self.block, self.num_tables, self.dim)
+      view = torch.as_tensor(_CudaArray(out.value, shape), device="cuda")
+      self._views[out.value] = view
+    self.recv = view
+    return view
+
+  def ready(self, stream=None):
+    C.check(C.lib.xse_shard_exchange_ready(self._handle,
+                                           stream_handle(stream)))
+
+  def check(self, stream=None):
+    C.check(C.lib.xse_shard_exchange_check(self._handle,
+                                           stream_handle(stream)))
+
+  def close(self):
+    if self._handle:
+      torch.cuda.synchronize()
+      if self.plan.world > 1 and dist.is_initialized():
+        dist.barrier()  # every rank is done with the others' slots
+      C.lib.xse_shard_exchange_destroy(self._handle)
+      self._handle = ctypes.c_void_p()
