@@ -232,7 +232,8 @@ def timed_steps(step, first, count, world, local, finish=None):
   launches = 0
   start.record(stream)
   for i in range(first, first + count):
-    launches += step(i) or 0
+    r = step(i)
+    launches += r if isinstance(r, int) else 0
   if finish is not None:
     finish()
   end.record(stream)
@@ -514,11 +515,13 @@ class OperatorHostInputs:
     ids_l, rp_l, w_l = self.sets[0]
     self.h2d_bytes = sum(b.array.nbytes for b in ids_l + rp_l + w_l)
     self.d2h_bytes = batch * len(tables) * dim * 4
+    self.prepared = [ops.PreparedInputs(*bufs) for bufs in self.sets]
 
   def step(self, i, stream=None):
-    ids, rps, ws = self.sets[i % len(self.sets)]
-    for out in self.transform(ids, rps, ws, copy=False, stream=stream):
-      out.close()
+    prepared = self.prepared[i % len(self.prepared)]
+    outs = self.transform.output_array()
+    self.transform.run_prepared(prepared, outs, stream=stream)
+    self.transform.free_outputs(outs)
 
   def run(self, steps, threads):
     """`steps` synchronous transform calls spread over `threads` host
@@ -1359,11 +1362,13 @@ class DenseLookupHostInputs:
         self.sets.append(ids_l)
     self.h2d_bytes = sum(b.array.nbytes for b in self.sets[0])
     self.d2h_bytes = batch * len(REF_VOCAB) * REF_DIM * 4
+    self.prepared = [ops.PreparedInputs(ids_l) for ids_l in self.sets]
 
   def step(self, i, stream=None):
-    for out in self.transform(self.sets[i % len(self.sets)], copy=False,
-                              stream=stream):
-      out.close()
+    outs = self.transform.output_array()
+    self.transform.run_prepared(self.prepared[i % len(self.prepared)], outs,
+                                stream=stream)
+    self.transform.free_outputs(outs)
 
   run = OperatorHostInputs.run
 

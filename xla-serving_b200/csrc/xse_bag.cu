@@ -101,6 +101,12 @@ struct ElemsPerVec<2> {
 #define XSE_POOL_I8_MIN_BLOCKS 3
 #endif
 
+// 1: int8 rows of 256, 512 or 1024 bytes take the wide layout (32-byte
+// lanes); 0: 16-byte lanes like every other row type.
+#ifndef XSE_POOL_I8_WIDE
+#define XSE_POOL_I8_WIDE 1
+#endif
+
 // PoolStagedKernel: 0 never, 1 for launches small enough for one wave of
 // it, 2 for every launch whose rows it serves.
 #ifndef XSE_POOL_STAGED
@@ -112,18 +118,34 @@ struct ElemsPerVec<2> {
 #define XSE_PDL 1
 #endif
 
-// Rows gathered per batch (in flight per lane, times V vectors each).
-template <int DT, int V>
+// Wide int8 layouts (32-byte lanes): rows in flight per lane and resident
+// 256-thread blocks per SM. Measured on the int8 row-wise workload (26
+// tables 10M x 256, Zipf(1.05)), pooling per step: 2 rows at 3 blocks/SM
+// 2.86 ms (80 registers, some spilled), 2 at 2 blocks 2.91 ms, 3 at 3
+// blocks 3.44 ms; 16-byte lanes 3.07 ms.
+#ifndef XSE_POOL_I8W_ROWS
+#define XSE_POOL_I8W_ROWS 2
+#endif
+#ifndef XSE_POOL_I8W_MIN_BLOCKS
+#define XSE_POOL_I8W_MIN_BLOCKS 3
+#endif
+
+// Rows gathered per batch (in flight per lane, times V vectors each; a wide
+// lane's V vectors are one load).
+template <int DT, int V, bool WIDE = false>
 struct RowsInFlight {
   static constexpr int base = DT == 2 ? XSE_POOL_I8_ROWS : XSE_POOL_ROWS;
-  static constexpr int value = V >= base ? 1 : base / V;
+  static constexpr int value =
+      WIDE ? XSE_POOL_I8W_ROWS : (V >= base ? 1 : base / V);
 };
 
 // Resident blocks per SM each variant's register budget is sized for.
-template <int DT, int V>
+template <int DT, int V, bool WIDE = false>
 struct MinBlocks {
   static constexpr int value =
-      ElemsPerVec<DT>::value * V <= 16 && RowsInFlight<DT, V>::value * V <= 8
+      WIDE ? XSE_POOL_I8W_MIN_BLOCKS
+      : ElemsPerVec<DT>::value * V <= 16 &&
+              RowsInFlight<DT, V>::value * V <= 8
           ? (DT == 2 ? XSE_POOL_I8_MIN_BLOCKS : XSE_POOL_MIN_BLOCKS)
           : 2;
 };
@@ -200,6 +222,55 @@ __device__ __forceinline__ uint4 LoadRowVec(const uint4* p) {
   return r;
 }
 
+// Read-only 32-byte row load (sm_100 256-bit ld.global) into two vectors:
+// the part of a row one lane owns in the wide int8 layouts (p 32-byte
+// aligned).
+template <bool L1>
+__device__ __forceinline__ void LoadRowVec32(const uint4* p, uint4* a,
+                                             uint4* b) {
+  if constexpr (L1) {
+    asm volatile(
+        "ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=r"(a->x), "=r"(a->y), "=r"(a->z), "=r"(a->w), "=r"(b->x),
+          "=r"(b->y), "=r"(b->z), "=r"(b->w)
+        : "l"(p));
+  } else {
+    asm volatile(
+        "ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, "
+        "[%8];"
+        : "=r"(a->x), "=r"(a->y), "=r"(a->z), "=r"(a->w), "=r"(b->x),
+          "=r"(b->y), "=r"(b->z), "=r"(b->w)
+        : "l"(p));
+  }
+}
+
+// Vector v of a lane's part of a row, relative to the lane's first vector:
+// lanes own vectors gl + v G, or (WIDE) V contiguous vectors gl V + v.
+template <int G, bool WIDE>
+__device__ __forceinline__ int LaneVec(int v) {
+  return WIDE ? v : v * G;
+}
+
+// Loads a lane's V vectors of one row (`src` = the row's first vector for
+// this lane); vectors past a non-exact row's end read as zeros.
+template <int G, int V, bool EXACT, bool WIDE, bool L1>
+__device__ __forceinline__ void LoadLaneRow(const uint4* src, int gl,
+                                            int row_vecs, uint4 (&raw)[V]) {
+  if constexpr (WIDE) {
+    static_assert(V == 2 && EXACT, "wide layouts are exact 32-byte lanes");
+    LoadRowVec32<L1>(src, &raw[0], &raw[1]);
+  } else {
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      if (EXACT || gl + v * G < row_vecs) {
+        raw[v] = LoadRowVec<L1>(src + v * G);
+      } else {
+        raw[v] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void PrefetchRowVec(const uint4* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
@@ -227,15 +298,13 @@ __device__ __forceinline__ u64 MulPair(float a, float lo, float hi) {
   return PackF(__fmul_rn(a, lo), __fmul_rn(a, hi));
 }
 
-// One 16-byte row vector as fp32 pairs: int8 rows dequantized as
-// fma(float(q), scale, bias) (one rounding). A byte b becomes float(b)
+// One 16-byte row vector as fp32 pairs; int8 rows give their quantized
+// values float(q) (exact), which AddRow scales. A byte b becomes float(b)
 // exactly by placing b + 128 (b ^ 0x80) in the low mantissa bits of 2^23
-// (one byte permute) and subtracting 2^23 + 128; pairs then take one packed
-// fma.
+// (one byte permute) and subtracting 2^23 + 128.
 template <int DT>
 __device__ __forceinline__ void UnpackPairs(
-    const uint4& r, float scale, u64 b2,
-    u64 (&x)[ElemsPerVec<DT>::value / 2]) {
+    const uint4& r, u64 (&x)[ElemsPerVec<DT>::value / 2]) {
   const uint32_t w[4] = {r.x, r.y, r.z, r.w};
   if constexpr (DT == 0) {
     x[0] = PackBits(w[0], w[1]);
@@ -246,7 +315,6 @@ __device__ __forceinline__ void UnpackPairs(
   } else {
     constexpr uint32_t kTwo23 = 0x4B000000u;         // 2^23
     const u64 neg_magic = PackF(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-    const u64 s2 = PackF(scale, scale);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const uint32_t t = w[k] ^ 0x80808080u;
@@ -254,27 +322,52 @@ __device__ __forceinline__ void UnpackPairs(
                               __byte_perm(t, kTwo23, 0x7441));
       const u64 hi = PackBits(__byte_perm(t, kTwo23, 0x7442),
                               __byte_perm(t, kTwo23, 0x7443));
-      x[2 * k] = Fma2(Add2(lo, neg_magic), s2, b2);
-      x[2 * k + 1] = Fma2(Add2(hi, neg_magic), s2, b2);
+      x[2 * k] = Add2(lo, neg_magic);
+      x[2 * k + 1] = Add2(hi, neg_magic);
     }
   }
 }
 
 // acc += row (or acc += w*row), element by element in fp32.
+//
+// Int8 row-wise rows: w * (q * scale + bias) summed over a bag's rows is
+// accumulated as acc = fma(q, w * scale, acc) per element plus, once per
+// row, bsum += w * bias (the bias is the same for every element of a row);
+// FinishBag adds bsum to every element. That is one packed fma per pair of
+// elements instead of a dequantizing fma and an add. The result equals
+// dequantize-then-pool up to fp32 rounding: each step rounds once, so the
+// difference stays within a few units of 2^-24 times
+// sum |w| (|q| scale + |bias|) per element.
 template <int DT, int V>
 __device__ __forceinline__ void AddRow(
     u64 (&acc)[V][ElemsPerVec<DT>::value / 2], const uint4 (&raw)[V],
-    float scale, u64 b2, bool weighted, float w) {
+    float scale, float bias, bool weighted, float w, float* bsum) {
   constexpr int PPV = ElemsPerVec<DT>::value / 2;
+  if constexpr (DT == 2) {
+    const float ws = weighted ? __fmul_rn(w, scale) : scale;
+    const u64 s2 = PackF(ws, ws);
 #pragma unroll
-  for (int v = 0; v < V; ++v) {
-    u64 x[PPV];
-    UnpackPairs<DT>(raw[v], scale, b2, x);
+    for (int v = 0; v < V; ++v) {
+      u64 x[PPV];
+      UnpackPairs<DT>(raw[v], x);
 #pragma unroll
-    for (int k = 0; k < PPV; ++k) {
-      acc[v][k] = weighted
-                      ? Add2(acc[v][k], MulPair(w, LoF(x[k]), HiF(x[k])))
-                      : Add2(acc[v][k], x[k]);
+      for (int k = 0; k < PPV; ++k) acc[v][k] = Fma2(x[k], s2, acc[v][k]);
+    }
+    *bsum = weighted ? __fmaf_rn(w, bias, *bsum) : __fadd_rn(*bsum, bias);
+  } else {
+    (void)scale;
+    (void)bias;
+    (void)bsum;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      u64 x[PPV];
+      UnpackPairs<DT>(raw[v], x);
+#pragma unroll
+      for (int k = 0; k < PPV; ++k) {
+        acc[v][k] = weighted
+                        ? Add2(acc[v][k], MulPair(w, LoF(x[k]), HiF(x[k])))
+                        : Add2(acc[v][k], x[k]);
+      }
     }
   }
 }
@@ -366,30 +459,25 @@ __device__ __forceinline__ void AddWeight(float* wsum, float w, int combine) {
   }
 }
 
-// Adds raw row u to acc (dequantizing int8 rows with their scale/bias).
+// Adds raw row u to acc (int8 rows with their scale/bias, see AddRow).
 template <int DT, int V, int WM>
 __device__ __forceinline__ void AddGathered(
     u64 (&acc)[V][ElemsPerVec<DT>::value / 2], const uint4 (&raw)[V],
-    float2 sb, float w) {
-  float scale = 0.0f;
-  u64 b2 = 0;
-  if constexpr (DT == 2) {
-    scale = sb.x;
-    b2 = PackF(sb.y, sb.y);
-  }
-  AddRow<DT, V>(acc, raw, scale, b2, WM != kUnweighted, w);
+    float2 sb, float w, float* bsum) {
+  AddRow<DT, V>(acc, raw, sb.x, sb.y, WM != kUnweighted, w, bsum);
 }
 
 // Full batch of U rows of a chunk whose ids all contribute: no per-row
 // checks. Lanes past the end of a non-exact row add zeros to accumulator
 // lanes that are never stored. PF: prefetch the chunk's next batch of rows
 // into L2 while this one is in flight.
-template <int DT, int G, int V, bool EXACT, int WM, int U, bool L1, bool PF,
-          typename Hook>
+template <int DT, int G, int V, bool EXACT, bool WIDE, int WM, int U,
+          bool L1, bool PF, typename Hook>
 __device__ __forceinline__ void FullBatch(
     const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
     int my_row, float my_w, int j0, int cnt,
-    u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, Hook&& hook) {
+    u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, float* bsum,
+    Hook&& hook) {
   const int stride = EXACT ? G * V : row_vecs;
   uint4 raw[U][V];
   float2 sb[U];
@@ -397,15 +485,8 @@ __device__ __forceinline__ void FullBatch(
   for (int u = 0; u < U; ++u) {
     const int r = __shfl_sync(gmask, my_row, j0 + u, G);
     if constexpr (DT == 2) sb[u] = __ldg(d.scale_bias + r);
-    const uint4* src = rows + static_cast<int64_t>(r) * stride;
-#pragma unroll
-    for (int v = 0; v < V; ++v) {
-      if (EXACT || gl + v * G < row_vecs) {
-        raw[u][v] = LoadRowVec<L1>(src + v * G);
-      } else {
-        raw[u][v] = make_uint4(0, 0, 0, 0);
-      }
-    }
+    LoadLaneRow<G, V, EXACT, WIDE, L1>(
+        rows + static_cast<int64_t>(r) * stride, gl, row_vecs, raw[u]);
   }
   if constexpr (PF) {
 #pragma unroll
@@ -414,9 +495,13 @@ __device__ __forceinline__ void FullBatch(
       if (j < cnt) {
         const int r = __shfl_sync(gmask, my_row, j, G);
         const uint4* src = rows + static_cast<int64_t>(r) * stride;
+        if constexpr (WIDE) {
+          PrefetchRowVec(src);  // the lane's 32 bytes share one line
+        } else {
 #pragma unroll
-        for (int v = 0; v < V; ++v) {
-          if (EXACT || gl + v * G < row_vecs) PrefetchRowVec(src + v * G);
+          for (int v = 0; v < V; ++v) {
+            if (EXACT || gl + v * G < row_vecs) PrefetchRowVec(src + v * G);
+          }
         }
       }
     }
@@ -432,18 +517,19 @@ __device__ __forceinline__ void FullBatch(
       AddWeight<WM>(wsum, w, d.combine);
     }
     AddGathered<DT, V, WM>(acc, raw[u], DT == 2 ? sb[u] : make_float2(0, 0),
-                           w);
+                           w, bsum);
   }
 }
 
 // General batch: up to U rows (positions j0..j0+n-1 of the chunk), skipping
 // ids that contribute nothing.
-template <int DT, int G, int V, bool EXACT, int WM, int U, bool L1,
-          typename Hook>
+template <int DT, int G, int V, bool EXACT, bool WIDE, int WM, int U,
+          bool L1, typename Hook>
 __device__ __forceinline__ void GatherBatch(
     const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
     int my_row, float my_w, int j0, int n,
-    u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, Hook&& hook) {
+    u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, float* bsum,
+    Hook&& hook) {
   const int stride = EXACT ? G * V : row_vecs;
   uint4 raw[U][V];
   float2 sb[U];
@@ -457,16 +543,9 @@ __device__ __forceinline__ void GatherBatch(
     if constexpr (DT == 2) {
       sb[u] = use ? __ldg(d.scale_bias + r) : make_float2(0.0f, 0.0f);
     }
-    const uint4* src = rows + static_cast<int64_t>(r) * stride;
-#pragma unroll
-    for (int v = 0; v < V; ++v) {
-      if (use) {
-        if (EXACT || gl + v * G < row_vecs) {
-          raw[u][v] = LoadRowVec<L1>(src + v * G);
-        } else {
-          raw[u][v] = make_uint4(0, 0, 0, 0);
-        }
-      }
+    if (use) {
+      LoadLaneRow<G, V, EXACT, WIDE, L1>(
+          rows + static_cast<int64_t>(r) * stride, gl, row_vecs, raw[u]);
     }
   }
   hook();  // runs while this batch's rows are in flight
@@ -480,7 +559,7 @@ __device__ __forceinline__ void GatherBatch(
       }
       if (present & (1u << u)) {
         AddGathered<DT, V, WM>(acc, raw[u],
-                               DT == 2 ? sb[u] : make_float2(0, 0), w);
+                               DT == 2 ? sb[u] : make_float2(0, 0), w, bsum);
       }
     }
   }
@@ -507,12 +586,23 @@ __device__ __forceinline__ void Store32B(float* p, u64 a, u64 b, u64 c,
 // device's or a peer's), so 32-byte st.global stores may be used; the fused
 // interaction kernel passes rows in shared memory and sets it false (a
 // st.global to a shared address faults).
-template <int DT, int G, int V, bool EXACT, bool GLOBAL_OUT>
+template <int DT, int G, int V, bool EXACT, bool GLOBAL_OUT, bool WIDE = false>
 __device__ __forceinline__ void FinishBag(
     const BagDesc& d, float* out, bool vec_out, int64_t n, bool weighted,
     u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, int gl,
-    int row_vecs) {
+    int row_vecs, float* bsum) {
   constexpr int PPV = ElemsPerVec<DT>::value / 2;
+  if constexpr (DT == 2) {
+    // The rows' biases (see AddRow), once per element.
+    const u64 b2 = PackF(*bsum, *bsum);
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+#pragma unroll
+      for (int k = 0; k < PPV; ++k) acc[v][k] = Add2(acc[v][k], b2);
+    *bsum = 0.0f;
+  } else {
+    (void)bsum;
+  }
   if (n > 0 && d.combine != 1) {
     const float s = BagScale(d.combine, weighted, n, *wsum);
     const u64 s2 = PackF(s, s);
@@ -527,7 +617,7 @@ __device__ __forceinline__ void FinishBag(
                     vec_out && (reinterpret_cast<uintptr_t>(out) & 31u) == 0;
 #pragma unroll
   for (int v = 0; v < V; ++v) {
-    const int k = gl + v * G;
+    const int k = WIDE ? gl * V + v : gl + v * G;
     if (EXACT || k < row_vecs) {
       float* o = out + k * (2 * PPV);
       if (wide) {
@@ -606,12 +696,12 @@ __device__ __forceinline__ void LoadChunk(const BagDesc& d, int64_t pos,
 // sorted by mode, and each mode's tasks [task_lo, task_hi) are pooled by its
 // own range of blocks with a body compiled for that mode (a block never
 // switches mode, so the bodies do not share registers).
-template <int DT, int G, int V, bool EXACT, int WM, int UR>
+template <int DT, int G, int V, bool EXACT, bool WIDE, int WM, int UR>
 __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
                                          int64_t task_hi, int64_t block,
                                          int64_t blocks) {
   constexpr int PPV = ElemsPerVec<DT>::value / 2;
-  constexpr int U = UR == 0 ? RowsInFlight<DT, V>::value : UR;
+  constexpr int U = UR == 0 ? RowsInFlight<DT, V, WIDE>::value : UR;
   constexpr int kGroupsPerBlock = kThreads / G;
   constexpr bool kL1 = XSE_POOL_L1 != 0;
   constexpr int kChunkPrefetchTo =  // 0 none, 1 L2, 2 L1
@@ -655,13 +745,14 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
     bool next_chunk = false;
     if (CheckBag(p, d, begin, end)) {
       const int row_vecs = EXACT ? G * V : d.dim / ElemsPerVec<DT>::value;
-      const uint4* rows = static_cast<const uint4*>(d.rows) + gl;
+      const uint4* rows = static_cast<const uint4*>(d.rows) + gl * (WIDE ? V : 1);
       u64 acc[V][PPV];
 #pragma unroll
       for (int v = 0; v < V; ++v)
 #pragma unroll
         for (int k = 0; k < PPV; ++k) acc[v][k] = 0;
       float wsum = 0.0f;
+      float bsum = 0.0f;
       if (!have_chunk) LoadChunk<WM>(d, begin, end, gl, &cid, &cw);
       for (int64_t base = begin; base < end; base += G) {
         const int cnt = static_cast<int>(end - base < G ? end - base : G);
@@ -697,22 +788,22 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
         int j0 = 0;
         if (__all_sync(gmask, gl >= cnt || my_row >= 0)) {
           for (; j0 + U <= cnt; j0 += U) {
-            FullBatch<DT, G, V, EXACT, WM, U, kL1, kBatchPrefetch>(
+            FullBatch<DT, G, V, EXACT, WIDE, WM, U, kL1, kBatchPrefetch>(
                 d, rows, row_vecs, gl, gmask, my_row, my_w, j0, cnt, acc,
-                &wsum, prefetch);
+                &wsum, &bsum, prefetch);
           }
         }
         for (; j0 < cnt; j0 += U) {
           const int n = cnt - j0 < U ? cnt - j0 : U;
-          GatherBatch<DT, G, V, EXACT, WM, U, kL1>(
+          GatherBatch<DT, G, V, EXACT, WIDE, WM, U, kL1>(
               d, rows, row_vecs, gl, gmask, my_row, my_w, j0, n, acc, &wsum,
-              prefetch);
+              &bsum, prefetch);
         }
       }
-      FinishBag<DT, G, V, EXACT, true>(d, d.out + bag * d.out_stride,
-                                       d.vec_out, end - begin,
-                                       WM != kUnweighted, acc, &wsum, gl,
-                                       row_vecs);
+      FinishBag<DT, G, V, EXACT, true, WIDE>(d, d.out + bag * d.out_stride,
+                                             d.vec_out, end - begin,
+                                             WM != kUnweighted, acc, &wsum,
+                                             gl, row_vecs, &bsum);
     }
     if (!has_next) break;
     task = ntask;
@@ -738,24 +829,25 @@ __device__ __forceinline__ void EnterDependent() {
 #endif
 }
 
-template <int DT, int G, int V, bool EXACT, int UR>
+template <int DT, int G, int V, bool EXACT, int UR, bool WIDE = false>
 __global__ void __launch_bounds__(kThreads,
-                                  UR == 0 ? MinBlocks<DT, V>::value : 2)
+                                  UR == 0 ? MinBlocks<DT, V, WIDE>::value : 2)
     PoolVecKernel(const __grid_constant__ PoolParams p) {
   EnterDependent();
   if (!p.fused_checks && p.status->group_error != 0) return;
   const int64_t b = blockIdx.x;
   const int64_t b0 = p.mode_blocks[0], b1 = p.mode_blocks[1];
   if (b < b0) {
-    PoolBody<DT, G, V, EXACT, kUnweighted, UR>(p, 0, p.mode_tasks[0], b, b0);
+    PoolBody<DT, G, V, EXACT, WIDE, kUnweighted, UR>(p, 0, p.mode_tasks[0], b,
+                                                     b0);
   } else if (b < b1) {
-    PoolBody<DT, G, V, EXACT, kWeightedSum, UR>(p, p.mode_tasks[0],
-                                                p.mode_tasks[1], b - b0,
-                                                b1 - b0);
+    PoolBody<DT, G, V, EXACT, WIDE, kWeightedSum, UR>(p, p.mode_tasks[0],
+                                                      p.mode_tasks[1], b - b0,
+                                                      b1 - b0);
   } else {
-    PoolBody<DT, G, V, EXACT, kWeightedNorm, UR>(p, p.mode_tasks[1],
-                                                 p.mode_tasks[2], b - b1,
-                                                 gridDim.x - b1);
+    PoolBody<DT, G, V, EXACT, WIDE, kWeightedNorm, UR>(p, p.mode_tasks[1],
+                                                       p.mode_tasks[2],
+                                                       b - b1, gridDim.x - b1);
   }
 }
 
@@ -896,6 +988,7 @@ __device__ __forceinline__ void StagedBody(const PoolParams& p,
 #pragma unroll
       for (int k = 0; k < PPV; ++k) acc[0][k] = 0;
       float wsum = 0.0f;
+      float bsum = 0.0f;
       for (int64_t base = begin; base < end; base += kStageRows) {
         const int cnt = static_cast<int>(
             end - base < kStageRows ? end - base : kStageRows);
@@ -951,7 +1044,7 @@ __device__ __forceinline__ void StagedBody(const PoolParams& p,
                 }
                 if ((present >> u) & 1u) {
                   const uint4 raw[1] = {mine[u * G]};
-                  AddGathered<DT, 1, WM>(acc, raw, sb, w);
+                  AddGathered<DT, 1, WM>(acc, raw, sb, w, &bsum);
                 }
               }
             }
@@ -960,7 +1053,8 @@ __device__ __forceinline__ void StagedBody(const PoolParams& p,
       }
       FinishBag<DT, G, 1, true, true>(d, d.out + bag * d.out_stride,
                                       d.vec_out, end - begin,
-                                      WM != kUnweighted, acc, &wsum, gl, G);
+                                      WM != kUnweighted, acc, &wsum, gl, G,
+                                      &bsum);
     }
     if (!prefetched) prefetch();
     if (!has_next) break;
@@ -1240,6 +1334,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
 #pragma unroll
     for (int k = 0; k < PPV; ++k) acc[0][k] = 0;
     float wsum = 0.0f;
+    float bsum = 0.0f;  // int8 rows only; the fused kernel serves fp32/bf16
     if (ok) {
       const int row_vecs = G * V;
       const uint4* rows = static_cast<const uint4*>(d.rows) + gl;
@@ -1275,16 +1370,16 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
         int j0 = 0;
         if (__all_sync(gmask, gl >= cnt || my_row >= 0)) {
           for (; j0 + U <= cnt; j0 += U) {
-            FullBatch<DT, G, V, EXACT, WM, U, kL1, kBatchPrefetch>(
+            FullBatch<DT, G, V, EXACT, false, WM, U, kL1, kBatchPrefetch>(
                 d, rows, row_vecs, gl, gmask, my_row, my_w, j0, cnt, acc,
-                &wsum, prefetch);
+                &wsum, &bsum, prefetch);
           }
         }
         for (; j0 < cnt; j0 += U) {
           const int n = cnt - j0 < U ? cnt - j0 : U;
-          GatherBatch<DT, G, V, EXACT, WM, U, kL1>(
+          GatherBatch<DT, G, V, EXACT, false, WM, U, kL1>(
               d, rows, row_vecs, gl, gmask, my_row, my_w, j0, n, acc, &wsum,
-              prefetch);
+              &bsum, prefetch);
         }
       }
     }
@@ -1297,7 +1392,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
     if (ok) {
       FinishBag<DT, G, V, EXACT, false>(d, zs + (1 + t) * RS, true,
                                         end - begin, WM != kUnweighted, acc,
-                                        &wsum, gl, G * V);
+                                        &wsum, gl, G * V, &bsum);
     }
     __syncwarp();
     __threadfence_block();
@@ -1593,7 +1688,7 @@ void SplitModes(PoolParams* p, int64_t max_grid, int groups_per_block) {
   }
 }
 
-template <int DT, int G, int V, bool EXACT>
+template <int DT, int G, int V, bool EXACT, bool WIDE = false>
 cudaError_t LaunchVec(const PoolParams& in, cudaStream_t stream) {
   PoolParams p = in;
   // Descriptors by weighting mode (stable: request order within a mode). An
@@ -1611,20 +1706,22 @@ cudaError_t LaunchVec(const PoolParams& in, cudaStream_t stream) {
     p.d[j] = moving;
   }
   AssignTasks(&p, 1);
-  auto kernel = PoolVecKernel<DT, G, V, EXACT, 0>;
+  auto kernel = PoolVecKernel<DT, G, V, EXACT, 0, WIDE>;
   int64_t max_grid = static_cast<int64_t>(SmCount()) * BlocksPerSm(kernel);
 #if XSE_POOL_STAGED
-  if constexpr (V == 1 && EXACT) {
+  if constexpr ((V == 1 || (WIDE && G * V <= 32)) && EXACT) {
     // At most one wave of the staged kernel's groups (one block per SM):
     // whole rounds of rows in flight per bag (see PoolStagedKernel). Larger
-    // launches take it when the caller chose it (kPoolStaged).
-    constexpr int kGroups = kStageThreads / G;
+    // launches take it when the caller chose it (kPoolStaged). A wide
+    // layout's rows are G * V 16-byte vectors to the staged kernel.
+    constexpr int kStagedG = WIDE ? G * V : G;
+    constexpr int kGroups = kStageThreads / kStagedG;
     const bool small =
         p.total_tasks <= static_cast<int64_t>(SmCount()) * kGroups;
     if (p.kernel_choice == kPoolStaged ||
         (p.kernel_choice == kPoolAuto &&
          (XSE_POOL_STAGED == 2 || small))) {
-      auto staged = PoolStagedKernel<DT, G>;
+      auto staged = PoolStagedKernel<DT, kStagedG>;
       // Set on every launch: the attribute belongs to the current device.
       cudaError_t e = cudaFuncSetAttribute(
           staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1659,6 +1756,25 @@ cudaError_t LaunchVecExact(const Layout& l, const PoolParams& p,
                  : LaunchVec<DT, G, V, false>(p, stream);
 }
 
+// Int8 rows of 16, 32 or 64 16-byte vectors, 32-byte aligned: each lane
+// owns 32 contiguous bytes (one 256-bit load per row), G = vectors / 2.
+template <int DT>
+cudaError_t LaunchWide(const Layout& l, const PoolParams& p,
+                       cudaStream_t stream) {
+  if constexpr (DT == 2) {
+    switch (l.g) {
+      case 8: return LaunchVec<DT, 8, 2, true, true>(p, stream);
+      case 16: return LaunchVec<DT, 16, 2, true, true>(p, stream);
+      default: return LaunchVec<DT, 32, 2, true, true>(p, stream);
+    }
+  } else {
+    (void)l;
+    (void)p;
+    (void)stream;
+    return cudaErrorNotSupported;
+  }
+}
+
 template <int DT>
 cudaError_t LaunchForDtype(const Layout& l, const PoolParams& p,
                            cudaStream_t stream) {
@@ -1669,6 +1785,7 @@ cudaError_t LaunchForDtype(const Layout& l, const PoolParams& p,
     const int grid = GridFor(kernel, q.total_tasks, kThreads / 32);
     return LaunchDependent(kernel, grid, stream, q);
   }
+  if (l.wide) return LaunchWide<DT>(l, p, stream);
   if (l.v == 1) {
     switch (l.g) {
       case 4: return LaunchVecExact<DT, 4, 1>(l, p, stream);
@@ -1731,7 +1848,7 @@ cudaError_t LaunchInteractMode(int wm, const PoolParams& p,
 
 bool PoolKernelTunable(const Layout& layout, int64_t total_tasks) {
 #if XSE_POOL_STAGED
-  if (layout.v != 1 || !layout.exact) return false;
+  if (layout.v != 1 || !layout.exact || layout.wide) return false;
   const int64_t groups = kStageThreads / layout.g;
   return total_tasks > static_cast<int64_t>(SmCount()) * groups;
 #else
@@ -1747,6 +1864,15 @@ Layout ChooseLayout(int dtype, int dim, const void* rows) {
   const bool aligned = (reinterpret_cast<uintptr_t>(rows) & 15u) == 0;
   if (!aligned || row_bytes % 16 != 0) return {dtype, 32, 0, false};
   const int64_t vecs = row_bytes / 16;
+#if XSE_POOL_I8_WIDE
+  // Int8 rows of 256, 512 or 1024 bytes: 32-byte lanes (a lane's 32 int8
+  // values dequantize in registers that a 16-byte lane would spend on
+  // twice as many shuffles, address computations and loop steps per row).
+  if (dtype == 2 && (vecs == 16 || vecs == 32 || vecs == 64) &&
+      (reinterpret_cast<uintptr_t>(rows) & 31u) == 0) {
+    return {dtype, static_cast<int>(vecs / 2), 2, true, 0, true};
+  }
+#endif
   if (vecs <= 32) {
     int g = 4;
     while (g < vecs) g *= 2;

@@ -822,12 +822,12 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
       for (const xse::BagDesc& d : descs) {
         const xse::Layout l = layout_of(d);
         // One launch per layout; its weighting modes share it.
-        groups[{l.dtype, l.g, l.v, l.exact, 0}].push_back(d);
+        groups[{l.dtype, l.g, l.v, l.exact, l.wide ? 1 : 0}].push_back(d);
       }
       for (auto& [key, list] : groups) {
         const xse::Layout l{std::get<0>(key), std::get<1>(key),
-                            std::get<2>(key), std::get<3>(key),
-                            std::get<4>(key)};
+                            std::get<2>(key), std::get<3>(key), 0,
+                            std::get<4>(key) != 0};
         for (size_t base = 0; base < list.size();
              base += xse::kMaxDescsPerLaunch) {
           xse::PoolParams p{};
@@ -873,7 +873,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
       for (const xse::BagDesc& d : descs) {
         const xse::Layout l = layout_of(d);
         same = same && l.dtype == l0.dtype && l.g == l0.g && l.v == l0.v &&
-               l.exact == l0.exact;
+               l.exact == l0.exact && l.wide == l0.wide;
       }
       e = cudaErrorNotSupported;
       if (same) {
@@ -1777,7 +1777,7 @@ extern "C" int xse_engine_execute_batch_noalloc(xse_engine* engine,
         }
         lj.wmode = lj.v == 0 ? 0 : xse::WeightModeOf(descs[j]);
         if (lj.dtype != li.dtype || lj.g != li.g || lj.v != li.v ||
-            lj.exact != li.exact) {
+            lj.exact != li.exact || lj.wide != li.wide) {
           continue;  // weighting modes share a launch
         }
         launched[j] = true;

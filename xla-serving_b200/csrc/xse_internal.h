@@ -93,6 +93,9 @@ struct Layout {
   int v;
   bool exact;  // rows are exactly g*v vectors: no per-lane bounds checks
   int wmode;   // unused by the launcher (kept for callers that group by it)
+  // Lanes own v contiguous vectors (one 256-bit load each) instead of
+  // vectors gl + k g: int8 rows of 256, 512 or 1024 bytes, 32-byte aligned.
+  bool wide = false;
 };
 
 // Weighting mode of a request (kernels are compiled per mode).

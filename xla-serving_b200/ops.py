@@ -71,6 +71,20 @@ def _buffer_array(items):
   return arr, bufs
 
 
+class PreparedInputs:
+  """The host-buffer arrays of one operator call, converted once. Keeps the
+  buffers alive; their contents may change between calls, their storage
+  may not."""
+
+  def __init__(self, ids, row_pointers=(), weights=()):
+    self.ids, self._ids = _buffer_array(ids)
+    self.row_pointers, self._rps = _buffer_array(row_pointers)
+    self.weights, self._ws = _buffer_array(weights)
+    self.num_ids = len(self._ids)
+    self.num_row_pointers = len(self._rps)
+    self.num_weights = len(self._ws)
+
+
 class PinnedBuffer(HostBuffer):
   """A host buffer in the library's pinned memory, viewed as numpy.
 
@@ -322,6 +336,25 @@ class CpuEmbeddingLookupTransform:
     del keep_i, keep_r, keep_w
     C.check(rc)
     return _take_outputs(outs, n, copy)
+
+  def run_prepared(self, prepared: "PreparedInputs", outs, *, stream=None):
+    """The call with inputs converted once (a serving loop's reused host
+    buffers): the pooled outputs land in `outs`, an array of
+    HostBufferStruct from output_array(), as the library's pinned buffers;
+    release them with free_outputs(outs) once read."""
+    C.check(C.lib.xse_lookup_transform_run(
+        self._handle, prepared.ids, prepared.num_ids, prepared.row_pointers,
+        prepared.num_row_pointers, prepared.weights, prepared.num_weights,
+        outs, stream_handle(stream)))
+    return outs
+
+  def output_array(self):
+    return (C.HostBufferStruct * len(self.feature_names))()
+
+  @staticmethod
+  def free_outputs(outs):
+    for o in outs:
+      C.lib.xse_host_buffer_free(ctypes.byref(o))
 
   def close(self):
     if self._handle:
