@@ -106,6 +106,9 @@ struct ElemsPerVec<2> {
 #ifndef XSE_POOL_I8_WIDE
 #define XSE_POOL_I8_WIDE 1
 #endif
+#ifndef XSE_POOL_BF16_WIDE
+#define XSE_POOL_BF16_WIDE 1
+#endif
 
 // PoolStagedKernel: 0 never, 1 for launches small enough for one wave of
 // it, 2 for every launch whose rows it serves.
@@ -129,6 +132,17 @@ struct ElemsPerVec<2> {
 #ifndef XSE_POOL_I8W_MIN_BLOCKS
 #define XSE_POOL_I8W_MIN_BLOCKS 3
 #endif
+// Wide bf16 layouts: rows in flight per lane and resident blocks per SM.
+// Measured on the multi-table workload (8 bf16 tables 500k x 128, uniform
+// ids), pooling per step: 4 rows at 2 blocks/SM 65.2 us (128 registers, no
+// spills); 2 at 3 blocks 75.1 us, 3 at 3 blocks 77.0 us (both spill);
+// 16-byte lanes 70.3 us.
+#ifndef XSE_POOL_BF16W_ROWS
+#define XSE_POOL_BF16W_ROWS 4
+#endif
+#ifndef XSE_POOL_BF16W_MIN_BLOCKS
+#define XSE_POOL_BF16W_MIN_BLOCKS 2
+#endif
 
 // Rows gathered per batch (in flight per lane, times V vectors each; a wide
 // lane's V vectors are one load).
@@ -136,14 +150,15 @@ template <int DT, int V, bool WIDE = false>
 struct RowsInFlight {
   static constexpr int base = DT == 2 ? XSE_POOL_I8_ROWS : XSE_POOL_ROWS;
   static constexpr int value =
-      WIDE ? XSE_POOL_I8W_ROWS : (V >= base ? 1 : base / V);
+      WIDE ? (DT == 2 ? XSE_POOL_I8W_ROWS : XSE_POOL_BF16W_ROWS)
+           : (V >= base ? 1 : base / V);
 };
 
 // Resident blocks per SM each variant's register budget is sized for.
 template <int DT, int V, bool WIDE = false>
 struct MinBlocks {
   static constexpr int value =
-      WIDE ? XSE_POOL_I8W_MIN_BLOCKS
+      WIDE ? (DT == 2 ? XSE_POOL_I8W_MIN_BLOCKS : XSE_POOL_BF16W_MIN_BLOCKS)
       : ElemsPerVec<DT>::value * V <= 16 &&
               RowsInFlight<DT, V>::value * V <= 8
           ? (DT == 2 ? XSE_POOL_I8_MIN_BLOCKS : XSE_POOL_MIN_BLOCKS)
@@ -1518,11 +1533,16 @@ __global__ void __launch_bounds__(kThreads)
 // [0, vocab). A request's offsets followed by its id positions are cut into
 // chunks of kValidateChunk elements; a warp checks one chunk, lane l taking
 // elements l, l+32, ... (coalesced), and looks up the chunk's request once.
+// Every load of a chunk (its offsets, or its ids -- all in [0, num_ids), so
+// in bounds -- and the request's first and last offsets) is issued before
+// any is checked, so a chunk costs one memory round trip; checking as the
+// loads returned made each id load wait for the previous one's verdict.
 constexpr int kValidateChunk = 256;
 
 __global__ void __launch_bounds__(kThreads)
     ValidateKernel(const __grid_constant__ PoolParams p, int64_t total_work) {
   EnterDependent();
+  constexpr int K = kValidateChunk / 32;
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
   int t = 0;
@@ -1536,28 +1556,38 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t i0 = (c - d.work_begin) * kValidateChunk;
     const int64_t first = LoadIndex(d.offsets, d.offs64, 0);
     const int64_t last = LoadIndex(d.offsets, d.offs64, d.num_bags);
+    int64_t cur[K], prev[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t i = i0 + k * 32 + lane;
+      cur[k] = 0;
+      prev[k] = 0;
+      if (i < num_offsets) {
+        cur[k] = LoadIndex(d.offsets, d.offs64, i);
+        if (i > 0) prev[k] = LoadIndex(d.offsets, d.offs64, i - 1);
+      } else if (i < elems && d.ids != nullptr) {
+        cur[k] = LoadIndex(d.ids, d.ids64, i - num_offsets);
+      }
+    }
     unsigned int flags = 0;
     int64_t bad_pos = -1;
-#pragma unroll 4
-    for (int k = 0; k < kValidateChunk / 32; ++k) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
       const int64_t i = i0 + k * 32 + lane;
-      if (i >= elems) break;
       if (i < num_offsets) {
-        const int64_t cur = LoadIndex(d.offsets, d.offs64, i);
-        if (i == 0 ? cur < 0 : LoadIndex(d.offsets, d.offs64, i - 1) > cur) {
-          flags |= kErrBadOffsets;
-        }
+        if (i == 0 ? cur[k] < 0 : prev[k] > cur[k]) flags |= kErrBadOffsets;
         if (i == num_offsets - 1) {
-          if (cur > d.num_ids) flags |= kErrLastExceedsIds;
-          if (d.weights != nullptr && cur > d.num_weights) {
+          if (cur[k] > d.num_ids) flags |= kErrLastExceedsIds;
+          if (d.weights != nullptr && cur[k] > d.num_weights) {
             flags |= kErrLastExceedsWeights;
           }
         }
-      } else if (d.ids != nullptr) {
+      } else if (i < elems && d.ids != nullptr) {
+        // Positions grow with k: the first bad one is this lane's smallest.
         const int64_t pos = i - num_offsets;
-        if (pos >= first && pos < last && bad_pos < 0) {
-          const int64_t id = LoadIndex(d.ids, d.ids64, pos);
-          if (id < 0 || id >= d.vocab) bad_pos = pos;
+        if (bad_pos < 0 && pos >= first && pos < last &&
+            (cur[k] < 0 || cur[k] >= d.vocab)) {
+          bad_pos = pos;
         }
       }
     }
@@ -1756,12 +1786,12 @@ cudaError_t LaunchVecExact(const Layout& l, const PoolParams& p,
                  : LaunchVec<DT, G, V, false>(p, stream);
 }
 
-// Int8 rows of 16, 32 or 64 16-byte vectors, 32-byte aligned: each lane
-// owns 32 contiguous bytes (one 256-bit load per row), G = vectors / 2.
+// Int8 or bf16 rows of 16, 32 or 64 16-byte vectors, 32-byte aligned: each
+// lane owns 32 contiguous bytes (one 256-bit load per row), G = vectors / 2.
 template <int DT>
 cudaError_t LaunchWide(const Layout& l, const PoolParams& p,
                        cudaStream_t stream) {
-  if constexpr (DT == 2) {
+  if constexpr (DT != 0) {
     switch (l.g) {
       case 8: return LaunchVec<DT, 8, 2, true, true>(p, stream);
       case 16: return LaunchVec<DT, 16, 2, true, true>(p, stream);
@@ -1848,8 +1878,11 @@ cudaError_t LaunchInteractMode(int wm, const PoolParams& p,
 
 bool PoolKernelTunable(const Layout& layout, int64_t total_tasks) {
 #if XSE_POOL_STAGED
-  if (layout.v != 1 || !layout.exact || layout.wide) return false;
-  const int64_t groups = kStageThreads / layout.g;
+  const int staged_g = layout.wide ? layout.g * layout.v : layout.g;
+  if (!layout.exact || (layout.v != 1 && !layout.wide) || staged_g > 32) {
+    return false;
+  }
+  const int64_t groups = kStageThreads / staged_g;
   return total_tasks > static_cast<int64_t>(SmCount()) * groups;
 #else
   (void)layout;
@@ -1864,15 +1897,17 @@ Layout ChooseLayout(int dtype, int dim, const void* rows) {
   const bool aligned = (reinterpret_cast<uintptr_t>(rows) & 15u) == 0;
   if (!aligned || row_bytes % 16 != 0) return {dtype, 32, 0, false};
   const int64_t vecs = row_bytes / 16;
-#if XSE_POOL_I8_WIDE
-  // Int8 rows of 256, 512 or 1024 bytes: 32-byte lanes (a lane's 32 int8
-  // values dequantize in registers that a 16-byte lane would spend on
-  // twice as many shuffles, address computations and loop steps per row).
-  if (dtype == 2 && (vecs == 16 || vecs == 32 || vecs == 64) &&
+  // Int8 (and bf16) rows of 256, 512 or 1024 bytes: 32-byte lanes, so a
+  // row takes half the lanes, shuffles, address computations and loop
+  // steps, and a lane keeps twice the bytes in flight per row it holds.
+  // (fp32 rows keep 16-byte lanes: the fused interaction kernel serves
+  // that layout.)
+  if (((dtype == 2 && XSE_POOL_I8_WIDE) ||
+       (dtype == 1 && XSE_POOL_BF16_WIDE)) &&
+      (vecs == 16 || vecs == 32 || vecs == 64) &&
       (reinterpret_cast<uintptr_t>(rows) & 31u) == 0) {
     return {dtype, static_cast<int>(vecs / 2), 2, true, 0, true};
   }
-#endif
   if (vecs <= 32) {
     int g = 4;
     while (g < vecs) g *= 2;
