@@ -287,6 +287,18 @@ int xse_engine_execute_interaction(xse_engine* engine,
                                    int64_t out_stride, void* stream,
                                    int32_t flags, xse_status* status);
 
+/* xse_engine_execute_interaction writing the split operands of the next
+ * layer's three-pass TF32 GEMM (xse_linear_forward_tf32x3) instead of the
+ * values: out_hi receives each value rounded to TF32 (as xse_tf32_split) and
+ * out_lo the exact remainder (out_hi + out_lo == the value), both rows of
+ * out_stride floats. The fused kernel writes them directly, so the top MLP's
+ * first layer needs no separate split pass over the interaction rows. */
+int xse_engine_execute_interaction_tf32(
+    xse_engine* engine, const xse_bag_request* reqs, int32_t n,
+    const float* dense, int64_t dense_stride, int64_t batch, float* out_hi,
+    float* out_lo, int64_t out_stride, void* stream, int32_t flags,
+    xse_status* status);
+
 /* ---------------------------------------------------------------------------
  * Seeded synthetic inputs on the device (counter-based, reproducible on the
  * host). Used by tests and benchmarks; no reference counterpart (the

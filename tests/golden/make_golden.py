@@ -80,7 +80,10 @@ def addition_order_case():
 
 
 def main():
-  reference_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+  if len(sys.argv) != 2:
+    sys.exit(f"usage: {sys.argv[0]} REFERENCE_ROOT (the xla-serving source "
+             "tree holding examples/dlrm_benchmark/common.py)")
+  reference_root = sys.argv[1]
   lookup, stacked = load_reference_functions(reference_root)
   rng = np.random.default_rng(20260101)
   num_tables = 6

@@ -163,13 +163,17 @@ def test_linear_forward_tf32x3(xse, dlrm, rows, in_dim, out_dim, act):
                                1e-5 * bound + 1e-6)
 
 
-@pytest.mark.parametrize("fused_interaction", [False, True])
-def test_dlrm_forward_end_to_end(xse, dlrm, fused_interaction):
+@pytest.mark.parametrize("fused_interaction,math,index", [
+    (False, "fp32", "i64"), (True, "fp32", "i64"), (True, "tf32x3", "i32"),
+    (False, "tf32x3", "i32")])
+def test_dlrm_forward_end_to_end(xse, dlrm, fused_interaction, math, index):
   """Pooled lookup of 26 fp32 features (ragged Zipf bags, sum pooling) plus
   the tower: pooled values bit-exact to the oracle (unfused: read back from
   the pooled buffer), predictions within 1e-4 of the float64 tower applied to
   the oracle's pooled values (fused: pooling and interaction in one
-  kernel, the pooled rows never stored)."""
+  kernel, the pooled rows never stored; fused split-TF32: the interaction
+  kernel writes the first top layer's split operands). Ids and row pointers
+  int64, or int32 as the reference's DLRM bundle feeds them."""
   from xla_serving_b200 import synth  # pylint: disable=import-outside-toplevel
   engine = xse.EmbeddingEngine()
   rows = synth.log_uniform_rows(26, 50, 5000, 7)
@@ -185,10 +189,13 @@ def test_dlrm_forward_end_to_end(xse, dlrm, fused_interaction):
     host_tables.append(table.cpu().numpy())
     spec = synth.TableSpec(name, rows[t], 128, xse._capi.DT_F32, "SUM")
     fb = synth.synth_batch(spec, t, batch, 1, 100, 11, 1.05)
-    ids.append(fb.ids)
-    offsets.append(fb.offsets)
+    idt = torch.int32 if index == "i32" else torch.int64
+    ids.append(fb.ids.to(idt))
+    offsets.append(fb.offsets.to(idt))
   model = dlrm.DLRM(engine, names, seed=1,
-                    fused_interaction=fused_interaction)
+                    fused_interaction=fused_interaction,
+                    math=dlrm.MATH_TF32X3 if math == "tf32x3"
+                    else xse._capi.MATH_FP32)
   dense = torch.randn(batch, 13, generator=torch.Generator().manual_seed(2))
   pred = model.forward(dense.cuda(), ids, offsets).cpu().numpy()
   pooled = np.stack([
@@ -200,4 +207,41 @@ def test_dlrm_forward_end_to_end(xse, dlrm, fused_interaction):
                                   pooled)
   want = model.tower.reference_forward(dense.numpy(), pooled)
   np.testing.assert_allclose(pred, want, rtol=0, atol=1e-4)
+  engine.close()
+
+
+@pytest.mark.parametrize("dim,tables", [(128, 26), (64, 5)])
+def test_interaction_split_operands(xse, dim, tables):
+  """execute_interaction with out_lo writes the values' TF32 parts and the
+  exact remainders: hi + lo equals the plain call's values bit for bit, hi
+  has no bits below TF32 precision and |lo| <= 2^-11 |value|. dim 128 fp32
+  runs the fused kernel, dim 64 the pooling + interaction fallback."""
+  rng = np.random.default_rng(dim + tables)
+  engine = xse.EmbeddingEngine()
+  batch = 96
+  reqs = []
+  for t in range(tables):
+    table = torch.from_numpy(
+        rng.uniform(-1, 1, (300, dim)).astype(np.float32)).cuda()
+    engine.add_table(f"t{t}", table, "SUM")
+    engine.register_feature(f"f{t}", f"t{t}")
+    lengths = rng.integers(0, 9, batch)
+    offsets = np.concatenate([[0], np.cumsum(lengths)])
+    ids = rng.integers(0, 300, int(offsets[-1]))
+    reqs.append(xse.BagRequest(f"f{t}", torch.from_numpy(ids).cuda(),
+                               torch.from_numpy(offsets).cuda(), None))
+  dense = torch.randn(batch, dim, device="cuda")
+  width = dim + (tables + 1) * tables // 2
+  stride = (width + 3) // 4 * 4 + 4
+  plain = torch.full((batch, stride), 9.0, device="cuda")
+  engine.execute_interaction(reqs, dense, plain, fused=True)
+  hi = torch.full_like(plain, 7.0)
+  lo = torch.full_like(plain, 7.0)
+  engine.execute_interaction(reqs, dense, hi, fused=True, out_lo=lo)
+  v = plain.cpu().numpy()
+  h = hi.cpu().numpy()
+  l = lo.cpu().numpy()
+  np.testing.assert_array_equal((h + l).view(np.uint32), v.view(np.uint32))
+  assert not (h.view(np.uint32) & 0x1fff).any()
+  assert (np.abs(l) <= np.abs(v) * 2.0 ** -11).all()
   engine.close()

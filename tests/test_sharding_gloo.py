@@ -245,3 +245,62 @@ def test_rowwise_reduce_scatter_gloo(chunks):
   for r in range(world):
     exp = want[r * block:(r + 1) * block]
     np.testing.assert_allclose(got[r], exp, rtol=1e-5, atol=1e-6)
+
+
+def _leaving_rank(rank, world, port, mode, results):
+  """Both ranks run one exchange step; then rank 1 leaves (between steps,
+  nothing of it in flight) and rank 0 runs the next step. Rank 0's
+  collective must end with an error within the process group's short
+  timeout instead of waiting for ever."""
+  import time  # pylint: disable=import-outside-toplevel
+  from datetime import timedelta  # pylint: disable=import-outside-toplevel
+  os.environ["MASTER_ADDR"] = "127.0.0.1"
+  os.environ["MASTER_PORT"] = str(port)
+  dist.init_process_group("gloo", rank=rank, world_size=world,
+                          timeout=timedelta(seconds=5))
+  try:
+    from conftest import load_package  # pylint: disable=import-outside-toplevel
+    sharding = load_package().sharding
+    plan = sharding.ShardPlan(world, rank)
+    tables = make_tables()
+    rowwise = mode == "rowwise"
+    local = (range(NUM_TABLES) if rowwise
+             else plan.tables_of(rank, NUM_TABLES))
+    features, by_name = [], {}
+    for t in local:
+      ids, offsets, weights = make_batch(t)
+      by_name[f"f{t}"] = (tables[t], COMBINE[t])
+      features.append((f"f{t}", torch.from_numpy(ids),
+                       torch.from_numpy(offsets),
+                       None if weights is None else torch.from_numpy(weights)))
+    if rowwise:
+      ex = sharding.RowwiseExchange(plan, BATCH, NUM_TABLES, DIM,
+                                    cpu_pooler(by_name), chunks=2)
+    else:
+      ex = sharding.TablewiseExchange(plan, BATCH, NUM_TABLES, DIM,
+                                      cpu_pooler(by_name), mode=mode)
+    steps = ex.schedule(features)
+    ex.run(steps)  # every rank takes part
+    if rank == 1:
+      results[1] = "left"
+      return
+    t0 = time.monotonic()
+    try:
+      ex.run(steps)
+      results[0] = ("no error", time.monotonic() - t0)
+    except Exception as e:  # pylint: disable=broad-except
+      results[0] = (type(e).__name__, time.monotonic() - t0)
+  finally:
+    try:
+      dist.destroy_process_group()
+    except Exception:  # pylint: disable=broad-except
+      pass
+
+
+@pytest.mark.parametrize("mode", ["a2a", "pipelined", "rowwise"])
+def test_rank_leaving_between_steps_ends_the_next_exchange(mode):
+  got = _spawn(_leaving_rank, mode)
+  assert got[1] == "left"
+  kind, seconds = got[0]
+  assert kind != "no error", got[0]
+  assert seconds < 60, got[0]

@@ -142,6 +142,9 @@ SIGNATURES = {
                                      ctypes.POINTER(_I64)]),
     "xse_engine_execute_interaction": (_I, [_P, _P, _I32, _P, _I64, _I64, _P,
                                             _I64, _P, _I32, _P]),
+    "xse_engine_execute_interaction_tf32": (_I, [_P, _P, _I32, _P, _I64,
+                                                 _I64, _P, _P, _I64, _P,
+                                                 _I32, _P]),
     "xse_dot_interaction": (_I, [_P, _P, _I64, _I32, _I32, _P, _P]),
     "xse_synth_table": (_I, [_P, _P, _P, _I32, _U64, _U64, _I64, _I64, _I32,
                              _P]),

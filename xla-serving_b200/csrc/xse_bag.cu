@@ -1140,6 +1140,23 @@ __device__ __forceinline__ void SplitTf32(float x, uint32_t* hi,
   *lo = __float_as_uint(x - __uint_as_float(h));
 }
 
+// Stores interaction value v at o[i], or -- when the caller asked for the
+// next layer's split operands (olo non-null) -- its TF32 part rounded to
+// nearest (ties away, as xse_tf32_split) at o[i] and the exact remainder
+// at olo[i].
+__device__ __forceinline__ void StoreInteraction(float* o, float* olo,
+                                                 int64_t i, float v) {
+  if (olo == nullptr) {
+    o[i] = v;
+    return;
+  }
+  uint32_t h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+  const float vh = __uint_as_float(h);
+  o[i] = vh;
+  olo[i] = __fsub_rn(v, vh);
+}
+
 // acc += A (16x8, row-major fragment a) * B (8x8, column-major fragment b).
 __device__ __forceinline__ void MmaTf32(float (&acc)[4], const uint32_t (&a)[4],
                                         uint32_t b0, uint32_t b1) {
@@ -1159,7 +1176,7 @@ __device__ __forceinline__ void MmaTf32(float (&acc)[4], const uint32_t (&a)[4],
 // (i, j) to o[i (2R - i - 1) / 2 + j - i - 1].
 template <int D, int HALF>
 __device__ __forceinline__ void GramHalfTf32x3(const float* zs, int R, int RS,
-                                               float* o) {
+                                               float* o, float* olo) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
   const float* rp[4];
@@ -1208,7 +1225,10 @@ __device__ __forceinline__ void GramHalfTf32x3(const float* zs, int R, int RS,
     for (int e = 0; e < 4; ++e) {
       const int i = i0 + (e >= 2 ? 8 : 0);
       const int j = j0 + (e & 1);
-      if (i < j && j < R) o[i * (2 * R - i - 1) / 2 + j - i - 1] = acc[t][e];
+      if (i < j && j < R) {
+        StoreInteraction(o, olo, i * (2 * R - i - 1) / 2 + j - i - 1,
+                         acc[t][e]);
+      }
     }
   }
 }
@@ -1419,15 +1439,21 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
       __threadfence_block();
       const float* dense = a.dense + bag * a.dense_stride;
       float* o = a.out + bag * a.out_stride;
+      float* olo = a.out_lo != nullptr ? a.out_lo + bag * a.out_stride
+                                       : nullptr;
       for (int c = lane * 4; c < D; c += 128) {
         *reinterpret_cast<float4*>(zs + c) =
             __ldg(reinterpret_cast<const float4*>(dense + c));
       }
       __syncwarp();
-      for (int c = lane; c < D; c += 32) o[c] = zs[c];  // any out alignment
-      for (int64_t c = width + lane; c < a.out_stride; c += 32) o[c] = 0.0f;
-      GramHalfTf32x3<D, 0>(zs, R, RS, o + D);
-      GramHalfTf32x3<D, 1>(zs, R, RS, o + D);
+      for (int c = lane; c < D; c += 32) {
+        StoreInteraction(o, olo, c, zs[c]);  // any out alignment
+      }
+      for (int64_t c = width + lane; c < a.out_stride; c += 32) {
+        StoreInteraction(o, olo, c, 0.0f);
+      }
+      GramHalfTf32x3<D, 0>(zs, R, RS, o + D, olo ? olo + D : nullptr);
+      GramHalfTf32x3<D, 1>(zs, R, RS, o + D, olo ? olo + D : nullptr);
       __syncwarp();
       if (lane == 0) {
         filled[slot] = 0;

@@ -908,6 +908,16 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
                                         stream);
           ++launches;
         }
+        if (e == cudaSuccess && inter->out_lo != nullptr) {
+          // The split operands in place (hi over the values).
+          if (xse_tf32_split(inter->out, inter->batch,
+                             static_cast<int32_t>(inter->out_stride),
+                             inter->out_stride, inter->out, inter->out_lo,
+                             stream) != XSE_OK) {
+            e = cudaErrorLaunchFailure;
+          }
+          ++launches;
+        }
         cudaError_t fe = cudaFreeAsync(scratch, stream);
         if (e == cudaSuccess) e = fe;
       }
@@ -1333,6 +1343,7 @@ int xse_status_create(int32_t max_requests, xse_status** out) {
 int xse_engine_execute_batch(xse_engine* engine, const xse_bag_request* reqs,
                              int32_t n, void* stream, int32_t flags,
                              xse_status* status) {
+  xse::TraceRange trace("xse.execute_batch");
   if (engine == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null engine");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (status != nullptr) {
@@ -1352,6 +1363,19 @@ int xse_engine_execute_interaction(xse_engine* engine,
                                    int64_t batch, float* out,
                                    int64_t out_stride, void* stream,
                                    int32_t flags, xse_status* status) {
+  return xse_engine_execute_interaction_tf32(engine, reqs, n, dense,
+                                             dense_stride, batch, out,
+                                             nullptr, out_stride, stream,
+                                             flags, status);
+}
+
+int xse_engine_execute_interaction_tf32(
+    xse_engine* engine, const xse_bag_request* reqs, int32_t n,
+    const float* dense, int64_t dense_stride, int64_t batch, float* out_hi,
+    float* out_lo, int64_t out_stride, void* stream, int32_t flags,
+    xse_status* status) {
+  xse::TraceRange trace("xse.execute_interaction");
+  float* out = out_hi;
   if (engine == nullptr) return SetError(XSE_INVALID_ARGUMENT, "null engine");
   if (dense == nullptr || out == nullptr || batch < 0) {
     return SetError(XSE_INVALID_ARGUMENT,
@@ -1362,6 +1386,7 @@ int xse_engine_execute_interaction(xse_engine* engine,
   a.dense = dense;
   a.dense_stride = dense_stride;
   a.out = out;
+  a.out_lo = out_lo;
   a.out_stride = out_stride;
   a.batch = batch;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

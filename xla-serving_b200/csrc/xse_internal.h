@@ -3,9 +3,22 @@
 #define XSE_INTERNAL_H_
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 namespace xse {
+
+// An NVTX range over one entry point's host work (the reference traces
+// each graph node's execution with a tsl TraceMe span,
+// data/processor/cc/core/graph/graph_executor.cc:62,111). Header-only NVTX:
+// without a profiler attached a push or pop is one indirect call.
+class TraceRange {
+ public:
+  explicit TraceRange(const char* name) { nvtxRangePushA(name); }
+  ~TraceRange() { nvtxRangePop(); }
+  TraceRange(const TraceRange&) = delete;
+  TraceRange& operator=(const TraceRange&) = delete;
+};
 
 // Descriptors passed by value in one launch (kernel parameter space holds up
 // to 32 KB on sm_70+ with CUDA 12.1+).
@@ -139,6 +152,10 @@ struct InteractArgs {
   const float* dense;        // [batch] rows of dim floats, 16-byte aligned
   int64_t dense_stride;      // floats, multiple of 4
   float* out;                // [batch] rows of out_stride floats
+  // Non-null: out receives each value's TF32 part (round to nearest, ties
+  // away) and out_lo the exact remainder, the split operands of the next
+  // layer's three-pass TF32 GEMM (rows of out_stride floats).
+  float* out_lo;
   int64_t out_stride;        // >= dim + (T+1)T/2
   int64_t batch;
   int32_t samples_per_tile;  // shared-memory sample slots (set by the launcher)

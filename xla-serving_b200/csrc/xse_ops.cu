@@ -1038,6 +1038,7 @@ int xse_resource_load_sharded(const char* const* asset_names,
                               int32_t num_assets, int32_t device,
                               const xse_load_options* options,
                               xse_resource** out) {
+  xse::TraceRange trace("xse.resource_load");
   xse_load_options opt{1, 0, XSE_SHARD_NONE, 0, 0};
   if (options != nullptr) opt = *options;
   if (opt.sharding < XSE_SHARD_NONE || opt.sharding > XSE_SHARD_ROWWISE ||
@@ -1181,6 +1182,7 @@ int xse_lookup_transform_run(xse_lookup_transform* t,
                              const xse_host_buffer* weights,
                              int32_t num_weights, xse_host_buffer* outputs,
                              void* stream) {
+  xse::TraceRange trace("xse.lookup_transform");
   // CpuEmbeddingLookupTransform::operator() (cpu_embedding_lookup_
   // transform.cc:244-356).
   if (t == nullptr || outputs == nullptr) {
@@ -1326,6 +1328,7 @@ int xse_dense_lookup_transform_run(xse_dense_lookup_transform* t,
                                    const xse_host_buffer* dense_ids,
                                    int32_t num_inputs,
                                    xse_host_buffer* outputs, void* stream) {
+  xse::TraceRange trace("xse.dense_lookup_transform");
   // DenseCpuEmbeddingLookupTransform::operator() (dense_cpu_embedding_
   // lookup_transform.cc:148-268).
   if (t == nullptr || outputs == nullptr) {

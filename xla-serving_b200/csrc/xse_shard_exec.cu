@@ -691,6 +691,7 @@ int xse_shard_exchange_create(xse_engine* engine, xse_shard_comm* comm,
 int xse_shard_exchange_run(xse_shard_exchange* ex,
                            const xse_bag_request* features, int32_t n,
                            int32_t flags, void* stream, float** out) {
+  xse::TraceRange trace("xse.shard_exchange");
   if (ex == nullptr || features == nullptr) {
     return ShardFail(XSE_INVALID_ARGUMENT, "null argument");
   }

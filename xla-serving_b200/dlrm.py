@@ -5,10 +5,13 @@ CpuEmbeddingLookupTransform and feeds them, with 13 dense features, to a
 dense tower under XLA (examples/dlrm/model_jce.py:98-189): bottom MLP
 13-512-256-128 with ReLU, feature interaction over the 27 vectors, top MLP
 1024-1024-512-256-1 with a sigmoid head. Here every stage runs on the device:
-the pooled lookup in the engine's kernels, the Dense layers as fp32 GEMMs with
-fused bias+ReLU (xse_linear_forward), and the dot interaction (27 x 27 Gram,
-upper triangle, dense output first: 128 + 351 = 479 features) in place of
-the reference's DCN-v2 cross network.
+the pooled lookup in the engine's kernels, the dot interaction (27 x 27
+Gram, upper triangle, dense output first: 128 + 351 = 479 features) in place
+of the reference's DCN-v2 cross network, and the Dense layers with fused
+bias+ReLU (xse_linear_forward): fp32 GEMMs, or -- MATH_TF32X3, what the
+benchmark runs -- three TF32 tensor-core GEMMs over hi/lo split operands
+(fp32-level accuracy). With the fused interaction the interaction kernel
+writes the first top layer's split operands itself.
 
 Initialisation: Dense kernels Xavier-uniform, biases U(-1/sqrt(fan_in),
 1/sqrt(fan_in)) as the reference's uniform_init (model_jce.py:107-118),
@@ -194,9 +197,34 @@ class DenseTower:
     return self.width_stride * 4
 
   def split_launches(self, fused):
-    """Operand-split kernels one forward launches (one per split layer)."""
-    del fused
-    return len(self._split)
+    """Operand-split kernels one forward launches: one per split layer,
+    except the first top layer's when the fused interaction writes its
+    operands."""
+    return len(self._split) - (1 if fused and self.first_top_split() else 0)
+
+  def first_top_split(self):
+    """The split kernel of the first top layer, when it runs split-TF32 on
+    the interaction rows as they are laid out (else None)."""
+    return self._split.get(id(self.top[0]))
+
+  def interaction_split_buffers(self, batch):
+    """[B, width_stride] hi and lo views of the split scratch, where the
+    fused interaction writes the first top layer's operands."""
+    bufs = self._buffers_for(batch)
+    n = batch * self.width_stride
+    return (bufs["hi"][:n].view(batch, self.width_stride),
+            bufs["lo"][:n].view(batch, self.width_stride))
+
+  def top_forward_split(self, hi, lo, *, stream=None):
+    """The top MLP from the first layer's split operands -> predictions."""
+    bufs = self._buffers_for(hi.shape[0])
+    layer = self.top[0]
+    k_hi, k_lo = self._split[id(layer)]
+    x = linear_tf32x3(hi, lo, k_hi, k_lo, layer, bufs["top"][0],
+                      stream=stream)
+    for layer, out in zip(self.top[1:], bufs["top"][1:]):
+      x = self._layer(x, layer, out, bufs, stream)
+    return x.view(-1)
 
   def top_forward(self, inter, *, stream=None):
     """The top MLP over interaction rows -> predictions [B]."""
@@ -290,7 +318,15 @@ class DLRM:
     # raised, or reported by status.wait()); no separate validation pass.
     if self.fused_interaction:
       x = self.tower.bottom_forward(dense, stream=stream)
-      inter = self.tower.interaction_buffer(dense.shape[0])
+      batch = dense.shape[0]
+      if self.tower.first_top_split() is not None:
+        # The interaction kernel writes the first top layer's split-TF32
+        # operands: no split pass over the interaction rows.
+        hi, lo = self.tower.interaction_split_buffers(batch)
+        self.engine.execute_interaction(requests, x, hi, stream=stream,
+                                        status=status, fused=True, out_lo=lo)
+        return self.tower.top_forward_split(hi, lo, stream=stream)
+      inter = self.tower.interaction_buffer(batch)
       self.engine.execute_interaction(requests, x, inter, stream=stream,
                                       status=status, fused=True)
       return self.tower.top_forward(inter, stream=stream)

@@ -273,12 +273,14 @@ class EmbeddingEngine:
 
   def execute_interaction(self, requests: Sequence[BagRequest], dense, out,
                           *, stream=None, fused=False,
-                          status: Optional[Status] = None):
+                          status: Optional[Status] = None, out_lo=None):
     """Pools request t (feature t of every sample; `output` unused, may be
     None) and writes the dot interaction of [dense_b; pooled_b,0..T-1] into
     out [batch, >= dim + (T+1)T/2] (fp32): one fused kernel where it serves
     the tables' layout, without writing the pooled rows. Flags and status as
-    execute_batch."""
+    execute_batch. With `out_lo` (same shape and strides as out), out gets
+    each value's TF32 part and out_lo the remainder: the split operands of
+    the next three-pass TF32 layer."""
     arr, names = self._c_requests(requests)
     flags = C.EXEC_FUSED if fused else C.EXEC_STRICT
     if status is not None:
@@ -290,10 +292,17 @@ class EmbeddingEngine:
       raise C.XseError(C.INVALID_ARGUMENT,
                        "dense [B, dim] and out [B, width] need unit column "
                        "stride and one batch")
-    rc = C.lib.xse_engine_execute_interaction(
+    if out_lo is not None and (out_lo.dtype != torch.float32 or
+                               out_lo.shape != out.shape or
+                               out_lo.stride() != out.stride()):
+      raise C.XseError(C.INVALID_ARGUMENT,
+                       "out_lo must match out's shape, strides and dtype")
+    rc = C.lib.xse_engine_execute_interaction_tf32(
         self._handle, arr, len(requests), dense.data_ptr(), dense.stride(0),
-        dense.shape[0], out.data_ptr(), out.stride(0), stream_handle(stream),
-        flags, status.handle if status is not None else None)
+        dense.shape[0], out.data_ptr(),
+        None if out_lo is None else out_lo.data_ptr(), out.stride(0),
+        stream_handle(stream), flags,
+        status.handle if status is not None else None)
     del names
     C.check(rc)
 
