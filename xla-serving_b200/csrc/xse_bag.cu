@@ -630,6 +630,46 @@ __device__ __forceinline__ void FinishBag(
   // 32-byte aligned (each lane's part then is too).
   const bool wide = XSE_POOL_WIDE_STORES && GLOBAL_OUT && PPV % 4 == 0 &&
                     vec_out && (reinterpret_cast<uintptr_t>(out) & 31u) == 0;
+  if constexpr (WIDE && DT == 1 && PPV == 4 && V == 2) {
+    // A wide bf16 lane holds two consecutive 32-byte pieces of the row
+    // (pieces 2gl and 2gl+1); storing them as they lie leaves every store
+    // instruction of the group half-filling each 64-byte span, which costs
+    // twice the transactions when the row is a peer's memory over NVLink.
+    // So the pieces are exchanged first: store s writes piece s*G + gl,
+    // taken from lane (s*G + gl) / 2, and each store covers G contiguous
+    // pieces.
+    if (wide) {
+      const int lane = threadIdx.x & 31;
+      const unsigned gmask =
+          G == 32 ? 0xffffffffu : (((1u << G) - 1u) << (lane - gl));
+#pragma unroll
+      for (int st = 0; st < 2; ++st) {
+        const int q = st * G + gl;
+        const int src = q >> 1;
+        const bool odd = (q & 1) != 0;
+        u64 piece[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t a_lo = __shfl_sync(
+              gmask, static_cast<uint32_t>(acc[0][e]), src, G);
+          const uint32_t a_hi = __shfl_sync(
+              gmask, static_cast<uint32_t>(acc[0][e] >> 32), src, G);
+          const uint32_t b_lo = __shfl_sync(
+              gmask, static_cast<uint32_t>(acc[1][e]), src, G);
+          const uint32_t b_hi = __shfl_sync(
+              gmask, static_cast<uint32_t>(acc[1][e] >> 32), src, G);
+          piece[e] = odd ? PackBits(b_lo, b_hi) : PackBits(a_lo, a_hi);
+        }
+        Store32B(out + q * 8, piece[0], piece[1], piece[2], piece[3]);
+      }
+#pragma unroll
+      for (int v = 0; v < V; ++v)
+#pragma unroll
+        for (int e = 0; e < PPV; ++e) acc[v][e] = 0;
+      *wsum = 0.0f;
+      return;
+    }
+  }
 #pragma unroll
   for (int v = 0; v < V; ++v) {
     const int k = WIDE ? gl * V + v : gl + v * G;
