@@ -19,6 +19,7 @@
 #include <cinttypes>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -507,10 +508,28 @@ void PollTrials(PoolTuner* t) {
 
 // Sets p->kernel_choice for a launch of `engine`; returns the trial to time
 // (events created, choice set) or a trial with null events.
+// XSE_POOL_KERNEL=streaming or =staged in the environment fixes the choice
+// for every tunable launch (profiling one kernel on purpose: under a
+// profiler that serialises kernels the tuner's timings mean nothing).
+int32_t ForcedPoolKernel() {
+  static const int32_t forced = [] {
+    const char* v = std::getenv("XSE_POOL_KERNEL");
+    if (v == nullptr) return static_cast<int32_t>(xse::kPoolAuto);
+    if (std::strcmp(v, "streaming") == 0) return static_cast<int32_t>(xse::kPoolStreaming);
+    if (std::strcmp(v, "staged") == 0) return static_cast<int32_t>(xse::kPoolStaged);
+    return static_cast<int32_t>(xse::kPoolAuto);
+  }();
+  return forced;
+}
+
 PoolTrial ChoosePoolKernel(xse_engine* engine, const xse::Layout& l,
                            xse::PoolParams* p, uint64_t* key) {
   PoolTrial trial{xse::kPoolAuto, nullptr, nullptr};
   if (!xse::PoolKernelTunable(l, p->total_tasks)) return trial;
+  if (ForcedPoolKernel() != xse::kPoolAuto) {
+    p->kernel_choice = ForcedPoolKernel();
+    return trial;
+  }
   *key = TuneKey(l, *p);
   std::lock_guard<std::mutex> lock(engine->tune_mu);
   if (engine->tuners.size() >= kTuneMaxSignatures &&
