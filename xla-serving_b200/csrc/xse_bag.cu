@@ -580,6 +580,67 @@ __device__ __forceinline__ void GatherBatch(
   }
 }
 
+// A chunk in which some ids contribute nothing (another row-wise shard's
+// rows, or invalid ids under fused checks): the contributing positions are
+// found with one ballot and gathered U at a time, so a chunk costs one
+// memory round trip per U contributing rows rather than per U positions
+// (on a row-wise shard of W ranks only about 1/W of the ids are local).
+// Adds stay in CSR order; weight sums still count every position.
+template <int DT, int G, int V, bool EXACT, bool WIDE, int WM, int U, bool L1,
+          typename Hook>
+__device__ __forceinline__ void SparseChunk(
+    const BagDesc& d, const uint4* rows, int row_vecs, int gl, unsigned gmask,
+    int my_row, float my_w, int cnt,
+    u64 (&acc)[V][ElemsPerVec<DT>::value / 2], float* wsum, float* bsum,
+    Hook&& hook) {
+  const int stride = EXACT ? G * V : row_vecs;
+  const int lane = threadIdx.x & 31;
+  unsigned m = __ballot_sync(gmask, gl < cnt && my_row >= 0);
+  m = (m >> (lane - gl)) & (G == 32 ? 0xffffffffu : ((1u << G) - 1u));
+  if constexpr (WM == kWeightedNorm) {
+    for (int j = 0; j < cnt; ++j) {
+      AddWeight<WM>(wsum, __shfl_sync(gmask, my_w, j, G), d.combine);
+    }
+  }
+  bool hooked = false;
+  while (m != 0) {
+    uint4 raw[U][V];
+    float2 sb[U];
+    int pos[U];
+    int n = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      pos[u] = m != 0 ? __ffs(m) - 1 : 0;
+      if (m != 0) {
+        m &= m - 1;
+        n = u + 1;
+      }
+      const int r = __shfl_sync(gmask, my_row, pos[u], G);
+      if (u < n) {
+        if constexpr (DT == 2) sb[u] = __ldg(d.scale_bias + r);
+        LoadLaneRow<G, V, EXACT, WIDE, L1>(
+            rows + static_cast<int64_t>(r) * stride, gl, row_vecs, raw[u]);
+      }
+    }
+    if (!hooked) {
+      hook();  // runs while the first batch's rows are in flight
+      hooked = true;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float w = 1.0f;
+      if constexpr (WM != kUnweighted) {
+        w = __shfl_sync(gmask, my_w, pos[u], G);
+      }
+      if (u < n) {
+        AddGathered<DT, V, WM>(acc, raw[u],
+                               DT == 2 ? sb[u] : make_float2(0, 0), w, bsum);
+      }
+    }
+  }
+  if (!hooked) hook();
+}
+
 // 1: lanes holding 8 or 16 output floats store them with 32-byte stores.
 #ifndef XSE_POOL_WIDE_STORES
 #define XSE_POOL_WIDE_STORES 1
@@ -847,11 +908,15 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
                 d, rows, row_vecs, gl, gmask, my_row, my_w, j0, cnt, acc,
                 &wsum, &bsum, prefetch);
           }
-        }
-        for (; j0 < cnt; j0 += U) {
-          const int n = cnt - j0 < U ? cnt - j0 : U;
-          GatherBatch<DT, G, V, EXACT, WIDE, WM, U, kL1>(
-              d, rows, row_vecs, gl, gmask, my_row, my_w, j0, n, acc, &wsum,
+          for (; j0 < cnt; j0 += U) {
+            const int n = cnt - j0 < U ? cnt - j0 : U;
+            GatherBatch<DT, G, V, EXACT, WIDE, WM, U, kL1>(
+                d, rows, row_vecs, gl, gmask, my_row, my_w, j0, n, acc,
+                &wsum, &bsum, prefetch);
+          }
+        } else {
+          SparseChunk<DT, G, V, EXACT, WIDE, WM, 1, kL1>(
+              d, rows, row_vecs, gl, gmask, my_row, my_w, cnt, acc, &wsum,
               &bsum, prefetch);
         }
       }
