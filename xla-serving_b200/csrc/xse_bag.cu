@@ -88,10 +88,16 @@ struct ElemsPerVec<2> {
 #ifndef XSE_POOL_CHUNK_PREFETCH
 #define XSE_POOL_CHUNK_PREFETCH 1
 #endif
-// Chunk prefetch of int8 rows: 0 off (next-batch L2 prefetch), 1 into L2,
-// 2 into L1.
+// Chunk prefetch of int8 rows: 0 off, 1 into L2, 2 into L1.
 #ifndef XSE_POOL_I8_CHUNK_PREFETCH
 #define XSE_POOL_I8_CHUNK_PREFETCH 0
+#endif
+// Next-batch L2 prefetch of int8 rows: off. With the wide int8 lanes it cost
+// more issue slots than it saved latency (int8 row-wise workload, pooling
+// per step: 2.60 ms with it, 2.40 ms without; the chunk prefetch into L2:
+// 3.37 ms).
+#ifndef XSE_POOL_I8_PREFETCH
+#define XSE_POOL_I8_PREFETCH 0
 #endif
 
 #ifndef XSE_POOL_I8_ROWS
@@ -825,7 +831,9 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
       : DT == 2 ? XSE_POOL_I8_CHUNK_PREFETCH
                 : (XSE_POOL_CHUNK_PREFETCH != 0 ? (kL1 ? 2 : 1) : 0);
   constexpr bool kChunkPrefetch = kChunkPrefetchTo != 0;
-  constexpr bool kBatchPrefetch = XSE_POOL_PREFETCH != 0 && !kChunkPrefetch;
+  constexpr bool kBatchPrefetch =
+      (DT == 2 ? XSE_POOL_I8_PREFETCH : XSE_POOL_PREFETCH) != 0 &&
+      !kChunkPrefetch;
 
   const int lane = threadIdx.x & 31;
   const int gl = lane % G;
@@ -1365,7 +1373,9 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
   constexpr int kNs = kInteractSlots;
   constexpr bool kL1 = XSE_INTERACT_L1 != 0;
   constexpr bool kChunkPrefetch = XSE_INTERACT_CHUNK_PREFETCH != 0;
-  constexpr bool kBatchPrefetch = XSE_POOL_PREFETCH != 0 && !kChunkPrefetch;
+  constexpr bool kBatchPrefetch =
+      (DT == 2 ? XSE_POOL_I8_PREFETCH : XSE_POOL_PREFETCH) != 0 &&
+      !kChunkPrefetch;
   EnterDependent();
   if (!p.fused_checks && p.status->group_error != 0) return;
   extern __shared__ float4 smem_vec[];
