@@ -1406,7 +1406,7 @@ def measure_dlrm_lookup(xse, args, world, local):
   examples = sum_over_ranks(REF_BATCH * args.steps, world)
   peak, peak_kind = measured_peaks()
   achieved = wl.bytes_per_step() / (pool_ms / 1000.0) / 1e9
-  threads = 4
+  threads = args.lookup_threads
   host = DenseLookupHostInputs(xse, wl, REF_BATCH_REQ)
   host.run(2 * threads, threads)
   barrier(world, local)
@@ -1690,6 +1690,9 @@ def main():
   ap.add_argument("--e2e-threads", type=int, default=E2E_THREADS,
                   help="concurrent host callers of the operator in the e2e "
                        "run")
+  ap.add_argument("--lookup-threads", type=int, default=4,
+                  help="concurrent host callers of the dense-lookup operator "
+                       "in dlrm_lookup's end-to-end run")
   ap.add_argument("--cpu-seconds", type=float, default=10.0)
   ap.add_argument("--no-cpu-baseline", action="store_true",
                   help="skip the CPU baselines and the parity checks")

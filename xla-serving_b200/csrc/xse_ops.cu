@@ -752,11 +752,17 @@ int RunGroup(xse_engine* engine, StagingPool* staging_pool,
   char* dev_csr = dev_out + AlignUp(out_bytes, 256);
   // Inputs already in pinned memory go straight to the device; the others
   // are gathered into the pinned staging block and sent in one transfer.
+  // Small calls (a serving request of a few hundred examples) gather every
+  // input, pinned or not, and get their dense_lookup row pointers written
+  // by the host: one transfer instead of a DMA per buffer and a launch per
+  // feature, whose host-side cost is far above the copy's.
+  constexpr size_t kGatherAllBytes = static_cast<size_t>(1) << 20;
+  const bool gather_all = in_bytes <= kGatherAllBytes;
   cudaError_t e = cudaSuccess;
   size_t lo = SIZE_MAX, hi = 0;
   auto stage = [&](const void* src, size_t at, size_t bytes) {
     if (bytes == 0 || e != cudaSuccess) return;
-    if (IsPinned(src)) {
+    if (!gather_all && IsPinned(src)) {
       e = cudaMemcpyAsync(dev_in + at, src, bytes, cudaMemcpyHostToDevice,
                           stream);
     } else {
@@ -765,11 +771,22 @@ int RunGroup(xse_engine* engine, StagingPool* staging_pool,
       hi = std::max(hi, at + bytes);
     }
   };
+  std::vector<bool> host_rp(n, false);
   for (size_t i = 0; i < n; ++i) {
     const Prepared& p = prep[i];
     stage(p.ids, ids_at[i], p.num_ids * (p.ids_type == XSE_INDEX_I64 ? 8 : 4));
     if (p.row_pointers != nullptr) {
       stage(p.row_pointers, rp_at[i], p.num_row_pointers * 4);
+    } else if (gather_all && !p.device_csr && p.device_rp_valency >= 0) {
+      // dense_lookup row pointers b * valency (int32 range checked when the
+      // call was prepared).
+      int32_t* rp = reinterpret_cast<int32_t*>(host_in + rp_at[i]);
+      for (int64_t b = 0; b <= p.batch_size; ++b) {
+        rp[b] = static_cast<int32_t>(b * p.device_rp_valency);
+      }
+      lo = std::min(lo, rp_at[i]);
+      hi = std::max(hi, rp_at[i] + static_cast<size_t>(p.batch_size + 1) * 4);
+      host_rp[i] = true;
     }
     stage(p.weights, w_at[i], p.num_weights * 4);
   }
@@ -787,7 +804,7 @@ int RunGroup(xse_engine* engine, StagingPool* staging_pool,
           p.batch_size, p.dense_seq, p.pad_value, rp,
           reinterpret_cast<int64_t*>(dev_csr + csr_at[i]),
           dev_csr + scratch_at[i], scratch_bytes[i], stream);
-    } else if (p.device_rp_valency >= 0) {
+    } else if (p.device_rp_valency >= 0 && !host_rp[i]) {
       e = xse::LaunchRowPointers(rp, p.batch_size, p.device_rp_valency,
                                  stream);
     }
@@ -1248,7 +1265,8 @@ int xse_lookup_transform_run(xse_lookup_transform* t,
                     "Batch volume (batch_size * valency) exceeds INT32_MAX "
                     "bounds.");
       }
-      // Row pointers b * valency, generated on the device.
+      // Row pointers b * valency, generated on the device (by the host for
+      // calls small enough to go in one transfer).
       p.device_rp_valency = valency;
       p.row_pointers = nullptr;
       p.num_row_pointers = p.batch_size + 1;
