@@ -53,7 +53,7 @@ def full_pooled(step):
   return out
 
 
-def run_rank(xse, rank, world, mode, steps=3):
+def run_rank(xse, rank, world, mode, steps=5):
   """Builds this rank's engine and exchange, runs `steps` steps (different
   inputs each) and returns the outputs of every step as numpy arrays."""
   sharding = xse.sharding
@@ -85,8 +85,14 @@ def run_rank(xse, rank, world, mode, steps=3):
                      None if weights is None else
                      torch.from_numpy(weights).cuda()))
     keep.append(feats)
-    out = ex.run(ex.prepare(feats))
-    outs.append(out.clone())  # queued before the next run: slot reuse rule
+    # Deferred steps (the next step's pooling overlaps this step's exchange)
+    # except the last; readers are queued after ready(), before the next
+    # run (the slot reuse rule). Five steps rotate the peer mode's three
+    # output slots past their first reuse.
+    last = step == steps - 1
+    out = ex.run(ex.prepare(feats), defer=not last and step % 2 == 0)
+    ex.ready()
+    outs.append(out.clone())
   ex.check()
   result = [o.cpu().numpy() for o in outs]
   ex.close()

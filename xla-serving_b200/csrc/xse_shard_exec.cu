@@ -272,7 +272,10 @@ int RunPeer(xse_shard_exchange* ex, const xse_bag_request* f, int32_t flags,
   // queued that step's readers before its pooling of step i - 2, which the
   // barrier of step i - 2 waited for on every rank.
   const int32_t prev = static_cast<int32_t>((i + 1) % ex->slots);
-  if (i >= 2 && ex->done_valid[prev]) {
+  // A barrier that has already completed needs no wait node on the stream.
+  if (i >= 2 && ex->done_valid[prev] &&
+      cudaEventQuery(ex->done[prev]) != cudaSuccess) {
+    (void)cudaGetLastError();  // cudaErrorNotReady is not an error here
     cudaError_t e = cudaStreamWaitEvent(stream, ex->done[prev], 0);
     if (e != cudaSuccess) return xse::CudaFail(e, "slot reuse wait");
   }
