@@ -220,12 +220,24 @@ def sum_over_ranks(value, world):
   return float(t.item())
 
 
+def align_streams(world):
+  """Lines the ranks' streams up before a timed region: a one-element NCCL
+  all-reduce ends on every GPU at about the same moment, so the start events
+  recorded right after it fire together (after a host barrier the ranks'
+  host threads wake up tens to hundreds of microseconds apart, and a rank
+  that starts early waits for the others inside its timed steps)."""
+  if world > 1:
+    t = torch.zeros(1, device="cuda")
+    dist.all_reduce(t)
+
+
 def timed_steps(step, first, count, world, local, finish=None):
   """`count` steps between CUDA events on the current stream, with a barrier
   and a synchronize on both sides; returns (max-over-ranks ms, launches)."""
   torch.cuda.synchronize()
   barrier(world, local)
   torch.cuda.synchronize()
+  align_streams(world)
   stream = torch.cuda.current_stream()
   start = torch.cuda.Event(enable_timing=True)
   end = torch.cuda.Event(enable_timing=True)
