@@ -66,6 +66,9 @@ BAG = 20
 SEED = 0
 ROTATE = 8  # distinct input/output sets cycled between steps (> L2 in all)
 E2E_THREADS = 2  # concurrent host callers of the operator in the e2e run
+# A config's operator e2e run times about this long (calls sized from a
+# warm-up run), so that starting the caller threads stays a small share.
+E2E_TARGET_MS = 100.0
 MIN_WARMUP = 3
 # Pooling launches timed with CUDA events in the kernel-timing pass.
 KERNEL_TIMING_LAUNCHES = 24
@@ -903,9 +906,11 @@ def measure_config(xse, args, name, world, rank, local, max_rows=None):
         xse, wl.tables,
         [[(f[1], f[2], f[3]) for f in feats] for feats in wl.inputs],
         cfg["batch"], cfg["dim"])
-    host.run(2 * E2E_THREADS, E2E_THREADS)
+    warm = 4 * E2E_THREADS
+    per_call = host.run(warm, E2E_THREADS) / warm
+    per_call = max_over_ranks(per_call, world)
+    e_steps = int(min(2000, max(16, E2E_TARGET_MS / max(per_call, 1e-3))))
     barrier(world, local)
-    e_steps = max(4, min(args.e2e_steps, 4 * args.steps) // 8)
     e_ms = max_over_ranks(host.run(e_steps, E2E_THREADS), world)
     e_path = ("CpuEmbeddingLookupTransform (xse_lookup_transform_run, C "
               f"ABI) over {len(wl.local)} features with pinned host "

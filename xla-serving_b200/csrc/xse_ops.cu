@@ -76,21 +76,23 @@ class PinnedPool {
   // Returns a block of at least `bytes` with one reference.
   PinnedBlock* Acquire(size_t bytes) {
     const size_t cls = SizeClass(bytes);
-    std::lock_guard<std::mutex> lock(mu_);
-    auto& free_list = free_[cls];
-    PinnedBlock* b = nullptr;
-    if (!free_list.empty()) {
-      b = free_list.back();
-      free_list.pop_back();
-    } else {
-      void* p = nullptr;
-      if (cudaHostAlloc(&p, cls, cudaHostAllocDefault) != cudaSuccess) {
-        return nullptr;
+    {
+      std::lock_guard<std::mutex> lock(mu_);
+      auto& free_list = free_[cls];
+      if (!free_list.empty()) {
+        PinnedBlock* b = free_list.back();
+        free_list.pop_back();
+        b->refs = 1;
+        return b;
       }
-      b = new PinnedBlock{p, cls, 0};
     }
-    b->refs = 1;
-    return b;
+    // A new block is allocated outside the lock: cudaHostAlloc takes
+    // milliseconds, and other callers' acquires and releases go on meanwhile.
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, cls, cudaHostAllocDefault) != cudaSuccess) {
+      return nullptr;
+    }
+    return new PinnedBlock{p, cls, 1};
   }
 
   void Retain(PinnedBlock* b, void* data) {
@@ -755,9 +757,21 @@ int RunGroup(xse_engine* engine, StagingPool* staging_pool,
   // Small calls (a serving request of a few hundred examples) gather every
   // input, pinned or not, and get their dense_lookup row pointers written
   // by the host: one transfer instead of a DMA per buffer and a launch per
-  // feature, whose host-side cost is far above the copy's.
+  // feature. That pays while the host copy (about 64 KiB per transfer or
+  // launch saved, at a few microseconds each) costs less than what it
+  // saves; a call of one or two large buffers sends them directly.
   constexpr size_t kGatherAllBytes = static_cast<size_t>(1) << 20;
-  const bool gather_all = in_bytes <= kGatherAllBytes;
+  constexpr size_t kGatherBytesPerSaving = static_cast<size_t>(64) << 10;
+  size_t savings = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const Prepared& p = prep[i];
+    savings += (p.num_ids > 0) + (p.num_weights > 0) +
+               (p.row_pointers != nullptr ||
+                (!p.device_csr && p.device_rp_valency >= 0));
+  }
+  const bool gather_all =
+      in_bytes <= std::min(kGatherAllBytes,
+                           kGatherBytesPerSaving * (savings > 0 ? savings - 1 : 0));
   cudaError_t e = cudaSuccess;
   size_t lo = SIZE_MAX, hi = 0;
   auto stage = [&](const void* src, size_t at, size_t bytes) {
