@@ -414,6 +414,17 @@ __device__ __forceinline__ float BagScale(int combine, bool weighted,
                       : __fdiv_rn(1.0f, __fsqrt_rn(denom));
 }
 
+// Output row of bag `bag` of descriptor d (blocked outputs: see
+// BagDesc::block_bags; block indexes fit 32 bits).
+__device__ __forceinline__ float* BagOut(const PoolParams& p, const BagDesc& d,
+                                         int64_t bag) {
+  if (d.block_bags <= 0) return d.out + bag * d.out_stride;
+  const uint32_t j = static_cast<uint32_t>(bag) /
+                     static_cast<uint32_t>(d.block_bags);
+  return p.block_base[j] + d.out_offset +
+         (bag - static_cast<int64_t>(j) * d.block_bags) * d.out_stride;
+}
+
 // Locates the descriptor of `task`; descriptors are ordered by task_begin and
 // every group walks its tasks in increasing order, so the search only moves
 // forward.
@@ -928,7 +939,7 @@ __device__ __forceinline__ void PoolBody(const PoolParams& p, int64_t task_lo,
               &bsum, prefetch);
         }
       }
-      FinishBag<DT, G, V, EXACT, true, WIDE>(d, d.out + bag * d.out_stride,
+      FinishBag<DT, G, V, EXACT, true, WIDE>(d, BagOut(p, d, bag),
                                              d.vec_out, end - begin,
                                              WM != kUnweighted, acc, &wsum,
                                              gl, row_vecs, &bsum);
@@ -1179,7 +1190,7 @@ __device__ __forceinline__ void StagedBody(const PoolParams& p,
           }
         }
       }
-      FinishBag<DT, G, 1, true, true>(d, d.out + bag * d.out_stride,
+      FinishBag<DT, G, 1, true, true>(d, BagOut(p, d, bag),
                                       d.vec_out, end - begin,
                                       WM != kUnweighted, acc, &wsum, gl, G,
                                       &bsum);
@@ -1660,7 +1671,7 @@ __global__ void __launch_bounds__(kThreads)
       for (int k = 0; k < kCols; ++k) {
         const int c = c0 + lane + 32 * k;
         if (c < d.dim) {
-          d.out[bag * d.out_stride + c] =
+          BagOut(p, d, bag)[c] =
               (n > 0 && d.combine != 1) ? __fmul_rn(acc[k], s) : acc[k];
         }
       }

@@ -582,10 +582,13 @@ class DeviceGuard {
 
 // `inter` non-null: the pooled rows feed the dot interaction (the requests'
 // outputs are not used) -- the fused kernel where one serves the layout,
-// else pooling into scratch and the interaction kernel.
+// else pooling into scratch and the interaction kernel. `parts` non-null:
+// the parts are pooled instead of `reqs` (whose outputs are not used), and
+// `reqs` are validated only when parts->validate asks for it.
 int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
                  cudaStream_t stream, int32_t flags, xse_status* st,
-                 const xse::InteractArgs* inter = nullptr) {
+                 const xse::InteractArgs* inter = nullptr,
+                 const xse::PartSet* parts = nullptr) {
   g_last_launches = 0;
   if (n <= 0 || reqs == nullptr) {
     return SetError(XSE_INVALID_ARGUMENT,
@@ -668,7 +671,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
       m.code = code;
       m.message = buf;
     };
-    if (r.output == nullptr && inter == nullptr) {
+    if (r.output == nullptr && inter == nullptr && parts == nullptr) {
       early(kStageEarly, XSE_INVALID_ARGUMENT,
             "FP32 embedding-bag request %d requires an output allocator.",
             false);
@@ -763,10 +766,69 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
                       static_cast<long long>(width));
     }
   }
+  // The parts' descriptors: their whole request's, with the part's bags
+  // and output (a part's slot is its whole request's).
+  std::vector<xse::BagDesc> part_descs;
+  std::vector<std::shared_ptr<Table>> part_tables;
+  if (parts != nullptr && !any_early) {
+    part_descs.reserve(static_cast<size_t>(parts->n));
+    part_tables.reserve(static_cast<size_t>(parts->n));
+    for (int32_t j = 0; j < parts->n; ++j) {
+      const xse_bag_request& r = parts->reqs[j];
+      const int32_t o = parts->owner[j];
+      if (o < 0 || o >= n || r.output == nullptr || r.offsets == nullptr ||
+          r.num_offsets < 2 || r.offsets_type != reqs[o].offsets_type ||
+          r.output_stride < 0 ||
+          (r.output_stride != 0 && r.output_stride < tables[o]->dim)) {
+        return SetError(XSE_INTERNAL, "malformed part %d of an execution", j);
+      }
+      xse::BagDesc d = descs[static_cast<size_t>(o)];
+      d.offsets = r.offsets;
+      d.num_bags = r.num_offsets - 1;
+      d.out = r.output;
+      d.out_stride = r.output_stride > 0 ? r.output_stride : tables[o]->dim;
+      d.vec_out = static_cast<int8_t>(
+          (reinterpret_cast<uintptr_t>(r.output) & 15u) == 0 &&
+          d.out_stride % 4 == 0);
+      part_descs.push_back(d);
+      part_tables.push_back(tables[o]);
+    }
+    if (parts->blocks > 0) {
+      // One blocked descriptor per whole request instead of one per part.
+      if (parts->blocks > xse::kMaxOutBlocks || parts->block_bags <= 0 ||
+          parts->block_base == nullptr || parts->block_offset == nullptr ||
+          parts->block_stride <= 0 ||
+          parts->block_bags * parts->blocks > INT32_MAX) {
+        return SetError(XSE_INTERNAL, "malformed blocked execution");
+      }
+      bool aligned = parts->block_stride % 4 == 0;
+      for (int32_t j = 0; j < parts->blocks; ++j) {
+        aligned = aligned &&
+                  (reinterpret_cast<uintptr_t>(parts->block_base[j]) & 15u) == 0;
+      }
+      part_descs.clear();
+      for (int32_t k = 0; k < n; ++k) {
+        xse::BagDesc d = descs[static_cast<size_t>(k)];
+        if (d.num_bags != parts->block_bags * parts->blocks ||
+            parts->block_stride < d.dim) {
+          return SetError(XSE_INTERNAL, "malformed blocked execution");
+        }
+        d.block_bags = parts->block_bags;
+        d.out_offset = parts->block_offset[k];
+        d.out = parts->block_base[0] + d.out_offset;
+        d.out_stride = parts->block_stride;
+        d.vec_out = static_cast<int8_t>(aligned && d.out_offset % 4 == 0);
+        part_descs.push_back(d);
+      }
+    }
+  }
   std::string iso_message;
   int iso_code = XSE_OK;
   if (!any_early && inter == nullptr) {
-    iso_code = CheckIsolation(reqs, tables, n, &iso_message);
+    iso_code = parts != nullptr
+                   ? CheckIsolation(parts->reqs, part_tables, parts->n,
+                                    &iso_message)
+                   : CheckIsolation(reqs, tables, n, &iso_message);
   }
 
   // Clear this execution's slot: the whole ring when an asynchronous run of
@@ -788,7 +850,9 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
   // Validation pass over every descriptor (strict mode, or whenever the
   // group is known to fail and only its error order is needed).
   int launches = 0;
-  if (!fused || validate_only || any_soft) {
+  const bool validate =
+      parts == nullptr || parts->validate || validate_only || any_soft;
+  if ((!fused || validate_only || any_soft) && validate) {
     for (size_t base = 0; base < descs.size();
          base += xse::kMaxDescsPerLaunch) {
       xse::PoolParams p{};
@@ -838,7 +902,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
       std::map<std::tuple<int, int, int, bool, int>,
                std::vector<xse::BagDesc>>
           groups;
-      for (const xse::BagDesc& d : descs) {
+      for (const xse::BagDesc& d : parts != nullptr ? part_descs : descs) {
         const xse::Layout l = layout_of(d);
         // One launch per layout; its weighting modes share it.
         groups[{l.dtype, l.g, l.v, l.exact, l.wide ? 1 : 0}].push_back(d);
@@ -852,6 +916,11 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
           xse::PoolParams p{};
           p.status = dev_status;
           p.fused_checks = fused ? 1 : 0;
+          if (parts != nullptr && parts->blocks > 0) {
+            for (int32_t j = 0; j < parts->blocks; ++j) {
+              p.block_base[j] = parts->block_base[j];
+            }
+          }
           const size_t cnt =
               std::min<size_t>(xse::kMaxDescsPerLaunch, list.size() - base);
           int64_t tasks = 0;
@@ -2073,3 +2142,19 @@ extern "C" int xse_engine_execute_legacy(xse_engine* engine,
   }
   return SetError(XSE_INTERNAL, "legacy execution failed");
 }
+
+namespace xse {
+
+int ExecuteParts(xse_engine* engine, const xse_bag_request* whole, int32_t n,
+                 const PartSet& parts, cudaStream_t stream, int32_t flags,
+                 xse_status* status) {
+  TraceRange trace("xse.execute_parts");
+  if (engine == nullptr || status == nullptr || parts.reqs == nullptr ||
+      parts.owner == nullptr) {
+    return SetError(XSE_INVALID_ARGUMENT, "null argument");
+  }
+  return ExecuteBatch(engine, whole, n, stream, flags, status, nullptr,
+                      &parts);
+}
+
+}  // namespace xse

@@ -23,6 +23,9 @@ class TraceRange {
 // Descriptors passed by value in one launch (kernel parameter space holds up
 // to 32 KB on sm_70+ with CUDA 12.1+).
 constexpr int kMaxDescsPerLaunch = 64;
+// Sample blocks of one descriptor written to separate places (a sharded
+// step's destinations); see BagDesc::block_bags.
+constexpr int kMaxOutBlocks = 8;
 
 // One pooling request as the kernels see it.
 struct BagDesc {
@@ -33,6 +36,10 @@ struct BagDesc {
   const float* weights;       // nullptr when unweighted
   float* out;                 // bag b at out + b * out_stride
   int64_t out_stride;
+  // > 0: blocked output instead -- bag b at PoolParams::block_base[j] +
+  // out_offset + (b - j * block_bags) * out_stride, j = b / block_bags.
+  int64_t block_bags;
+  int64_t out_offset;
   int64_t vocab;              // global rows; valid ids are [0, vocab)
   int64_t row_begin;          // shard window [row_begin, row_end)
   int64_t row_end;
@@ -92,6 +99,7 @@ struct PoolParams {
   // kPoolAuto, kPoolStreaming (PoolVecKernel) or kPoolStaged
   // (PoolStagedKernel).
   int32_t kernel_choice;
+  float* block_base[kMaxOutBlocks];  // blocked outputs (BagDesc::block_bags)
   BagDesc d[kMaxDescsPerLaunch];
 };
 
@@ -228,6 +236,42 @@ cudaError_t LaunchRowPointers(int32_t* rp, int64_t batch, int64_t valency,
 
 // Sets what xse_last_launch_count() reports for this thread.
 void SetLastLaunchCount(int32_t launches);
+
+}  // namespace xse
+
+#include "../../include/xse_emb.h"
+
+namespace xse {
+
+// Slices of whole requests: part j pools a contiguous range of the bags of
+// whole request owner[j] (its offsets point into the whole request's row
+// pointers; ids, weights and feature are the whole request's) into its own
+// output. The sharded executor sends each destination's sample block to a
+// different place this way.
+struct PartSet {
+  const xse_bag_request* reqs;
+  const int32_t* owner;
+  int32_t n;
+  bool validate;  // run the validation pass over the whole requests
+  // Blocked form (blocks > 0; the parts must describe the same outputs and
+  // are then only used for the isolation check): every whole request k is
+  // cut into `blocks` sample blocks of block_bags, block j written at
+  // block_base[j] + block_offset[k] with rows block_stride floats apart.
+  // The kernels then see one descriptor per whole request.
+  int32_t blocks = 0;
+  int64_t block_bags = 0;
+  float* const* block_base = nullptr;
+  const int64_t* block_offset = nullptr;
+  int64_t block_stride = 0;
+};
+
+// ExecuteBatch over `whole` (the status block's requests: its errors name
+// whole requests) that pools `parts` instead of the whole requests. The
+// validation pass, when it runs, reads every whole request once, not once
+// per part.
+int ExecuteParts(xse_engine* engine, const xse_bag_request* whole, int32_t n,
+                 const PartSet& parts, cudaStream_t stream, int32_t flags,
+                 xse_status* status);
 
 }  // namespace xse
 

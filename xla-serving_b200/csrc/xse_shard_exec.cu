@@ -217,7 +217,10 @@ struct xse_shard_exchange {
   int64_t step = -1;
   int32_t slot = 0;
   bool pending_ready = false;
-  std::vector<xse_bag_request> reqs;
+  std::vector<xse_bag_request> reqs;  // sample blocks of the feature requests
+  std::vector<int32_t> owner;          // feature request of each block
+  std::vector<float*> block_base;      // peer mode: destinations' slots
+  std::vector<int64_t> block_offset;   // peer mode: feature k's column
 };
 
 namespace {
@@ -246,10 +249,45 @@ float* OutSlot(xse_shard_exchange* ex, int32_t peer, int32_t slot) {
   return reinterpret_cast<float*>(base) + slot * ex->out_floats;
 }
 
-int Execute(xse_shard_exchange* ex, cudaStream_t stream) {
-  return xse_engine_execute_batch(ex->engine, ex->reqs.data(),
-                                  static_cast<int32_t>(ex->reqs.size()),
-                                  stream, XSE_EXEC_ASYNC, ex->status);
+void ClearBlocks(xse_shard_exchange* ex) {
+  ex->reqs.clear();
+  ex->owner.clear();
+}
+
+void AddBlock(xse_shard_exchange* ex, int32_t k, const xse_bag_request& r) {
+  ex->reqs.push_back(r);
+  ex->owner.push_back(k);
+}
+
+// Pools the blocks in ex->reqs. The feature requests `f` are the execution's
+// requests: errors name feature k, and the validation pass (when `validate`;
+// the first execution of a step) reads each feature's ids once, however many
+// blocks it is cut into.
+int Execute(xse_shard_exchange* ex, const xse_bag_request* f, int32_t n,
+            bool validate, cudaStream_t stream) {
+  xse::PartSet parts{ex->reqs.data(), ex->owner.data(),
+                     static_cast<int32_t>(ex->reqs.size()), validate};
+  return xse::ExecuteParts(ex->engine, f, n, parts, stream, XSE_EXEC_ASYNC,
+                           ex->status);
+}
+
+// Peer mode: every feature's block for destination d lands in d's slot at
+// the feature's column, so the kernels take one blocked descriptor per
+// feature (instead of one per feature and destination).
+int ExecuteBlocked(xse_shard_exchange* ex, const xse_bag_request* f,
+                   int32_t n, cudaStream_t stream) {
+  xse::PartSet parts{ex->reqs.data(), ex->owner.data(),
+                     static_cast<int32_t>(ex->reqs.size()), true};
+  if (ex->world > 1 && ex->world <= xse::kMaxOutBlocks) {
+    parts.blocks = ex->world;
+    parts.block_bags = ex->block;
+    parts.block_base = ex->block_base.data();
+    parts.block_offset = ex->block_offset.data();
+    parts.block_stride =
+        static_cast<int64_t>(ex->plan.num_tables) * ex->plan.dim;
+  }
+  return xse::ExecuteParts(ex->engine, f, n, parts, stream, XSE_EXEC_ASYNC,
+                           ex->status);
 }
 
 int SideAfter(xse_shard_exchange* ex, cudaStream_t stream) {
@@ -280,17 +318,23 @@ int RunPeer(xse_shard_exchange* ex, const xse_bag_request* f, int32_t flags,
     if (e != cudaSuccess) return xse::CudaFail(e, "slot reuse wait");
   }
   const int32_t w = ex->world, d_ = ex->plan.dim, t = ex->plan.num_tables;
-  ex->reqs.clear();
+  ClearBlocks(ex);
+  ex->block_base.assign(static_cast<size_t>(w), nullptr);
+  ex->block_offset.assign(static_cast<size_t>(ex->num_local), 0);
+  for (int32_t k = 0; k < ex->num_local; ++k) {
+    ex->block_offset[k] = static_cast<int64_t>(ex->rank + k * w) * d_;
+  }
   for (int32_t dest = 0; dest < w; ++dest) {
     float* slot_base = OutSlot(ex, dest, slot);
+    ex->block_base[dest] = slot_base;
     for (int32_t k = 0; k < ex->num_local; ++k) {
-      const int32_t g = ex->rank + k * w;
-      ex->reqs.push_back(Slice(f[k], dest * ex->block, ex->block,
-                               slot_base + static_cast<int64_t>(g) * d_,
-                               static_cast<int64_t>(t) * d_));
+      AddBlock(ex, k,
+               Slice(f[k], dest * ex->block, ex->block,
+                     slot_base + ex->block_offset[k],
+                     static_cast<int64_t>(t) * d_));
     }
   }
-  int code = Execute(ex, stream);
+  int code = ExecuteBlocked(ex, f, ex->num_local, stream);
   if (code != XSE_OK) return code;
   if (w > 1) {
     code = SideAfter(ex, stream);
@@ -355,25 +399,27 @@ void BlockRequests(xse_shard_exchange* ex, const xse_bag_request* f,
   for (int32_t k = 0; k < ex->num_local; ++k) {
     if (dest == ex->rank) {
       const int32_t g = ex->rank + k * w;
-      ex->reqs.push_back(Slice(f[k], dest * ex->block, ex->block,
-                               ex->out_local + static_cast<int64_t>(g) * d_,
-                               static_cast<int64_t>(t) * d_));
+      AddBlock(ex, k,
+               Slice(f[k], dest * ex->block, ex->block,
+                     ex->out_local + static_cast<int64_t>(g) * d_,
+                     static_cast<int64_t>(t) * d_));
     } else {
       float* base = ex->send + dest * ex->block * ex->num_local * d_;
-      ex->reqs.push_back(Slice(f[k], dest * ex->block, ex->block,
-                               base + static_cast<int64_t>(k) * d_,
-                               static_cast<int64_t>(ex->num_local) * d_));
+      AddBlock(ex, k,
+               Slice(f[k], dest * ex->block, ex->block,
+                     base + static_cast<int64_t>(k) * d_,
+                     static_cast<int64_t>(ex->num_local) * d_));
     }
   }
 }
 
 int RunA2A(xse_shard_exchange* ex, const xse_bag_request* f,
            cudaStream_t stream) {
-  ex->reqs.clear();
+  ClearBlocks(ex);
   for (int32_t dest = 0; dest < ex->world; ++dest) {
     BlockRequests(ex, f, dest);
   }
-  int code = Execute(ex, stream);
+  int code = Execute(ex, f, ex->num_local, true, stream);
   if (code != XSE_OK || ex->world == 1) return code;
   const xse::NcclApi& n = xse::Nccl();
   const int64_t send_floats =
@@ -401,16 +447,16 @@ int RunPipelined(xse_shard_exchange* ex, const xse_bag_request* f,
   for (int32_t j = 1; j < w; ++j) {
     const int32_t dest = (r + j) % w;
     const int32_t src = (r - j + w) % w;
-    ex->reqs.clear();
+    ClearBlocks(ex);
     BlockRequests(ex, f, dest);
-    int code = Execute(ex, stream);
+    int code = Execute(ex, f, ex->num_local, j == 1, stream);
     if (code == XSE_OK) code = SideAfter(ex, stream);
     if (code == XSE_OK) code = SendRecv(ex, dest, src, ex->side);
     if (code != XSE_OK) return code;
   }
-  ex->reqs.clear();
+  ClearBlocks(ex);
   BlockRequests(ex, f, r);
-  int code = Execute(ex, stream);
+  int code = Execute(ex, f, ex->num_local, w == 1, stream);
   if (code != XSE_OK || w == 1) return code;
   code = StreamAfterSide(ex, stream);
   if (code != XSE_OK) return code;
@@ -422,25 +468,24 @@ int RunRow(xse_shard_exchange* ex, const xse_bag_request* f,
   const int32_t w = ex->world, t = ex->plan.num_tables, d_ = ex->plan.dim;
   const int64_t row = static_cast<int64_t>(t) * d_;
   if (w == 1) {
-    ex->reqs.clear();
+    ClearBlocks(ex);
     for (int32_t k = 0; k < t; ++k) {
-      ex->reqs.push_back(
-          Slice(f[k], 0, ex->block, ex->out_local + k * d_, row));
+      AddBlock(ex, k, Slice(f[k], 0, ex->block, ex->out_local + k * d_, row));
     }
-    return Execute(ex, stream);
+    return Execute(ex, f, t, true, stream);
   }
   const xse::NcclApi& n = xse::Nccl();
   for (int32_t c = 0; c < ex->chunks; ++c) {
     float* part = ex->partial + c * w * ex->piece * row;
-    ex->reqs.clear();
+    ClearBlocks(ex);
     for (int32_t s = 0; s < w; ++s) {
       const int64_t b0 = s * ex->block + c * ex->piece;
       for (int32_t k = 0; k < t; ++k) {
-        ex->reqs.push_back(Slice(f[k], b0, ex->piece,
-                                 part + s * ex->piece * row + k * d_, row));
+        AddBlock(ex, k, Slice(f[k], b0, ex->piece,
+                              part + s * ex->piece * row + k * d_, row));
       }
     }
-    int code = Execute(ex, stream);
+    int code = Execute(ex, f, t, c == 0, stream);
     if (code == XSE_OK) code = SideAfter(ex, stream);
     if (code != XSE_OK) return code;
     const ncclResult_t res = n.ReduceScatter(
