@@ -259,8 +259,9 @@ def timed_steps(step, first, count, world, local, finish=None):
 
 def kernel_timing(engine, step, first, count, finish=None):
   """The pooling kernel's duration: CUDA events around the pooling launch of
-  each of `count` further steps (engine profiling, period 1). Returns
-  (mean ms per timed launch, timed launches)."""
+  each of `count` further steps (engine profiling, period 1), with another
+  event before the validation launch. Returns (mean pooling ms per timed
+  launch, timed launches, validation ms per step or None)."""
   torch.cuda.synchronize()
   engine.profile_read()  # restart the sampling
   engine.set_profiling(True, 1)
@@ -269,9 +270,24 @@ def kernel_timing(engine, step, first, count, finish=None):
   if finish is not None:
     finish()
   torch.cuda.synchronize()
-  ms, n = engine.profile_read()
+  r = engine.profile_read_stages()
   engine.set_profiling(False)
-  return ms / max(n, 1), n
+  n = r["executions"]
+  val = r["validate_ms"] / count if r["validated"] else None
+  return r["pool_ms"] / max(n, 1), n, val
+
+
+def validation_share(val_ms, step_ms):
+  """The validation kernels' own event-timed duration per step and that
+  time against the untimed step (programmatic dependent launch overlaps
+  most of it with the previous step's pooling, so the share of the step it
+  actually costs is smaller)."""
+  if val_ms is None:
+    return None
+  return {"ms_per_step": val_ms, "fraction_of_step": val_ms / step_ms,
+          "timing": "CUDA events before the validation and before the "
+                    "pooling launch of each kernel-timing step (kernels "
+                    "serialised)"}
 
 
 def check_parity(items, count, seed=SEED):
@@ -888,7 +904,7 @@ def measure_config(xse, args, name, world, rank, local, max_rows=None):
   ms, launches = timed_steps(wl.step, args.warmup, args.steps, world, local,
                              wl.finish)
   wl.exchange.check()
-  pool_ms, pool_n = kernel_timing(
+  pool_ms, pool_n, val_ms = kernel_timing(
       wl.engine, wl.step, args.warmup + args.steps,
       max(KERNEL_TIMING_LAUNCHES // wl.pool_groups, 8), wl.finish)
   wl.exchange.check()
@@ -992,6 +1008,7 @@ def measure_config(xse, args, name, world, rank, local, max_rows=None):
               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
               "path": e_path},
       "gpu_launches": launches,
+      "validation": validation_share(val_ms, ms / args.steps),
       "cpu_baseline": base,
       "parity": parity,
   }
@@ -1214,7 +1231,7 @@ def measure_dlrm(xse, args, world, local, check=True):
   ms, launches = timed_steps(wl.step, args.warmup, args.dlrm_steps, world,
                              local)
   wl.status.wait()
-  pool_avg, pool_n = kernel_timing(wl.engine, wl.step,
+  pool_avg, pool_n, _ = kernel_timing(wl.engine, wl.step,
                                    args.warmup + args.dlrm_steps,
                                    KERNEL_TIMING_LAUNCHES)
   wl.status.wait()
@@ -1417,8 +1434,9 @@ def measure_dlrm_lookup(xse, args, world, local):
   wl.status.wait()
   ms, launches = timed_steps(wl.step, args.warmup, args.steps, world, local)
   wl.status.wait()
-  pool_ms, pool_n = kernel_timing(wl.engine, wl.step, args.warmup + args.steps,
-                                  KERNEL_TIMING_LAUNCHES)
+  pool_ms, pool_n, val_ms = kernel_timing(wl.engine, wl.step,
+                                          args.warmup + args.steps,
+                                          KERNEL_TIMING_LAUNCHES)
   wl.status.wait()
   examples = sum_over_ranks(REF_BATCH * args.steps, world)
   peak, peak_kind = measured_peaks()
@@ -1476,6 +1494,7 @@ def measure_dlrm_lookup(xse, args, world, local):
                    "algorithmic_bytes_per_step": wl.bytes_per_step(),
                    "avg_launch_ms": pool_ms, "timed_launches": pool_n,
                    "traffic": None},
+      "validation": validation_share(val_ms, ms / args.steps),
       "e2e": {"value": e_examples / (e_ms / 1000.0), "unit": "examples/s",
               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
               "path": "CpuEmbeddingLookupTransform(dense_lookup=True) with "
@@ -1776,8 +1795,9 @@ def main():
                                      local, wl.finish)
   wl.check()
   first = args.warmup + args.steps
-  pool_avg_ms, pool_n = kernel_timing(wl.engine, wl.step, first,
-                                      KERNEL_TIMING_LAUNCHES, wl.finish)
+  pool_avg_ms, pool_n, val_ms = kernel_timing(wl.engine, wl.step, first,
+                                              KERNEL_TIMING_LAUNCHES,
+                                              wl.finish)
   wl.check()
 
   # End to end with host buffers: the operator at N=1, the sharded exchange
@@ -1863,7 +1883,7 @@ def main():
         "roofline": {
             "bound": "hbm",
             "kernel": "the pooling kernel the engine's tuner keeps for this "
-                      "launch (PoolVecKernel<bf16, G=16, V=1, exact> on "
+                      "launch (PoolVecKernel<bf16, G=8, V=2, exact, wide> on "
                       "uniform ids over tables larger than L2), one launch "
                       "serving both weighting modes",
             "achieved": achieved,
@@ -1889,6 +1909,7 @@ def main():
             "path": e2e_path,
         },
         "gpu_launches": launches,
+        "validation": validation_share(val_ms, elapsed_ms / args.steps),
         "cpu_baseline": base,
         "parity": parity,
         "clocks": clock_info,

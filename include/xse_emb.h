@@ -249,6 +249,17 @@ int32_t xse_last_launch_count(void);
 int xse_engine_set_profiling(xse_engine* engine, int32_t period);
 int xse_engine_profile_read(xse_engine* engine, double* pool_ms,
                             int64_t* executions, int64_t* calls);
+/* As xse_engine_profile_read, and also the validation kernels' summed time
+ * (from an event recorded before them to the one before the pooling
+ * kernels) and the number of timed executions that ran them
+ * (validate_ms / validated may be NULL). The events serialise the
+ * validation kernels with the pooling kernels that would otherwise overlap
+ * them (programmatic dependent launch), so this is each kernel's own
+ * duration, not its share of an untimed execution. Same tracing role as
+ * xse_engine_profile_read (graph_executor.cc:62,111). */
+int xse_engine_profile_read_stages(xse_engine* engine, double* validate_ms,
+                                   int64_t* validated, double* pool_ms,
+                                   int64_t* executions, int64_t* calls);
 
 /* ---------------------------------------------------------------------------
  * DLRM dot interaction. No counterpart in the reference: its DLRM bundle uses

@@ -433,6 +433,13 @@ def test_profiling_period(xse):
   eng.execute_batch(reqs)  # the read restarts the sampling: timed
   ms, timed = eng.profile_read()
   assert timed == 1
+  # Strict executions run the validation kernel, fused ones do not.
+  eng.set_profiling(True, 1)
+  eng.execute_batch(reqs)
+  eng.execute_batch(reqs, fused=True)
+  st = eng.profile_read_stages()
+  assert (st["executions"], st["validated"], st["calls"]) == (2, 1, 2)
+  assert st["validate_ms"] > 0 and st["pool_ms"] > 0
   eng.set_profiling(False)
   eng.execute_batch(reqs)
   assert eng.profile_read(with_calls=True)[1:] == (0, 0)

@@ -140,6 +140,10 @@ SIGNATURES = {
     "xse_engine_profile_read": (_I, [_P, ctypes.POINTER(ctypes.c_double),
                                      ctypes.POINTER(_I64),
                                      ctypes.POINTER(_I64)]),
+    "xse_engine_profile_read_stages": (_I, [
+        _P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_I64),
+        ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_I64),
+        ctypes.POINTER(_I64)]),
     "xse_engine_execute_interaction": (_I, [_P, _P, _I32, _P, _I64, _I64, _P,
                                             _I64, _P, _I32, _P]),
     "xse_engine_execute_interaction_tf32": (_I, [_P, _P, _I32, _P, _I64,

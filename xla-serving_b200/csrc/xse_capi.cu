@@ -189,12 +189,17 @@ struct xse_engine {
   std::unordered_map<std::string, std::shared_ptr<Table>> tables;
   std::mutex default_status_mu;
   xse_status* default_status = nullptr;
-  // Kernel timing: event pairs recorded around the pooling kernels of every
-  // profile_period-th execution (0: off).
+  // Kernel timing of every profile_period-th execution (0: off): events
+  // before the validation kernels (when they run), before the pooling
+  // kernels and after them.
+  struct ProfileEvents {
+    cudaEvent_t validate = nullptr, pool = nullptr, end = nullptr;
+    bool validated = false;
+  };
   std::mutex profile_mu;
   int32_t profile_period = 0;
   int64_t profile_calls = 0;
-  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> profile_events;
+  std::vector<ProfileEvents> profile_events;
   size_t profile_used = 0;
   // Pooling-kernel tuner, keyed by launch signature.
   std::mutex tune_mu;
@@ -852,7 +857,31 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
   int launches = 0;
   const bool validate =
       parts == nullptr || parts->validate || validate_only || any_soft;
-  if ((!fused || validate_only || any_soft) && validate) {
+  const bool run_validation = (!fused || validate_only || any_soft) && validate;
+  // Kernel timing (a copy of the engine's event set: the vector may grow
+  // under another caller).
+  xse_engine::ProfileEvents timing{};
+  if (!validate_only && !any_soft) {
+    std::lock_guard<std::mutex> lock(engine->profile_mu);
+    if (engine->profile_period > 0 &&
+        engine->profile_calls++ % engine->profile_period == 0) {
+      if (engine->profile_used == engine->profile_events.size()) {
+        xse_engine::ProfileEvents ev;
+        cudaEventCreate(&ev.validate);
+        cudaEventCreate(&ev.pool);
+        cudaEventCreate(&ev.end);
+        engine->profile_events.push_back(ev);
+      }
+      xse_engine::ProfileEvents& ev =
+          engine->profile_events[engine->profile_used++];
+      ev.validated = run_validation;
+      timing = ev;
+    }
+  }
+  if (timing.validate != nullptr && run_validation) {
+    cudaEventRecord(timing.validate, stream);
+  }
+  if (run_validation) {
     for (size_t base = 0; base < descs.size();
          base += xse::kMaxDescsPerLaunch) {
       xse::PoolParams p{};
@@ -871,22 +900,8 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
       ++launches;
     }
   }
-  std::pair<cudaEvent_t, cudaEvent_t> timing{nullptr, nullptr};
   if (!validate_only && !any_soft) {
-    {
-      std::lock_guard<std::mutex> lock(engine->profile_mu);
-      if (engine->profile_period > 0 &&
-          engine->profile_calls++ % engine->profile_period == 0) {
-        if (engine->profile_used == engine->profile_events.size()) {
-          cudaEvent_t a, b;
-          cudaEventCreate(&a);
-          cudaEventCreate(&b);
-          engine->profile_events.emplace_back(a, b);
-        }
-        timing = engine->profile_events[engine->profile_used++];
-      }
-    }
-    if (timing.first != nullptr) cudaEventRecord(timing.first, stream);
+    if (timing.pool != nullptr) cudaEventRecord(timing.pool, stream);
     auto layout_of = [&](const xse::BagDesc& d) {
       xse::Layout l = xse::ChooseLayout(tables[d.slot]->dtype, d.dim, d.rows);
       if (tables[d.slot]->dtype == XSE_DT_I8_ROWWISE &&
@@ -1011,7 +1026,7 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
       }
       if (e != cudaSuccess) return CudaError(e, "interaction launch");
     }
-    if (timing.second != nullptr) cudaEventRecord(timing.second, stream);
+    if (timing.end != nullptr) cudaEventRecord(timing.end, stream);
   }
   g_last_launches = launches;
   if (iso_code != XSE_OK) {
@@ -1100,8 +1115,9 @@ void xse_engine_destroy(xse_engine* engine) {
   }
   xse_status_destroy(engine->default_status);
   for (auto& ev : engine->profile_events) {
-    cudaEventDestroy(ev.first);
-    cudaEventDestroy(ev.second);
+    cudaEventDestroy(ev.validate);
+    cudaEventDestroy(ev.pool);
+    cudaEventDestroy(ev.end);
   }
   for (auto& [key, tuner] : engine->tuners) {
     (void)key;
@@ -1125,29 +1141,45 @@ int xse_engine_set_profiling(xse_engine* engine, int32_t period) {
   return Ok();
 }
 
-int xse_engine_profile_read(xse_engine* engine, double* pool_ms,
-                            int64_t* executions, int64_t* calls) {
+int xse_engine_profile_read_stages(xse_engine* engine, double* validate_ms,
+                                   int64_t* validated, double* pool_ms,
+                                   int64_t* executions, int64_t* calls) {
   if (engine == nullptr || pool_ms == nullptr || executions == nullptr) {
     return SetError(XSE_INVALID_ARGUMENT, "arguments must be non-null");
   }
   DeviceGuard guard(engine->device);
   std::lock_guard<std::mutex> lock(engine->profile_mu);
-  double total = 0.0;
+  double total = 0.0, vtotal = 0.0;
+  int64_t vcount = 0;
   for (size_t k = 0; k < engine->profile_used; ++k) {
     const auto& ev = engine->profile_events[k];
-    cudaError_t e = cudaEventSynchronize(ev.second);
+    cudaError_t e = cudaEventSynchronize(ev.end);
     if (e != cudaSuccess) return CudaError(e, "profile event");
     float ms = 0.0f;
-    e = cudaEventElapsedTime(&ms, ev.first, ev.second);
+    e = cudaEventElapsedTime(&ms, ev.pool, ev.end);
     if (e != cudaSuccess) return CudaError(e, "profile elapsed time");
     total += ms;
+    if (ev.validated) {
+      e = cudaEventElapsedTime(&ms, ev.validate, ev.pool);
+      if (e != cudaSuccess) return CudaError(e, "profile elapsed time");
+      vtotal += ms;
+      ++vcount;
+    }
   }
   *pool_ms = total;
   *executions = static_cast<int64_t>(engine->profile_used);
+  if (validate_ms != nullptr) *validate_ms = vtotal;
+  if (validated != nullptr) *validated = vcount;
   if (calls != nullptr) *calls = engine->profile_calls;
   engine->profile_used = 0;
   engine->profile_calls = 0;
   return Ok();
+}
+
+int xse_engine_profile_read(xse_engine* engine, double* pool_ms,
+                            int64_t* executions, int64_t* calls) {
+  return xse_engine_profile_read_stages(engine, nullptr, nullptr, pool_ms,
+                                        executions, calls);
 }
 
 }  // extern "C"

@@ -351,6 +351,20 @@ class EmbeddingEngine:
       return ms.value, n.value, calls.value
     return ms.value, n.value
 
+  def profile_read_stages(self):
+    """Since the last read: {"pool_ms", "executions", "validate_ms",
+    "validated", "calls"} -- summed pooling and validation kernel times (each
+    kernel timed alone, events between them), the timed executions and those
+    of them that ran validation kernels, and all executions."""
+    ms, vms = ctypes.c_double(), ctypes.c_double()
+    n, vn, calls = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    C.check(C.lib.xse_engine_profile_read_stages(
+        self._handle, ctypes.byref(vms), ctypes.byref(vn), ctypes.byref(ms),
+        ctypes.byref(n), ctypes.byref(calls)))
+    return {"pool_ms": ms.value, "executions": n.value,
+            "validate_ms": vms.value, "validated": vn.value,
+            "calls": calls.value}
+
   def pool(self, feature_name, ids, offsets, weights=None, *, stream=None,
            fused=False):
     """Single-feature convenience: returns a new [num_bags, dim] tensor."""
