@@ -12,7 +12,7 @@ row-wise (partials are added in another order). The exchange's own request
 checks are exercised too."""
 
 import os
-import socket
+import tempfile
 from datetime import timedelta
 
 import numpy as np
@@ -148,18 +148,19 @@ def test_exchange_rejects_bad_requests(xse):
   engine.close()
 
 
-def _free_port():
-  with socket.socket() as s:
-    s.bind(("127.0.0.1", 0))
-    return s.getsockname()[1]
+def _rendezvous():
+  """A rendezvous for the ranks of one test: a FileStore in a fresh
+  temporary directory (no TCP port that another process could take
+  between choosing it and the store binding it)."""
+  return "file://" + os.path.join(tempfile.mkdtemp(prefix="xse_rdv_"),
+                                  "store")
 
 
-def _rank_main(rank, world, port, mode, results):
-  os.environ["MASTER_ADDR"] = "127.0.0.1"
-  os.environ["MASTER_PORT"] = str(port)
+def _rank_main(rank, world, rendezvous, mode, results):
   os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
   torch.cuda.set_device(rank)
-  dist.init_process_group("nccl", rank=rank, world_size=world,
+  dist.init_process_group("nccl", init_method=rendezvous, rank=rank,
+                          world_size=world,
                           timeout=timedelta(seconds=60),
                           device_id=torch.device("cuda", rank))
   try:
@@ -177,7 +178,7 @@ def test_two_gpu_exchange(mode):
   world = 2
   with mp.get_context("spawn").Manager() as manager:
     results = manager.dict()
-    mp.start_processes(_rank_main, args=(world, _free_port(), mode, results),
+    mp.start_processes(_rank_main, args=(world, _rendezvous(), mode, results),
                        nprocs=world, start_method="spawn")
     got = {r: results[r] for r in range(world)}
   for r in range(world):

@@ -7,7 +7,7 @@ bit table-wise, within 1e-5 of the magnitude sum row-wise (partial sums are
 added in another order)."""
 
 import os
-import socket
+import tempfile
 
 import numpy as np
 import pytest
@@ -60,16 +60,17 @@ def full_pooled(tables):
   return out
 
 
-def _free_port():
-  with socket.socket() as s:
-    s.bind(("127.0.0.1", 0))
-    return s.getsockname()[1]
+def _rendezvous():
+  """A rendezvous for the ranks of one test: a FileStore in a fresh
+  temporary directory (no TCP port that another process could take
+  between choosing it and the store binding it)."""
+  return "file://" + os.path.join(tempfile.mkdtemp(prefix="xse_rdv_"),
+                                  "store")
 
 
-def _tablewise_rank(rank, world, port, mode, results):
-  os.environ["MASTER_ADDR"] = "127.0.0.1"
-  os.environ["MASTER_PORT"] = str(port)
-  dist.init_process_group("gloo", rank=rank, world_size=world)
+def _tablewise_rank(rank, world, rendezvous, mode, results):
+  dist.init_process_group("gloo", init_method=rendezvous, rank=rank,
+                          world_size=world)
   try:
     from conftest import load_package  # pylint: disable=import-outside-toplevel
     sharding = load_package().sharding
@@ -115,12 +116,11 @@ class TorchPacker:
         d_w.copy_(weights[lo:hi])
 
 
-def _ids_a2a_rank(rank, world, port, mode, results):
+def _ids_a2a_rank(rank, world, rendezvous, mode, results):
   """Data-parallel input: this rank holds every table's ids for its own
   sample block only (absolute offsets into the whole batch's arrays)."""
-  os.environ["MASTER_ADDR"] = "127.0.0.1"
-  os.environ["MASTER_PORT"] = str(port)
-  dist.init_process_group("gloo", rank=rank, world_size=world)
+  dist.init_process_group("gloo", init_method=rendezvous, rank=rank,
+                          world_size=world)
   try:
     from conftest import load_package  # pylint: disable=import-outside-toplevel
     sharding = load_package().sharding
@@ -148,10 +148,9 @@ def _ids_a2a_rank(rank, world, port, mode, results):
     dist.destroy_process_group()
 
 
-def _rowwise_rank(rank, world, port, chunks, results):
-  os.environ["MASTER_ADDR"] = "127.0.0.1"
-  os.environ["MASTER_PORT"] = str(port)
-  dist.init_process_group("gloo", rank=rank, world_size=world)
+def _rowwise_rank(rank, world, rendezvous, chunks, results):
+  dist.init_process_group("gloo", init_method=rendezvous, rank=rank,
+                          world_size=world)
   try:
     from conftest import load_package  # pylint: disable=import-outside-toplevel
     sharding = load_package().sharding
@@ -179,7 +178,7 @@ def _spawn(fn, *args):
   world = 2
   with mp.get_context("spawn").Manager() as manager:
     results = manager.dict()
-    mp.start_processes(fn, args=(world, _free_port()) + args + (results,),
+    mp.start_processes(fn, args=(world, _rendezvous()) + args + (results,),
                        nprocs=world, start_method="spawn")
     return [results[r] for r in range(world)]
 
@@ -247,16 +246,15 @@ def test_rowwise_reduce_scatter_gloo(chunks):
     np.testing.assert_allclose(got[r], exp, rtol=1e-5, atol=1e-6)
 
 
-def _leaving_rank(rank, world, port, mode, results):
+def _leaving_rank(rank, world, rendezvous, mode, results):
   """Both ranks run one exchange step; then rank 1 leaves (between steps,
   nothing of it in flight) and rank 0 runs the next step. Rank 0's
   collective must end with an error within the process group's short
   timeout instead of waiting for ever."""
   import time  # pylint: disable=import-outside-toplevel
   from datetime import timedelta  # pylint: disable=import-outside-toplevel
-  os.environ["MASTER_ADDR"] = "127.0.0.1"
-  os.environ["MASTER_PORT"] = str(port)
-  dist.init_process_group("gloo", rank=rank, world_size=world,
+  dist.init_process_group("gloo", init_method=rendezvous, rank=rank,
+                          world_size=world,
                           timeout=timedelta(seconds=5))
   try:
     from conftest import load_package  # pylint: disable=import-outside-toplevel

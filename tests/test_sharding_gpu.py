@@ -8,7 +8,7 @@ whole batch: bit for bit table-wise, within 1e-5 relative to the magnitude
 sum row-wise (partials are added in another order). Needs two GPUs."""
 
 import os
-import socket
+import tempfile
 from datetime import timedelta
 
 import numpy as np
@@ -38,17 +38,18 @@ def batch_of(t):
   return ids, offsets, weights
 
 
-def _free_port():
-  with socket.socket() as s:
-    s.bind(("127.0.0.1", 0))
-    return s.getsockname()[1]
+def _rendezvous():
+  """A rendezvous for the ranks of one test: a FileStore in a fresh
+  temporary directory (no TCP port that another process could take
+  between choosing it and the store binding it)."""
+  return "file://" + os.path.join(tempfile.mkdtemp(prefix="xse_rdv_"),
+                                  "store")
 
 
-def _rank_main(rank, world, port, mode, results):
-  os.environ["MASTER_ADDR"] = "127.0.0.1"
-  os.environ["MASTER_PORT"] = str(port)
+def _rank_main(rank, world, rendezvous, mode, results):
   torch.cuda.set_device(rank)
-  dist.init_process_group("nccl", rank=rank, world_size=world,
+  dist.init_process_group("nccl", init_method=rendezvous, rank=rank,
+                          world_size=world,
                           timeout=timedelta(seconds=60),
                           device_id=torch.device("cuda", rank))
   try:
@@ -149,7 +150,7 @@ def test_sharded_two_gpus(mode):
   world = 2
   with mp.get_context("spawn").Manager() as manager:
     results = manager.dict()
-    mp.start_processes(_rank_main, args=(world, _free_port(), mode, results),
+    mp.start_processes(_rank_main, args=(world, _rendezvous(), mode, results),
                        nprocs=world, start_method="spawn")
     got = [results[r] for r in range(world)]
   want = full_pooled()
@@ -162,13 +163,12 @@ def test_sharded_two_gpus(mode):
       np.testing.assert_array_equal(got[r], exp)
 
 
-def _barrier_timeout_main(rank, world, port, results):
+def _barrier_timeout_main(rank, world, rendezvous, results):
   """Rank 1 never reaches the barrier: rank 0's bounded wait gives up and
   the group reports DEADLINE_EXCEEDED; the context stays usable."""
-  os.environ["MASTER_ADDR"] = "127.0.0.1"
-  os.environ["MASTER_PORT"] = str(port)
   torch.cuda.set_device(rank)
-  dist.init_process_group("nccl", rank=rank, world_size=world,
+  dist.init_process_group("nccl", init_method=rendezvous, rank=rank,
+                          world_size=world,
                           timeout=timedelta(seconds=60),
                           device_id=torch.device("cuda", rank))
   try:
@@ -199,7 +199,7 @@ def test_peer_barrier_gives_up_when_a_rank_never_arrives(xse):
   with mp.get_context("spawn").Manager() as manager:
     results = manager.dict()
     mp.start_processes(_barrier_timeout_main,
-                       args=(2, _free_port(), results), nprocs=2,
+                       args=(2, _rendezvous(), results), nprocs=2,
                        start_method="spawn")
     got = dict(results)
   assert got[0][0] == xse._capi.DEADLINE_EXCEEDED
