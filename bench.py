@@ -12,9 +12,8 @@ With N GPUs (torchrun, one process per GPU, NCCL) every rank holds 8 such
 tables (8N tables in all, table-wise sharded) and pools them for the whole
 batch; each sample block goes to its owning rank (weak scaling: fixed work
 per GPU). By default the pooling kernel stores the blocks straight into the
-owners' buffers over NVLink and its last block sets this rank's arrival flag
-on every rank (--exchange peer); --exchange a2a / pipelined use NCCL
-instead.
+owners' buffers over NVLink and a flag barrier ends the step (--exchange
+peer); --exchange a2a / pipelined use NCCL instead.
 
 The same run measures the other workloads and reports each under its own key
 of the one JSON line (each with its roofline, end-to-end rate, CPU baseline
@@ -419,9 +418,8 @@ class Workload:
       before = self.pooler.launches
       self.pooler(self.requests[v])
       return self.pooler.launches - before
-    # Nothing reads the received rows here: no step waits for the others'
-    # arrival (a step's validation launch only waits for the slot it
-    # overwrites); finish() waits for the last step's.
+    # Nothing reads the received rows here: each step's barrier overlaps
+    # the next step's pooling; finish() waits for the last one.
     self.exchange.run(self.steps[v], defer=True)
     return self.launches_per_step
 
@@ -467,13 +465,13 @@ class Workload:
 
 
 def exchange_launches(mode, world, chunks=1):
-  """Own kernels one sharded step launches: validation + pooling per group
-  (the peer mode's kernels synchronise the step themselves), plus the
-  reorder of received blocks in the NCCL table-wise modes."""
+  """Own kernels one sharded step launches: validation + pooling per group,
+  plus the peer barrier (peer) or the reorder of received blocks (NCCL
+  table-wise modes)."""
   if world == 1:
     return 2
   if mode == "peer":
-    return 2
+    return 3
   if mode == "a2a":
     return 3
   if mode == "pipelined":
@@ -497,8 +495,7 @@ def multi_table_config(world, exchange):
                        "a2a": "one NCCL all-to-all",
                        "peer": "the pooling kernel's own stores into "
                                "the owners' buffers over NVLink (CUDA "
-                               "IPC); the pooling launch sets the ranks' "
-                               "arrival flags"}[exchange]),
+                               "IPC) and a flag barrier"}[exchange]),
       "l2": "inputs larger than L2: 1.0 GB of tables per GPU and "
             f"{ROTATE} rotating id/offset/weight sets",
       "validation": "strict (separate validation kernel each step)",

@@ -968,102 +968,26 @@ __device__ __forceinline__ void EnterDependent() {
 #endif
 }
 
-// ---- peer exchange step synchronisation (PeerSync) ------------------------
-
-__device__ __forceinline__ uint32_t PeerLoadAcquire(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];"
-               : "=r"(v)
-               : "l"(p)
-               : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void PeerStoreRelease(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v)
-               : "memory");
-}
-
-// Warp-wide (one warp of the launch): lane q < world polls rank q's flag
-// until it has reached p.peer.wait_epoch, all lanes at once. False when a
-// wait ran out, or an earlier wait of this rank had (the error word is set
-// then). The first polls run back to back, then 100 ns apart, then 1 us
-// apart.
-__device__ __forceinline__ bool PeerSlotWait(const PoolParams& p) {
-  const int q = threadIdx.x & 31;
-  int bad = 0;
-  if (q < p.peer.world) {
-    for (int64_t spins = 0;; ++spins) {
-      if (static_cast<int32_t>(PeerLoadAcquire(p.peer.flags + q) -
-                               p.peer.wait_epoch) >= 0) {
-        break;
-      }
-      if (spins >= p.peer.spin_limit ||
-          *reinterpret_cast<volatile int32_t*>(p.peer.error) != 0) {
-        atomicExch(p.peer.error, 1);
-        bad = 1;
-        break;
-      }
-      if (spins >= 64) __nanosleep(spins < 4096 ? 100 : 1000);
-    }
-  }
-  return __any_sync(0xffffffffu, bad) == 0;
-}
-
-// Block-wide, before the block's first store, for a pooling launch that no
-// validation launch of the step precedes (the validation kernel waits for
-// the slot otherwise, and the pooling launch starts after it completes).
-// False (for the whole block) when the wait ran out: the block must not
-// pool.
-__device__ __forceinline__ bool PeerEnter(const PoolParams& p) {
-  if (p.peer.world == 0 || p.peer.wait == 0) return true;
-  int bad = 0;
-  if (threadIdx.x < 32) bad = PeerSlotWait(p) ? 0 : 1;
-  return __syncthreads_or(bad) == 0;
-}
-
-// Block-wide, at the end of the launch that carries the step's arrival:
-// after a block barrier (which orders the block's stores, peer slots
-// included, before thread 0's next operations) thread 0 fences system-wide
-// and counts the block; the last block to finish fences again and stores
-// the epoch into every rank's flag for this rank (release, system scope),
-// then clears the counter for the next step (ordered after this grid).
-__device__ __forceinline__ void PeerArrive(const PoolParams& p) {
-  if (p.peer.world == 0 || p.peer.counter == nullptr) return;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const unsigned prev = atomicAdd(p.peer.counter, 1u);
-    if (prev == gridDim.x - 1) {
-      __threadfence_system();
-      for (int q = 0; q < p.peer.world; ++q) {
-        PeerStoreRelease(p.peer.arrive[q], p.peer.epoch);
-      }
-      *p.peer.counter = 0u;
-    }
-  }
-}
-
 template <int DT, int G, int V, bool EXACT, int UR, bool WIDE = false>
 __global__ void __launch_bounds__(kThreads,
                                   UR == 0 ? MinBlocks<DT, V, WIDE>::value : 2)
     PoolVecKernel(const __grid_constant__ PoolParams p) {
   EnterDependent();
-  if (PeerEnter(p) && (p.fused_checks || p.status->group_error == 0)) {
-    const int64_t b = blockIdx.x;
-    const int64_t b0 = p.mode_blocks[0], b1 = p.mode_blocks[1];
-    if (b < b0) {
-      PoolBody<DT, G, V, EXACT, WIDE, kUnweighted, UR>(p, 0, p.mode_tasks[0],
-                                                       b, b0);
-    } else if (b < b1) {
-      PoolBody<DT, G, V, EXACT, WIDE, kWeightedSum, UR>(
-          p, p.mode_tasks[0], p.mode_tasks[1], b - b0, b1 - b0);
-    } else {
-      PoolBody<DT, G, V, EXACT, WIDE, kWeightedNorm, UR>(
-          p, p.mode_tasks[1], p.mode_tasks[2], b - b1, gridDim.x - b1);
-    }
+  if (!p.fused_checks && p.status->group_error != 0) return;
+  const int64_t b = blockIdx.x;
+  const int64_t b0 = p.mode_blocks[0], b1 = p.mode_blocks[1];
+  if (b < b0) {
+    PoolBody<DT, G, V, EXACT, WIDE, kUnweighted, UR>(p, 0, p.mode_tasks[0], b,
+                                                     b0);
+  } else if (b < b1) {
+    PoolBody<DT, G, V, EXACT, WIDE, kWeightedSum, UR>(p, p.mode_tasks[0],
+                                                      p.mode_tasks[1], b - b0,
+                                                      b1 - b0);
+  } else {
+    PoolBody<DT, G, V, EXACT, WIDE, kWeightedNorm, UR>(p, p.mode_tasks[1],
+                                                       p.mode_tasks[2],
+                                                       b - b1, gridDim.x - b1);
   }
-  PeerArrive(p);
 }
 
 // ---- staged kernel ---------------------------------------------------------
@@ -1293,22 +1217,19 @@ template <int DT, int G>
 __global__ void __launch_bounds__(kStageThreads, 1)
     PoolStagedKernel(const __grid_constant__ PoolParams p) {
   EnterDependent();
+  if (!p.fused_checks && p.status->group_error != 0) return;
   extern __shared__ uint4 stage_smem[];
-  if (PeerEnter(p) && (p.fused_checks || p.status->group_error == 0)) {
-    const int64_t b = blockIdx.x;
-    const int64_t b0 = p.mode_blocks[0], b1 = p.mode_blocks[1];
-    if (b < b0) {
-      StagedBody<DT, G, kUnweighted>(p, 0, p.mode_tasks[0], b, b0,
-                                     stage_smem);
-    } else if (b < b1) {
-      StagedBody<DT, G, kWeightedSum>(p, p.mode_tasks[0], p.mode_tasks[1],
-                                      b - b0, b1 - b0, stage_smem);
-    } else {
-      StagedBody<DT, G, kWeightedNorm>(p, p.mode_tasks[1], p.mode_tasks[2],
-                                       b - b1, gridDim.x - b1, stage_smem);
-    }
+  const int64_t b = blockIdx.x;
+  const int64_t b0 = p.mode_blocks[0], b1 = p.mode_blocks[1];
+  if (b < b0) {
+    StagedBody<DT, G, kUnweighted>(p, 0, p.mode_tasks[0], b, b0, stage_smem);
+  } else if (b < b1) {
+    StagedBody<DT, G, kWeightedSum>(p, p.mode_tasks[0], p.mode_tasks[1],
+                                    b - b0, b1 - b0, stage_smem);
+  } else {
+    StagedBody<DT, G, kWeightedNorm>(p, p.mode_tasks[1], p.mode_tasks[2],
+                                     b - b1, gridDim.x - b1, stage_smem);
   }
-  PeerArrive(p);
 }
 
 // ---- fused pooling + dot interaction --------------------------------------
@@ -1684,8 +1605,11 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<DT, 1>::value)
 // dims or unaligned tables). A warp owns a bag; lanes own columns
 // c = lane + 32*k, in column chunks of 32*kCols.
 template <int DT>
-__device__ __forceinline__ void ScalarBody(const PoolParams& p) {
+__global__ void __launch_bounds__(kThreads)
+    PoolScalarKernel(const __grid_constant__ PoolParams p) {
   constexpr int kCols = 4;
+  EnterDependent();
+  if (!p.fused_checks && p.status->group_error != 0) return;
   const int lane = threadIdx.x & 31;
   const int64_t warps_per_block = kThreads / 32;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * warps_per_block;
@@ -1755,16 +1679,6 @@ __device__ __forceinline__ void ScalarBody(const PoolParams& p) {
   }
 }
 
-template <int DT>
-__global__ void __launch_bounds__(kThreads)
-    PoolScalarKernel(const __grid_constant__ PoolParams p) {
-  EnterDependent();
-  if (PeerEnter(p) && (p.fused_checks || p.status->group_error == 0)) {
-    ScalarBody<DT>(p);
-  }
-  PeerArrive(p);
-}
-
 // Group validation (ValidateEmbeddingBagInput, embedding_bag.cc:99-133).
 // Offsets must start >= 0 and never decrease; the final offset must not
 // exceed the ids (or weights); every id in [first, last) must be in
@@ -1780,11 +1694,6 @@ constexpr int kValidateChunk = 256;
 __global__ void __launch_bounds__(kThreads)
     ValidateKernel(const __grid_constant__ PoolParams p, int64_t total_work) {
   EnterDependent();
-  // A peer exchange step: its pooling launch starts after this kernel has
-  // completed, so one warp waits here for the slot the step overwrites.
-  if (p.peer.wait != 0 && blockIdx.x == 0 && threadIdx.x < 32) {
-    (void)PeerSlotWait(p);
-  }
   constexpr int K = kValidateChunk / 32;
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);

@@ -881,18 +881,11 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
   if (timing.validate != nullptr && run_validation) {
     cudaEventRecord(timing.validate, stream);
   }
-  // A peer exchange step (parts->peer): the validation launch waits for
-  // the slot the step overwrites; its pooling launches then need not.
-  const xse::PeerSync* peer = parts != nullptr ? parts->peer : nullptr;
   if (run_validation) {
     for (size_t base = 0; base < descs.size();
          base += xse::kMaxDescsPerLaunch) {
       xse::PoolParams p{};
       p.status = dev_status;
-      if (peer != nullptr && base == 0) {
-        p.peer = *peer;
-        p.peer.counter = nullptr;
-      }
       int64_t work = 0;
       const size_t cnt =
           std::min<size_t>(xse::kMaxDescsPerLaunch, descs.size() - base);
@@ -929,13 +922,6 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
         // One launch per layout; its weighting modes share it.
         groups[{l.dtype, l.g, l.v, l.exact, l.wide ? 1 : 0}].push_back(d);
       }
-      // A peer exchange step: the last pooling launch carries the arrival;
-      // without a validation launch every one waits for the slot.
-      size_t total_launches = 0, launch_index = 0;
-      for (const auto& kv : groups) {
-        total_launches += (kv.second.size() + xse::kMaxDescsPerLaunch - 1) /
-                          xse::kMaxDescsPerLaunch;
-      }
       for (auto& [key, list] : groups) {
         const xse::Layout l{std::get<0>(key), std::get<1>(key),
                             std::get<2>(key), std::get<3>(key), 0,
@@ -960,14 +946,6 @@ int ExecuteBatch(xse_engine* engine, const xse_bag_request* reqs, int32_t n,
           }
           p.n = static_cast<int32_t>(cnt);
           p.total_tasks = tasks;
-          if (peer != nullptr) {
-            p.peer = *peer;
-            if (run_validation) p.peer.wait = 0;
-            const bool last = ++launch_index == total_launches;
-            if (!last) p.peer.counter = nullptr;
-            // The arrival must not be lost to a launch with nothing to do.
-            if (last && tasks <= 0) return cudaErrorInvalidValue;
-          }
           uint64_t key = 0;
           const PoolTrial trial = ChoosePoolKernel(engine, l, &p, &key);
           // A failed record only spoils the trial (PollTrials drops it).

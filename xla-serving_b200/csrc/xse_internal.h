@@ -84,26 +84,6 @@ inline size_t DevStatusBytes(int capacity) {
   return sizeof(DevStatus) + sizeof(DevRequestStatus) * (capacity - 1);
 }
 
-// Step synchronisation of the table-wise peer exchange, carried by the
-// launches of one step (world == 0: none). Before the step's first store
-// one warp waits until each rank's flag here has reached wait_epoch (the
-// ranks have finished the step whose readers the overwritten slot served):
-// the validation launch's, or, without one, every pooling block's. The last
-// block of the launch with a counter then makes the step's stores visible
-// system-wide and stores `epoch` into every rank's flag for this rank (its
-// arrival). Waits are bounded: a wait that runs out sets *error.
-struct PeerSync {
-  uint32_t* counter;                 // finished blocks; nullptr: no arrival
-  uint32_t* arrive[kMaxOutBlocks];   // rank q's flag word for this rank
-  const uint32_t* flags;             // this rank's flags, one per rank
-  int32_t* error;                    // this rank's error word
-  int64_t spin_limit;                // polls before a wait gives up
-  uint32_t epoch;                    // this step's arrival value
-  uint32_t wait_epoch;               // value every flag must reach first
-  int32_t wait;                      // 1: wait for wait_epoch
-  int32_t world;
-};
-
 struct PoolParams {
   int32_t n;
   int32_t fused_checks;   // 1: record errors here; 0: a validation pass ran
@@ -120,7 +100,6 @@ struct PoolParams {
   // (PoolStagedKernel).
   int32_t kernel_choice;
   float* block_base[kMaxOutBlocks];  // blocked outputs (BagDesc::block_bags)
-  PeerSync peer;
   BagDesc d[kMaxDescsPerLaunch];
 };
 
@@ -284,9 +263,6 @@ struct PartSet {
   float* const* block_base = nullptr;
   const int64_t* block_offset = nullptr;
   int64_t block_stride = 0;
-  // Peer exchange step (PeerSync): the validation launch waits for the
-  // slot; the last pooling launch arrives.
-  const PeerSync* peer = nullptr;
 };
 
 // ExecuteBatch over `whole` (the status block's requests: its errors name
@@ -296,23 +272,6 @@ struct PartSet {
 int ExecuteParts(xse_engine* engine, const xse_bag_request* whole, int32_t n,
                  const PartSet& parts, cudaStream_t stream, int32_t flags,
                  xse_status* status);
-
-}  // namespace xse
-
-#include "../../include/xse_peer.h"
-
-namespace xse {
-
-// Peer exchange steps (csrc/xse_peer.cu). PeerStepSync fills `out` for the
-// group's next epoch, waiting (when back > 0 and that epoch is past it) for
-// every rank to have arrived at epoch - back; PeerCommitEpoch records that
-// the step with that epoch was launched. LaunchPeerWait queues a bounded
-// wait on `stream` until every rank has arrived at `epoch`.
-int PeerStepSync(xse_peer_group* group, int64_t spin_limit, uint32_t back,
-                 PeerSync* out);
-void PeerCommitEpoch(xse_peer_group* group, uint32_t epoch);
-int LaunchPeerWait(xse_peer_group* group, uint32_t epoch, int64_t spin_limit,
-                   cudaStream_t stream);
 
 }  // namespace xse
 

@@ -1,11 +1,9 @@
 // Peer-memory exchange group and its flag barrier (include/xse_peer.h).
 //
 // Each rank's buffer starts with a 256-byte header: flags[q] (uint32) at
-// 4q is written by rank q when it reaches a barrier, the error word at byte
-// 128 is set by this rank's barrier when a wait gives up, and the word at
-// byte 192 counts the finished blocks of a pooling launch that arrives for
-// this rank (PeerSync). Data starts at byte 256, so it keeps the
-// allocation's 256-byte alignment.
+// 4q is written by rank q when it reaches a barrier, and the error word at
+// byte 128 is set by this rank's barrier when a wait gives up. Data starts at
+// byte 256, so it keeps the allocation's 256-byte alignment.
 //
 // The barrier is one kernel of `world` threads per rank. Thread q first makes
 // this rank's earlier work visible system-wide (the stream order already
@@ -34,9 +32,6 @@ namespace {
 
 constexpr int64_t kHeaderBytes = 256;
 constexpr int64_t kErrorOffset = 128;
-constexpr int64_t kCounterOffset = 192;
-static_assert(kMaxOutBlocks == XSE_PEER_MAX_RANKS,
-              "a pooling launch addresses every rank of a group");
 constexpr int64_t kDefaultSpinLimit = 2000000;  // ~1 us per poll
 
 int Fail(int code, const char* fmt, ...)
@@ -72,24 +67,6 @@ __device__ __forceinline__ uint32_t LoadAcquire(const uint32_t* p) {
                : "l"(p)
                : "memory");
   return v;
-}
-
-// The waiting half of the barrier: thread q polls flags[q] of this rank's
-// header until rank q has arrived at the epoch (the pooling launch of a peer
-// exchange step does the arriving, PeerSync).
-__global__ void PeerWaitKernel(BarrierParams p) {
-  const int q = threadIdx.x;
-  if (q >= p.world) return;
-  const uint32_t* mine = p.flags[p.rank] + q;
-  for (int64_t spins = 0;; ++spins) {
-    if (static_cast<int32_t>(LoadAcquire(mine) - p.epoch) >= 0) break;
-    if (spins >= p.spin_limit || *reinterpret_cast<volatile int32_t*>(
-                                     p.error) != 0) {
-      atomicExch(p.error, 1);  // gave up: rank q never arrived
-      break;
-    }
-    if (spins >= 64) __nanosleep(spins < 4096 ? 100 : 1000);
-  }
 }
 
 __global__ void PeerBarrierKernel(BarrierParams p) {
@@ -285,60 +262,3 @@ extern "C" void xse_peer_group_destroy(xse_peer_group* g) {
   }
   delete g;
 }
-
-namespace xse {
-
-int PeerStepSync(xse_peer_group* g, int64_t spin_limit, uint32_t back,
-                 PeerSync* out) {
-  if (g == nullptr || out == nullptr) {
-    return Fail(XSE_INVALID_ARGUMENT, "null peer group");
-  }
-  std::lock_guard<std::mutex> lock(g->mu);
-  if (!g->connected) {
-    return Fail(XSE_FAILED_PRECONDITION, "peer step before connect");
-  }
-  PeerSync s{};
-  s.counter = reinterpret_cast<uint32_t*>(g->own + kCounterOffset);
-  for (int32_t q = 0; q < g->world; ++q) {
-    s.arrive[q] = reinterpret_cast<uint32_t*>(g->mapped[q]) + g->rank;
-  }
-  s.flags = reinterpret_cast<const uint32_t*>(g->own);
-  s.error = reinterpret_cast<int32_t*>(g->own + kErrorOffset);
-  s.spin_limit = spin_limit > 0 ? spin_limit : kDefaultSpinLimit;
-  s.epoch = g->epoch + 1;
-  s.wait = back > 0 && s.epoch > back ? 1 : 0;
-  s.wait_epoch = s.wait ? s.epoch - back : 0;
-  s.world = g->world;
-  *out = s;
-  return XSE_OK;
-}
-
-void PeerCommitEpoch(xse_peer_group* g, uint32_t epoch) {
-  std::lock_guard<std::mutex> lock(g->mu);
-  g->epoch = epoch;
-}
-
-int LaunchPeerWait(xse_peer_group* g, uint32_t epoch, int64_t spin_limit,
-                   cudaStream_t stream) {
-  if (g == nullptr) return Fail(XSE_INVALID_ARGUMENT, "null peer group");
-  BarrierParams p = {};
-  {
-    std::lock_guard<std::mutex> lock(g->mu);
-    for (int32_t q = 0; q < g->world; ++q) {
-      p.flags[q] = reinterpret_cast<uint32_t*>(g->mapped[q]);
-    }
-    p.error = reinterpret_cast<int32_t*>(g->own + kErrorOffset);
-    p.world = g->world;
-    p.rank = g->rank;
-  }
-  p.spin_limit = spin_limit > 0 ? spin_limit : kDefaultSpinLimit;
-  p.epoch = epoch;
-  PeerWaitKernel<<<1, 32, 0, stream>>>(p);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    return Fail(XSE_INTERNAL, "peer wait launch: %s", cudaGetErrorString(e));
-  }
-  return XSE_OK;
-}
-
-}  // namespace xse

@@ -5,12 +5,8 @@
 // execution (validation + pooling kernels, asynchronous status ring) with
 // requests whose outputs point where each sample block must end up:
 //   PEER       the owner's output slot, mapped over NVLink (the pooling
-//              kernel's stores are the exchange); the step's validation
-//              launch waits for the slot it overwrites to be free and the
-//              pooling launch, when its last block finishes, sets this
-//              rank's arrival flag on every rank (PeerSync), so a step is
-//              its validation and pooling kernels only; a bounded wait
-//              kernel orders a reader after every rank's arrival;
+//              kernel's stores are the exchange), then the flag barrier of
+//              xse_peer.cu on a side stream;
 //   A2A        this rank's own block straight into the output, the other
 //              blocks into a send buffer; one grouped NCCL send/recv and a
 //              reorder of the received blocks into the output;
@@ -214,13 +210,13 @@ struct xse_shard_exchange {
   float* recv = nullptr;            // A2A / PIPELINED: [q][block][T_q][D]
   float* partial = nullptr;         // ROW, W > 1: [chunks][W][piece][T][D]
   xse_status* status = nullptr;
-  cudaStream_t side = nullptr;      // NCCL stream
+  cudaStream_t side = nullptr;      // PEER barrier / NCCL stream
   cudaEvent_t pooled = nullptr;
-  std::vector<cudaEvent_t> done;    // done[0]: last NCCL step
+  std::vector<cudaEvent_t> done;    // per slot (PEER) / last NCCL step
+  std::vector<bool> done_valid;
   int64_t step = -1;
   int32_t slot = 0;
   bool pending_ready = false;
-  uint32_t ready_epoch = 0;         // PEER: epoch of the last step
   std::vector<xse_bag_request> reqs;  // sample blocks of the feature requests
   std::vector<int32_t> owner;          // feature request of each block
   std::vector<float*> block_base;      // peer mode: destinations' slots
@@ -279,11 +275,9 @@ int Execute(xse_shard_exchange* ex, const xse_bag_request* f, int32_t n,
 // the feature's column, so the kernels take one blocked descriptor per
 // feature (instead of one per feature and destination).
 int ExecuteBlocked(xse_shard_exchange* ex, const xse_bag_request* f,
-                   int32_t n, cudaStream_t stream,
-                   const xse::PeerSync* sync) {
+                   int32_t n, cudaStream_t stream) {
   xse::PartSet parts{ex->reqs.data(), ex->owner.data(),
                      static_cast<int32_t>(ex->reqs.size()), true};
-  parts.peer = sync;
   if (ex->world > 1 && ex->world <= xse::kMaxOutBlocks) {
     parts.blocks = ex->world;
     parts.block_bags = ex->block;
@@ -312,19 +306,18 @@ int RunPeer(xse_shard_exchange* ex, const xse_bag_request* f, int32_t flags,
             cudaStream_t stream, float** out) {
   const int64_t i = ex->step + 1;
   const int32_t slot = static_cast<int32_t>(i % ex->slots);
-  const int32_t w = ex->world, d_ = ex->plan.dim, t = ex->plan.num_tables;
-  // The step's kernels synchronise it themselves (PeerSync): step i
-  // overwrites, on every rank, the slot of step i - 3; each rank queued that
-  // step's readers before its pooling of step i - 2, so the validation
-  // launch of step i first waits until all ranks have arrived at step
-  // i - 2's epoch, and the last pooling block to finish arrives at step i's.
-  xse::PeerSync sync{};
-  if (w > 1) {
-    const int code = xse::PeerStepSync(
-        ex->peers, ex->plan.spin_limit,
-        static_cast<uint32_t>(ex->slots - 1), &sync);
-    if (code != XSE_OK) return code;
+  // Step i overwrites, on every rank, the slot of step i - 3. Each rank
+  // queued that step's readers before its pooling of step i - 2, which the
+  // barrier of step i - 2 waited for on every rank.
+  const int32_t prev = static_cast<int32_t>((i + 1) % ex->slots);
+  // A barrier that has already completed needs no wait node on the stream.
+  if (i >= 2 && ex->done_valid[prev] &&
+      cudaEventQuery(ex->done[prev]) != cudaSuccess) {
+    (void)cudaGetLastError();  // cudaErrorNotReady is not an error here
+    cudaError_t e = cudaStreamWaitEvent(stream, ex->done[prev], 0);
+    if (e != cudaSuccess) return xse::CudaFail(e, "slot reuse wait");
   }
+  const int32_t w = ex->world, d_ = ex->plan.dim, t = ex->plan.num_tables;
   ClearBlocks(ex);
   ex->block_base.assign(static_cast<size_t>(w), nullptr);
   ex->block_offset.assign(static_cast<size_t>(ex->num_local), 0);
@@ -341,16 +334,19 @@ int RunPeer(xse_shard_exchange* ex, const xse_bag_request* f, int32_t flags,
                      static_cast<int64_t>(t) * d_));
     }
   }
-  int code = ExecuteBlocked(ex, f, ex->num_local, stream,
-                            w > 1 ? &sync : nullptr);
+  int code = ExecuteBlocked(ex, f, ex->num_local, stream);
   if (code != XSE_OK) return code;
   if (w > 1) {
-    xse::PeerCommitEpoch(ex->peers, sync.epoch);
-    ex->ready_epoch = sync.epoch;
+    code = SideAfter(ex, stream);
+    if (code != XSE_OK) return code;
+    code = xse_peer_group_barrier(ex->peers, ex->plan.spin_limit, ex->side);
+    if (code != XSE_OK) return code;
+    cudaError_t e = cudaEventRecord(ex->done[slot], ex->side);
+    if (e != cudaSuccess) return xse::CudaFail(e, "barrier event");
+    ex->done_valid[slot] = true;
     if ((flags & XSE_SHARD_DEFER_WAIT) == 0) {
-      code = xse::LaunchPeerWait(ex->peers, sync.epoch, ex->plan.spin_limit,
-                                 stream);
-      if (code != XSE_OK) return code;
+      e = cudaStreamWaitEvent(stream, ex->done[slot], 0);
+      if (e != cudaSuccess) return xse::CudaFail(e, "barrier wait");
       ex->pending_ready = false;
     } else {
       ex->pending_ready = true;
@@ -683,6 +679,7 @@ int xse_shard_exchange_create(xse_engine* engine, xse_shard_comm* comm,
     cudaEvent_t ev = nullptr;
     e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
     ex->done.push_back(ev);
+    ex->done_valid.push_back(false);
   }
   if (e != cudaSuccess) return fail(xse::CudaFail(e, "exchange streams"));
   const size_t out_bytes = static_cast<size_t>(ex->out_floats) * 4;
@@ -790,12 +787,11 @@ int xse_shard_exchange_run(xse_shard_exchange* ex,
 
 int xse_shard_exchange_ready(xse_shard_exchange* ex, void* stream) {
   if (ex == nullptr) return ShardFail(XSE_INVALID_ARGUMENT, "null exchange");
-  if (ex->pending_ready && ex->peers != nullptr) {
+  if (ex->pending_ready && ex->done_valid[ex->slot]) {
     xse::DeviceScope scope(ex->comm->device);
-    const int code = xse::LaunchPeerWait(ex->peers, ex->ready_epoch,
-                                         ex->plan.spin_limit,
-                                         static_cast<cudaStream_t>(stream));
-    if (code != XSE_OK) return code;
+    const cudaError_t e = cudaStreamWaitEvent(
+        static_cast<cudaStream_t>(stream), ex->done[ex->slot], 0);
+    if (e != cudaSuccess) return xse::CudaFail(e, "barrier wait");
     ex->pending_ready = false;
   }
   return ShardOk();
