@@ -215,6 +215,14 @@ def max_over_ranks(value, world):
   return float(t.item())
 
 
+def min_over_ranks(value, world):
+  if world == 1:
+    return value
+  t = torch.tensor([value], dtype=torch.float64, device="cuda")
+  dist.all_reduce(t, op=dist.ReduceOp.MIN)
+  return float(t.item())
+
+
 def sum_over_ranks(value, world):
   if world == 1:
     return value
@@ -1841,6 +1849,9 @@ def main():
     torch.cuda.synchronize()
     wl.check()
     parity = check_parity(wl.parity_items(v), BATCH)
+  # Per-rank spread of the pooling kernel's time (every rank takes part).
+  pool_lo = min_over_ranks(pool_avg_ms, world)
+  pool_hi = max_over_ranks(pool_avg_ms, world)
   ids_total = sum_over_ranks(wl.ids_per_step() * args.steps, world)
   value = ids_total / (elapsed_ms / 1000.0)
   e2e_ids = sum_over_ranks(wl.ids_per_step() * e2e_steps, world)
@@ -1909,6 +1920,16 @@ def main():
             "path": e2e_path,
         },
         "gpu_launches": launches,
+        "ranks": {
+            "step_ms": elapsed_ms / args.steps,
+            "pool_ms_min": pool_lo,
+            "pool_ms_max": pool_hi,
+            "step_minus_slowest_pool_ms": elapsed_ms / args.steps - pool_hi,
+            "note": "step = max over ranks of the timed region / steps; "
+                    "pooling = each rank's CUDA-event mean over the "
+                    "kernel-timing pass; the remainder is validation not "
+                    "hidden under the previous step, the exchange's "
+                    "synchronisation and launch gaps"},
         "validation": validation_share(val_ms, elapsed_ms / args.steps),
         "cpu_baseline": base,
         "parity": parity,
