@@ -1,7 +1,7 @@
 // CPU oracle for the embedding-bag / DLRM interaction path.
 //
-// TEST INFRASTRUCTURE ONLY: the checker for the CUDA path and the timed CPU
-// baseline. It restates, in plain C++17, the reference CPU engine of
+// TEST INFRASTRUCTURE ONLY: the results the CUDA path is tested against and
+// the timed CPU baseline. It restates, in plain C++17, the reference CPU engine of
 // openxla/xla-serving. Each function cites the reference file:line it follows.
 // Compiled with -ffp-contract=off so that every multiply and add rounds
 // separately, in the order the reference's scalar semantics give.

@@ -2,10 +2,11 @@
  *
  * TEST INFRASTRUCTURE ONLY. This library is a plain C++17 restatement of the
  * reference CPU embedding engine (openxla/xla-serving, directory
- * data/cpu_embedding/cc and data/kernels/cpu_embedding). It is the checker
- * that the CUDA path is compared against, and the timed CPU baseline. Only the
- * test suite, the smoke check and the benchmark's CPU-baseline leg may load it;
- * the product never links or calls it.
+ * data/cpu_embedding/cc and data/kernels/cpu_embedding). It is the
+ * reference result that the CUDA path is compared against in the tests, and
+ * the timed CPU baseline. Only the test suite, the smoke check and the
+ * benchmark's CPU-baseline leg may load it; the product never links or
+ * calls it.
  *
  * Parity pins: the reference cannot be compiled here (it needs Bazel, abseil
  * and Eigen, none of which are present), so the restatement is pinned against

@@ -1,7 +1,7 @@
 """CPU tests of the oracle against the reference's golden vectors.
 
-Pins the C++ restatement (oracle/xse_oracle.cc) before it is trusted as the
-checker of the CUDA path: every known answer of the reference's tests
+Pins the C++ restatement (oracle/xse_oracle.cc) before the CUDA path is
+tested against it: every known answer of the reference's tests
 (tests/golden/known_answers.json) and the reference's numpy lookup run on
 seeded inputs (tests/golden/numpy_lookup.npz).
 """
